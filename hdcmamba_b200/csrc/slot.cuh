@@ -1,0 +1,26 @@
+// Shared definitions of the slot-memory kernels.
+#pragma once
+#include "common.cuh"
+
+namespace hdc {
+
+struct SlotParams {
+  const void* q; const void* k; const void* v; int64_t in_sb, in_st;
+  const void* gamma; const float* log_a;
+  void* y; int64_t y_sb, y_sh, y_st;
+  const float* state_in; float* state_out;
+  float* Rst;   // CUDA-core path: [BH, N, bd, bd] chunk contributions, then entering states
+  float* gC;    // CUDA-core path: [BH, N] chunk decay factors
+  int L, H, hd, C, rows, N, bd;
+};
+
+// phi(z) = z > 0 ? z + 1 : exp(z)  (hdcmamba/model.py:261-262)
+__device__ __forceinline__ float phi(float z) { return z > 0.f ? z + 1.f : expf(z); }
+
+template <typename T>
+__device__ __forceinline__ float trnd(float v) { return store_round<T>(v); }
+
+size_t slot_simt_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
+int slot_simt_fwd(int dtype, SlotParams p, int64_t B, void* ws, cudaStream_t s);
+
+}  // namespace hdc

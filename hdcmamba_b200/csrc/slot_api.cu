@@ -1,0 +1,33 @@
+// hdc_slot_scan_fwd: argument checks and dispatch between the tcgen05 kernel
+// (bf16 activations) and the CUDA-core kernel (fp32 activations).
+#include "slot.cuh"
+
+using namespace hdc;
+
+extern "C" size_t hdc_slot_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C) {
+  if (B < 1 || H < 1 || hd < 1 || C < 1 || L < C) return 0;
+  return slot_simt_workspace(B, L, H, hd, C);
+}
+
+extern "C" int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                                 int64_t in_st, const void* gamma, const float* log_a, void* y, int64_t y_sb,
+                                 int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
+                                 void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                                 int64_t hd, int64_t C, int64_t rows, hdc_stream_t stream) {
+  if (dtype != HDC_F32 && dtype != HDC_BF16) return fail(HDC_E_DTYPE, "slot: dtype %d", dtype);
+  if (!q || !k || !v || !y || !workspace || (!gamma && !log_a)) return fail(HDC_E_NULL, "slot: null pointer");
+  if (B < 1 || H < 1 || hd < 1 || hd > 128 || C < 1 || C > 256 || L < C || L % C != 0)
+    return fail(HDC_E_SHAPE, "slot: B=%lld L=%lld H=%lld hd=%lld C=%lld (hd <= 128, C <= 256, L %% C == 0)",
+                (long long)B, (long long)L, (long long)H, (long long)hd, (long long)C);
+  if (rows < 1 || rows > C || (log_a && rows != C)) return fail(HDC_E_SHAPE, "slot: rows=%lld", (long long)rows);
+  const size_t need = hdc_slot_workspace_bytes(B, L, H, hd, C);
+  if (workspace_bytes < need)
+    return fail(HDC_E_WORKSPACE, "slot: workspace %zu < %zu bytes", workspace_bytes, need);
+  SlotParams p{};
+  p.q = q; p.k = k; p.v = v; p.in_sb = in_sb; p.in_st = in_st; p.gamma = gamma; p.log_a = log_a;
+  p.y = y; p.y_sb = y_sb; p.y_sh = y_sh; p.y_st = y_st; p.state_in = state_in; p.state_out = state_out;
+  p.L = (int)L; p.H = (int)H; p.hd = (int)hd; p.C = (int)C; p.rows = (int)rows; p.N = (int)(L / C);
+  p.bd = (int)feature_block(hd);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  return slot_simt_fwd(dtype, p, B, workspace, s);
+}

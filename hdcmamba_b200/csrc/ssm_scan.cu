@@ -1,0 +1,175 @@
+// Diagonal SSM chunked scan, sm_100a.
+//
+// Per batch b and state channel j < ds (hdcmamba/model.py:175-233):
+//   dt_s = softplus20(dt), a_t = exp(dt_s * A_j), u_t = dt_s * b_t * x_t, A_j = -exp(A_log_j)
+//   within chunk n:  h_t = a_t h_{t-1} + u_t  from h = 0 at the chunk start
+//   chunk stats:     last_n = bf16(h at chunk end), dec_n = bf16(sum_t dt_s*A)
+//   prefix:          G_0 = 0, G_{n+1} = G_n * exp(dec_n) + last_n (fp32), used as bf16(G_n)
+//   output:          y_t = bf16( bf16(h_t) + bf16(G_n) * exp(cum_log_t) )
+// These are the reference's rounding points (its three kernels store bf16).
+//
+// Schedule: one CTA per (chunk, batch) with ds*S threads; thread (j, s) scans
+// C/S consecutive steps of channel j.  Segment results are combined through
+// shared memory: (h_s, sum_log_s) with h = h_prev * exp(sum_log_s) + h_s.
+//   pass 1 (hdc_ssm_chunk_stats): chunk statistics -> stats[b, n, 0:2ds]
+//   pass 2 (hdc_ssm_scan_out):    exclusive prefix over all earlier chunks (including
+//                                 n_prev chunks of earlier sequence segments),
+//                                 then the outputs, written with caller strides.
+#include "common.cuh"
+
+namespace hdc {
+
+struct SsmParams {
+  const void* projs; int64_t psb, pst;
+  const void* A_log;
+  float* stats_w; const float* stats_r; int64_t stats_sb; int n_prev;
+  void* y; int64_t ysb, yst;
+  int L, ds, C, S;
+};
+
+template <typename T>
+__device__ __forceinline__ void ssm_step(const T* row, int j, int ds, float A, float& ld, float& u) {
+  const float dt = to_f(row[j]);
+  const float xv = to_f(row[ds + j]);
+  const float bv = to_f(row[2 * ds + j]);
+  const float dts = softplus20(dt);
+  ld = dts * A;
+  u = dts * bv * xv;
+}
+
+// per-thread scan of its segment from h = 0; returns (h, sum_log)
+template <typename T>
+__device__ __forceinline__ void ssm_segment(const SsmParams& p, int b, int n, int j, int s, float A,
+                                            float& h, float& sl) {
+  const int seglen = p.C / p.S;
+  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)(n * p.C + s * seglen) * p.pst;
+  h = 0.f;
+  sl = 0.f;
+  for (int t = 0; t < seglen; ++t) {
+    float ld, u;
+    ssm_step<T>(base + (size_t)t * p.pst, j, p.ds, A, ld, u);
+    sl += ld;
+    h = h * expf(ld) + u;
+  }
+}
+
+template <typename T>
+__global__ void ssm_chunk_stats_kernel(SsmParams p) {
+  extern __shared__ float sh[];  // [2][S][ds]
+  const int n = blockIdx.x, b = blockIdx.y;
+  const int j = threadIdx.x % p.ds, s = threadIdx.x / p.ds;
+  const int N = p.L / p.C;
+  const float A = -expf(to_f(static_cast<const T*>(p.A_log)[j]));
+  float h, sl;
+  ssm_segment<T>(p, b, n, j, s, A, h, sl);
+  sh[s * p.ds + j] = h;
+  sh[(p.S + s) * p.ds + j] = sl;
+  __syncthreads();
+  if (s == 0) {
+    float hc = 0.f, lc = 0.f;
+    for (int q = 0; q < p.S; ++q) {
+      hc = hc * expf(sh[(p.S + q) * p.ds + j]) + sh[q * p.ds + j];
+      lc += sh[(p.S + q) * p.ds + j];
+    }
+    float* st = p.stats_w + ((size_t)b * N + n) * 2 * p.ds;
+    st[j] = bf16_round(hc);
+    st[p.ds + j] = bf16_round(lc);
+  }
+}
+
+template <typename T>
+__global__ void ssm_scan_out_kernel(SsmParams p) {
+  extern __shared__ float sh[];  // [2][S][ds] + [ds] prefix
+  const int n = blockIdx.x, b = blockIdx.y;
+  const int j = threadIdx.x % p.ds, s = threadIdx.x / p.ds;
+  const float A = -expf(to_f(static_cast<const T*>(p.A_log)[j]));
+  float* shG = sh + 2 * p.S * p.ds;
+
+  // exclusive prefix over chunks [0, n_prev + n) -- fp32, sequential (the reference order)
+  if (s == 0) {
+    const float* st = p.stats_r + (size_t)b * p.stats_sb;
+    const int m_end = p.n_prev + n;
+    float G = 0.f;
+    for (int m = 0; m < m_end; ++m) G = G * expf(st[(size_t)m * 2 * p.ds + p.ds + j]) + st[(size_t)m * 2 * p.ds + j];
+    shG[j] = bf16_round(G);
+  }
+  float h, sl;
+  ssm_segment<T>(p, b, n, j, s, A, h, sl);
+  sh[s * p.ds + j] = h;
+  sh[(p.S + s) * p.ds + j] = sl;
+  __syncthreads();
+  // carry-in from earlier segments of this chunk
+  float hin = 0.f, cum = 0.f;
+  for (int q = 0; q < s; ++q) {
+    hin = hin * expf(sh[(p.S + q) * p.ds + j]) + sh[q * p.ds + j];
+    cum += sh[(p.S + q) * p.ds + j];
+  }
+  const float G = shG[j];
+  const int seglen = p.C / p.S;
+  const int t0 = n * p.C + s * seglen;
+  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)t0 * p.pst;
+  T* yb = static_cast<T*>(p.y) + (size_t)b * p.ysb + (size_t)t0 * p.yst;
+  float hh = hin;
+  for (int t = 0; t < seglen; ++t) {
+    float ld, u;
+    ssm_step<T>(base + (size_t)t * p.pst, j, p.ds, A, ld, u);
+    cum += ld;
+    hh = hh * expf(ld) + u;
+    const float yv = bf16_round(bf16_round(hh) + G * expf(cum));
+    yb[(size_t)t * p.yst + j] = from_f<T>(yv);
+  }
+}
+
+static int ssm_segments(int ds, int C) {
+  int S = 1;
+  while (S * 2 * ds <= 512 && C % (S * 2) == 0 && C / (S * 2) >= 4) S *= 2;
+  return S;
+}
+
+static int ssm_check(int dtype, const void* projs, const void* A_log, int64_t B, int64_t L, int64_t ds, int64_t C) {
+  if (dtype != HDC_F32 && dtype != HDC_BF16) return fail(HDC_E_DTYPE, "ssm: dtype %d", dtype);
+  if (!projs || !A_log) return fail(HDC_E_NULL, "ssm: null pointer");
+  if (ds < 16 || ds > 256 || (ds & (ds - 1)) != 0)
+    return fail(HDC_E_SHAPE, "ssm: d_state=%lld must be a power of two in [16,256]", (long long)ds);
+  if (C < 1 || L < C || L % C != 0 || B < 1) return fail(HDC_E_SHAPE, "ssm: L=%lld not a multiple of C=%lld", (long long)L, (long long)C);
+  return 0;
+}
+
+}  // namespace hdc
+
+using namespace hdc;
+
+extern "C" int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                                   const void* A_log, float* stats, int64_t B, int64_t L, int64_t ds,
+                                   int64_t C, hdc_stream_t stream) {
+  if (int e = ssm_check(dtype, projs, A_log, B, L, ds, C)) return e;
+  if (!stats) return fail(HDC_E_NULL, "ssm: null stats");
+  SsmParams p{};
+  p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_w = stats;
+  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C);
+  dim3 grid((unsigned)(L / C), (unsigned)B);
+  const size_t smem = 2 * p.S * ds * sizeof(float);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == HDC_F32) ssm_chunk_stats_kernel<float><<<grid, p.S * ds, smem, s>>>(p);
+  else ssm_chunk_stats_kernel<__nv_bfloat16><<<grid, p.S * ds, smem, s>>>(p);
+  return launch_status("ssm_chunk_stats_kernel");
+}
+
+extern "C" int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                                const void* A_log, const float* stats, int64_t stats_sb, int64_t n_prev,
+                                void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds,
+                                int64_t C, hdc_stream_t stream) {
+  if (int e = ssm_check(dtype, projs, A_log, B, L, ds, C)) return e;
+  if (!stats || !y) return fail(HDC_E_NULL, "ssm: null stats / y");
+  if (n_prev < 0 || stats_sb < (n_prev + L / C) * 2 * ds) return fail(HDC_E_SHAPE, "ssm: stats batch stride too small");
+  SsmParams p{};
+  p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_r = stats;
+  p.stats_sb = stats_sb; p.n_prev = (int)n_prev; p.y = y; p.ysb = y_sb; p.yst = y_st;
+  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C);
+  dim3 grid((unsigned)(L / C), (unsigned)B);
+  const size_t smem = (2 * p.S + 1) * ds * sizeof(float);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == HDC_F32) ssm_scan_out_kernel<float><<<grid, p.S * ds, smem, s>>>(p);
+  else ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * ds, smem, s>>>(p);
+  return launch_status("ssm_scan_out_kernel");
+}

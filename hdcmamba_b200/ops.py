@@ -1,0 +1,208 @@
+"""Tensor-level wrappers over the C ABI (include/hdcmamba_b200.h).
+
+Each op validates device / dtype / layout, allocates its outputs through the torch
+caching allocator on the current stream, and launches through ``_lib.call``.
+Only CUDA tensors are accepted: there is no CPU path.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.HDC_F32, torch.bfloat16: _lib.HDC_BF16}
+
+
+def _code(t):
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"hdcmamba_b200: unsupported dtype {t.dtype} (float32 or bfloat16)") from None
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("hdcmamba_b200 kernels run on CUDA tensors only (got a CPU tensor)")
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _same_dtype(ref, *ts):
+    for t in ts:
+        if t is not None and t.dtype != ref.dtype:
+            raise TypeError(f"hdcmamba_b200: dtype mismatch ({t.dtype} vs {ref.dtype})")
+
+
+# ------------------------------------------------------------------ LN + conv
+def ln_conv(x, norm_w, norm_b, conv_w, conv_b, eps=1e-5, act="none", halo=None, stats=False):
+    """LayerNorm + causal depthwise conv1d (width 4), optional SiLU.
+
+    Replaces ``_fused_norm_conv_fwd_kernel`` (hdcmamba/model.py:22-72).
+    x: [B, L, D]; conv_w: [D, 4] or [D, 1, 4]; halo: optional [B, 3, D].
+    Returns out (and bf16 mean, rstd [B, L] if ``stats``)."""
+    _cuda(x, norm_w, norm_b, conv_w, conv_b, halo)
+    B, L, D = x.shape
+    x = x.contiguous()
+    nw, nb = norm_w.to(x.dtype).contiguous(), norm_b.to(x.dtype).contiguous()
+    cw = conv_w.reshape(D, 4).to(x.dtype).contiguous()
+    cb = conv_b.to(x.dtype).contiguous()
+    if halo is not None:
+        halo = halo.to(x.dtype).contiguous()
+        if tuple(halo.shape) != (B, 3, D):
+            raise ValueError(f"halo must be [B, 3, D], got {tuple(halo.shape)}")
+    out = torch.empty_like(x)
+    mean = rstd = None
+    if stats:
+        mean = torch.empty(B, L, device=x.device, dtype=torch.bfloat16)
+        rstd = torch.empty(B, L, device=x.device, dtype=torch.bfloat16)
+    a = {"none": _lib.HDC_ACT_NONE, "silu": _lib.HDC_ACT_SILU}[act]
+    _lib.call("hdc_ln_conv_fwd", _code(x), _p(x), _p(nw), _p(nb), _p(cw), _p(cb), _p(halo), _p(out),
+              _p(mean), _p(rstd), B, L, D, float(eps), a, _stream(x))
+    return (out, mean, rstd) if stats else out
+
+
+# ------------------------------------------------------------------ SSM scan
+def _row_view(t, what):
+    """(batch stride, row stride) of a [B, L, cols] view whose last dim is unit-stride."""
+    if t.dim() != 3 or t.stride(2) != 1:
+        raise ValueError(f"{what} must be a [B, L, cols] view with unit column stride")
+    return t.stride(0), t.stride(1)
+
+
+def ssm_chunk_stats(projs, A_log, d_state, chunk):
+    """Per-chunk statistics [B, N, 2*ds] fp32 (last state, summed log decay), bf16-rounded.
+
+    Replaces the last_state / chunk_decay outputs of ``_ssm_intra_v2`` (hdcmamba/model.py:175-198)."""
+    _cuda(projs, A_log)
+    B, L, P = projs.shape
+    if P < 3 * d_state or L % chunk != 0:
+        raise ValueError(f"projs [B, L, {P}] needs >= 3*d_state columns and L % chunk == 0")
+    sb, st = _row_view(projs, "projs")
+    a = A_log.to(projs.dtype).contiguous()
+    stats = torch.empty(B, L // chunk, 2 * d_state, device=projs.device, dtype=torch.float32)
+    _lib.call("hdc_ssm_chunk_stats", _code(projs), _p(projs), sb, st, _p(a), _p(stats), B, L, d_state, chunk,
+              _stream(projs))
+    return stats
+
+
+def ssm_scan_out(projs, A_log, stats, n_prev, d_state, chunk, out=None):
+    """Outputs of the chunked scan given chunk statistics of [0, n_prev + N) chunks.
+
+    Replaces ``_ssm_scan_v2`` + ``_ssm_inter_v2`` (hdcmamba/model.py:200-233).
+    ``out``: optional [B, L, >=ds] view (unit column stride) to write into."""
+    _cuda(projs, A_log, stats, out)
+    B, L, P = projs.shape
+    if P < 3 * d_state or L % chunk != 0:
+        raise ValueError(f"projs [B, L, {P}] needs >= 3*d_state columns and L % chunk == 0")
+    sb, st = _row_view(projs, "projs")
+    a = A_log.to(projs.dtype).contiguous()
+    if out is None:
+        out = torch.empty(B, L, d_state, device=projs.device, dtype=projs.dtype)
+    _same_dtype(projs, out)
+    osb, ost = _row_view(out, "out")
+    stats = stats.contiguous()
+    if stats.dtype != torch.float32 or stats.shape[0] != B or stats.shape[1] != n_prev + L // chunk:
+        raise ValueError("stats must be fp32 [B, n_prev + L/chunk, 2*d_state]")
+    _lib.call("hdc_ssm_scan_out", _code(projs), _p(projs), sb, st, _p(a), _p(stats), stats.stride(0), n_prev,
+              _p(out), osb, ost, B, L, d_state, chunk, _stream(projs))
+    return out
+
+
+def ssm_scan(projs, A_log, d_state, chunk, out=None):
+    """The whole diagonal-SSM chunked scan (hdcmamba/model.py:175-233, launched 345-363)."""
+    stats = ssm_chunk_stats(projs, A_log, d_state, chunk)
+    return ssm_scan_out(projs, A_log, stats, 0, d_state, chunk, out=out)
+
+
+# ------------------------------------------------------------------ slot scan
+def slot_workspace_bytes(B, L, H, hd, chunk):
+    return int(_lib.load().hdc_slot_workspace_bytes(B, L, H, hd, chunk))
+
+
+def feature_block(hd):
+    b = 1
+    while b < hd:
+        b <<= 1
+    return max(64, b)
+
+
+def slot_scan(q, k, v, num_heads, chunk, gamma=None, log_a=None, rows=None, y=None, y_strides=None,
+              state_in=None, return_state=False):
+    """Slot memory scan (replaces ``_slot_all_fused``, hdcmamba/model.py:236-272).
+
+    q, k, v: [B, L, H*hd] views sharing strides (unit last-dim stride), raw
+    (before phi).  gamma: [H] (in the activation dtype) or log_a: fp32 [B, L, H].
+    y: optional output tensor with element strides ``y_strides = (sb, sh, st)``
+    (element (b, t, h, d) at b*sb + h*sh + t*st + d); default [B, L, H, hd].
+    Returns y (and the fp32 final state [B, H, bd, bd] if ``return_state``)."""
+    _cuda(q, k, v, gamma, log_a, y, state_in)
+    _same_dtype(q, k, v)
+    B, L, W = q.shape
+    H = num_heads
+    hd = W // H
+    if W != H * hd or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must be [B, L, H*hd] with equal shapes")
+    if q.stride() != k.stride() or q.stride() != v.stride() or q.stride(2) != 1:
+        raise ValueError("q, k, v must share strides with unit last-dim stride")
+    if (gamma is None) == (log_a is None):
+        raise ValueError("give exactly one of gamma (constant decay) or log_a (per-step decay)")
+    if gamma is not None:
+        gamma = gamma.to(q.dtype).contiguous()
+    if log_a is not None:
+        log_a = log_a.float().contiguous()
+        if tuple(log_a.shape) != (B, L, H):
+            raise ValueError("log_a must be [B, L, H]")
+    rows = chunk if rows is None else rows
+    if y is None:
+        y = torch.empty(B, L, H, hd, device=q.device, dtype=q.dtype)
+        y_strides = (L * H * hd, hd, H * hd)
+    elif y_strides is None:
+        raise ValueError("y_strides is required with y")
+    _same_dtype(q, y)
+    bd = feature_block(hd)
+    state_out = torch.empty(B, H, bd, bd, device=q.device, dtype=torch.float32) if return_state else None
+    if state_in is not None:
+        state_in = state_in.float().contiguous()
+    nbytes = slot_workspace_bytes(B, L, H, hd, chunk)
+    ws = torch.empty(max(nbytes, 16), device=q.device, dtype=torch.uint8)
+    _lib.call("hdc_slot_scan_fwd", _code(q), _p(q), _p(k), _p(v), q.stride(0), q.stride(1), _p(gamma), _p(log_a),
+              _p(y), y_strides[0], y_strides[1], y_strides[2], _p(state_in), _p(state_out), _p(ws), ws.numel(),
+              B, L, H, hd, chunk, rows, _stream(q))
+    return (y, state_out) if return_state else y
+
+
+# ------------------------------------------------------------------ gate / concat / LN
+def gate_cat(y_slot, slot_strides, slot_rows, y_ssm, ssm_strides, gate, gate_strides, gn_w, gn_b, out,
+             out_strides, B, L, H, hd, ds):
+    """GroupNorm(head) * sigmoid(gate), concatenated after y_ssm (replaces
+    ``_fused_gnorm_gate_cat_kernel``, hdcmamba/model.py:274-295).  Strides are in
+    elements and follow the reference launch (hdcmamba/model.py:377); the
+    pointers are the base addresses of the given tensors (views allowed)."""
+    _cuda(y_slot, y_ssm, gate, gn_w, gn_b, out)
+    _same_dtype(out, y_slot, y_ssm, gate)
+    gw = gn_w.to(out.dtype).contiguous()
+    gb = gn_b.to(out.dtype).contiguous()
+    _lib.call("hdc_gate_cat_fwd", _code(out), _p(y_slot), slot_strides[0], slot_strides[1], slot_strides[2],
+              slot_rows, _p(y_ssm), ssm_strides[0], ssm_strides[1], _p(gate), gate_strides[0], gate_strides[1],
+              _p(gw), _p(gb), _p(out), out_strides[0], out_strides[1], B, L, H, hd, ds, _stream(out))
+    return out
+
+
+def row_layernorm(x, eps=1e-5, out=None):
+    """LayerNorm over the last dim without affine, fp32 statistics, result in x.dtype
+    (replaces ``F.layer_norm(combined.float(), (ds+dm,)).to(x.dtype)``, hdcmamba/model.py:382)."""
+    _cuda(x, out)
+    if not x.is_contiguous():
+        raise ValueError("row_layernorm needs a contiguous input")
+    if out is None:
+        out = torch.empty_like(x)
+    width = x.shape[-1]
+    _lib.call("hdc_row_layernorm", _code(x), _p(x), _p(out), x.numel() // width, width, float(eps), _stream(x))
+    return out

@@ -1,0 +1,157 @@
+/*
+ * hdcmamba_b200 -- C ABI of the B200 (sm_100a) kernels for HdcMamba-9v3's layer forward.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, and
+ * a cudaStream_t; none allocates device memory.  Kernels are launched
+ * asynchronously on `stream`.  Return value: 0 on success, a negative HDC_E*
+ * code for a rejected argument (nothing launched), or a positive cudaError_t
+ * from the launch.  hdc_error_string() describes the last error of the calling
+ * thread.
+ *
+ * dtype codes: HDC_F32 (fp32 activations) or HDC_BF16 (bf16 activations).
+ * Unless stated otherwise, activations are in `dtype`, norm/conv/gn parameters
+ * in `dtype`, and decay / state tensors in fp32.
+ *
+ * Each declaration names the reference code it replaces (N01N9/hdcmamba,
+ * file:line).  The reference is Python + Triton; its "FFI" for this path is the
+ * Triton launch `kernel[grid](...)`, so the arguments below follow those
+ * launches' pointer / stride / size arguments.
+ */
+#ifndef HDCMAMBA_B200_H
+#define HDCMAMBA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hdc_stream_t; /* == cudaStream_t */
+
+enum { HDC_F32 = 0, HDC_BF16 = 1 };
+enum { HDC_ACT_NONE = 0, HDC_ACT_SILU = 1 };
+enum {
+  HDC_OK = 0,
+  HDC_E_DTYPE = -1,    /* unsupported dtype code */
+  HDC_E_SHAPE = -2,    /* a size is out of the supported range */
+  HDC_E_ALIGN = -3,    /* a pointer / stride breaks the 16-byte vector rule */
+  HDC_E_NULL = -4,     /* a required pointer is NULL */
+  HDC_E_WORKSPACE = -5 /* workspace too small */
+};
+
+/* Library version and the compute capability it was built for (100 = sm_100a). */
+int hdc_version(void);
+int hdc_built_arch(void);
+const char* hdc_error_string(void);
+/* Number of kernel launches this library has issued in the process (all devices). */
+long long hdc_launch_count(void);
+
+/*
+ * LayerNorm over D, then causal depthwise conv1d of width 4 over L, optional SiLU.
+ * Replaces _fused_norm_conv_fwd_kernel (hdcmamba/model.py:22-72) as launched by
+ * FusedNormConv1dFunction.forward (hdcmamba/model.py:128-146).
+ *   x, out    : [B, L, D] contiguous, dtype.  out must not alias x.
+ *   norm_w/b  : [D]; conv_w : [D, 4] (tap k multiplies row t-3+k); conv_b : [D].
+ *   halo      : NULL, or [B, 3, D] rows that precede x[:, 0] (sequence-parallel
+ *               segments); NULL means rows before t=0 are zeros, whose
+ *               LayerNorm is norm_b (hdcmamba/model.py:47-57).
+ *   mean,rstd : NULL, or [B, L] bf16 per-row statistics (hdcmamba/model.py:67-68).
+ *   act       : HDC_ACT_NONE (the reference) or HDC_ACT_SILU.
+ * D must be a multiple of 8 (bf16) / 4 (fp32), D <= 8192; pointers 16-byte aligned.
+ */
+int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* norm_b,
+                    const void* conv_w, const void* conv_b, const void* halo, void* out,
+                    void* mean, void* rstd, int64_t B, int64_t L, int64_t D, float eps, int act,
+                    hdc_stream_t stream);
+
+/*
+ * Diagonal SSM chunk statistics (pass 1 of the chunked scan).
+ * Replaces _ssm_intra_v2's last_state / chunk_decay outputs (hdcmamba/model.py:175-198,
+ * launched at 345-350).  For batch b and chunk n (C steps), per channel j < ds:
+ *   stats[((b*N)+n)*2*ds + j]      = bf16(h at the chunk end, started from 0)
+ *   stats[((b*N)+n)*2*ds + ds + j] = bf16(sum of dt_s*A over the chunk)
+ * (fp32 storage holding bf16-rounded values).
+ *   projs     : row (b, t) starts at projs + b*proj_sb + t*proj_st; columns
+ *               [0,ds) dt, [ds,2ds) x, [2ds,3ds) b (hdcmamba/model.py:189-191).
+ *   A_log     : [ds], dtype.
+ * L must be a multiple of C; ds a power of two in [16, 256].
+ */
+int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                        const void* A_log, float* stats, int64_t B, int64_t L, int64_t ds,
+                        int64_t C, hdc_stream_t stream);
+
+/*
+ * Diagonal SSM outputs (pass 2): exclusive prefix over chunk statistics, then
+ * y = bf16(bf16(y_intra) + G_n * exp(cum_log)).
+ * Replaces _ssm_scan_v2 + _ssm_inter_v2 (hdcmamba/model.py:200-233, launched 352-363).
+ *   stats     : [B, n_prev + N, 2*ds] from hdc_ssm_chunk_stats; the first n_prev
+ *               chunks precede this segment (sequence-parallel: earlier ranks),
+ *               stats_sb = (n_prev+N)*2*ds is the batch stride in floats.
+ *   y         : element (b, t, j) at y + b*y_sb + t*y_st + j, dtype.
+ */
+int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                     const void* A_log, const float* stats, int64_t stats_sb, int64_t n_prev,
+                     void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds,
+                     int64_t C, hdc_stream_t stream);
+
+/*
+ * Slot memory: size in bytes of the fp32 workspace hdc_slot_scan_fwd needs.
+ */
+size_t hdc_slot_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
+
+/*
+ * Slot memory: chunked decayed linear attention with a (bd x bd) fp32 state per
+ * (batch, head), bd = max(64, pow2(hd)).
+ * Replaces _slot_all_fused (hdcmamba/model.py:236-272, launched at 365-371).
+ *   q, k, v   : element (b, t, h, d) at ptr + b*in_sb + t*in_st + h*hd + d (dtype);
+ *               for the Block these are column slices of projs.
+ *   gamma     : [H] per-head decay in dtype (gamma_buf.to(x.dtype), model.py:335),
+ *               used when log_a is NULL.
+ *   log_a     : NULL, or fp32 per-step log decay, element (b,t,h) at
+ *               log_a + (b*L + t)*H + h (the per-step generalisation).
+ *   y         : element (b, t, h, d) at y + b*y_sb + h*y_sh + t*y_st + d (dtype).
+ *   rows      : rows of each chunk a launch covers (the reference's slot_block_c
+ *               when smaller than C, hdcmamba/model.py:17); rows == C normally.
+ *   state_in  : NULL or fp32 [B*H, bd, bd] initial state; state_out: NULL or
+ *               fp32 [B*H, bd, bd] state after the last chunk.
+ *   workspace : hdc_slot_workspace_bytes(...) bytes of device memory.
+ * bf16 activations run the tcgen05 tensor-core kernel; fp32 runs the CUDA-core kernel.
+ */
+int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                      int64_t in_st, const void* gamma, const float* log_a, void* y, int64_t y_sb,
+                      int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
+                      void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                      int64_t hd, int64_t C, int64_t rows, hdc_stream_t stream);
+
+/*
+ * GroupNorm over each head of y_slot, times sigmoid(gate), concatenated after y_ssm.
+ * Replaces _fused_gnorm_gate_cat_kernel (hdcmamba/model.py:274-295, launched at 375-380);
+ * the stride arguments mirror that launch, so the reference's literal strides
+ * (shipped quirks) and corrected strides are both expressible.
+ *   y_slot element (b,h,l,d): y_slot + (b*H+h)*slot_s_bh + (l/slot_rows)*slot_s_n
+ *                             + (l%slot_rows)*slot_s_c + d
+ *   y_ssm  element (b,l,j)  : y_ssm + b*ssm_s_b + l*ssm_s_l + j
+ *   gate   element (b,l,h,d): gate + b*gate_s_b + l*gate_s_l + h*hd + d
+ *   out    element (b,l,c)  : out + b*out_s_b + l*out_s_l + c, c in [0, ds+H*hd)
+ *   gn_w, gn_b : [H*hd] (dtype).  eps = 1e-5 (hdcmamba/model.py:291).
+ */
+int hdc_gate_cat_fwd(int dtype, const void* y_slot, int64_t slot_s_bh, int64_t slot_s_n,
+                     int64_t slot_s_c, int64_t slot_rows, const void* y_ssm, int64_t ssm_s_b,
+                     int64_t ssm_s_l, const void* gate, int64_t gate_s_b, int64_t gate_s_l,
+                     const void* gn_w, const void* gn_b, void* out, int64_t out_s_b,
+                     int64_t out_s_l, int64_t B, int64_t L, int64_t H, int64_t hd, int64_t ds,
+                     hdc_stream_t stream);
+
+/*
+ * Row LayerNorm without affine, fp32 statistics, result in dtype (in place allowed).
+ * Replaces F.layer_norm(combined.float(), (ds+dm,)).to(x.dtype) (hdcmamba/model.py:382).
+ *   in/out : [rows, width] contiguous.
+ */
+int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t rows, int64_t width,
+                      float eps, hdc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HDCMAMBA_B200_H */
