@@ -104,6 +104,53 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def _time_cuda(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def kernel_c2(dev, iters, hbm):
+    """LayerNorm + causal conv1d (width 4) + SiLU, x bf16 [8, 8192, 2048]
+    (268 MB in, 268 MB out: larger than L2, so no flush is needed)."""
+    from hdcmamba_b200 import ops
+    B, L, D = 8, 8192, 2048
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, L, D, device=dev, generator=g).bfloat16()
+    cw = (0.02 * torch.randn(D, 4, device=dev, generator=g)).bfloat16()
+    nw, nb, cb = (torch.ones(D, device=dev).bfloat16(), torch.zeros(D, device=dev).bfloat16(),
+                  torch.zeros(D, device=dev).bfloat16())
+    ms = _time_cuda(lambda: ops.ln_conv(x, nw, nb, cw, cb, 1e-5, act="silu"), iters)
+    nbytes = 2 * B * L * D * 2
+    return {"workload": "c2: ln_conv+silu bf16 [8,8192,2048]", "ms_per_launch": ms,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm}
+
+
+def kernel_c3(dev, iters, hbm):
+    """slot scan with per-step decay, q/k/v bf16 [4, 32768, 16, 64],
+    a = sigmoid(N(0,1)) fp32, chunk 64, zero initial state, final state returned."""
+    from hdcmamba_b200 import ops
+    B, L, H, hd, C = 4, 32768, 16, 64, 64
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, k, v = (torch.randn(B, L, H * hd, device=dev, generator=g).bfloat16() for _ in range(3))
+    log_a = torch.nn.functional.logsigmoid(torch.randn(B, L, H, device=dev, generator=g))
+    y = torch.empty(B, L, H, hd, device=dev, dtype=torch.bfloat16)
+    ms = _time_cuda(lambda: ops.slot_scan(q, k, v, H, C, log_a=log_a, y=y, y_strides=(L * H * hd, hd, H * hd),
+                                          return_state=True), iters)
+    nbytes = 4 * B * L * H * hd * 2 + B * L * H * 4 + B * H * 64 * 64 * 4
+    flops = B * L * H * (4 * C * hd + 4 * hd * hd)
+    return {"workload": "c3: slot scan per-step decay bf16 [4,32768,16,64] C64", "ms_per_launch": ms,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm,
+            "algorithmic_flop": flops, "achieved_tflops": flops / ms / 1e9}
+
+
 def cpu_oracle_tokens_per_s(cfg, tokens, repeats=2):
     """CPU oracle port (oracle/restate.py, fp32 math with the bf16 rounding points) on
     the first ``tokens`` ids, all layers and the full vocab head."""
@@ -170,6 +217,9 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=512)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
+    ap.add_argument("--workload", default=None, choices=["c2", "c3"],
+                    help="time one kernel workload alone (for profiling) and print its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -181,6 +231,12 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, cfg, rank)
+    if args.workload:
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        fn = kernel_c2 if args.workload == "c2" else kernel_c3
+        print(json.dumps(fn(dev, args.steps, peaks()[0])), flush=True)
+        return
 
     import torch.distributed as dist
     from datetime import timedelta
@@ -284,6 +340,8 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
         }
+        if world == 1 and not args.no_kernels:
+            line["kernels"] = [kernel_c2(dev, 20, hbm), kernel_c3(dev, 10, hbm)]
         if world == 1 and not args.no_cpu_baseline:
             v, cores = cpu_oracle_tokens_per_s(cfg, args.cpu_tokens)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",

@@ -22,5 +22,8 @@ __device__ __forceinline__ float trnd(float v) { return store_round<T>(v); }
 
 size_t slot_simt_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
 int slot_simt_fwd(int dtype, SlotParams p, int64_t B, void* ws, cudaStream_t s);
+size_t slot_tc_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
+bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st);
+int slot_tc_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s);
 
 }  // namespace hdc

@@ -4,9 +4,21 @@
 
 using namespace hdc;
 
+static int g_path_mode = 0;                // 0 auto, 1 force CUDA-core, 2 require tcgen05
+static thread_local int g_last_path = -1;  // 1 tcgen05, 0 CUDA-core
+
+extern "C" int hdc_slot_set_path(int mode) {
+  if (mode < 0 || mode > 2) return fail(HDC_E_SHAPE, "slot: path mode %d", mode);
+  g_path_mode = mode;
+  return 0;
+}
+
+extern "C" int hdc_slot_last_path(void) { return g_last_path; }
+
 extern "C" size_t hdc_slot_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C) {
   if (B < 1 || H < 1 || hd < 1 || C < 1 || L < C) return 0;
-  return slot_simt_workspace(B, L, H, hd, C);
+  const size_t a = slot_simt_workspace(B, L, H, hd, C), b = slot_tc_workspace(B, L, H, hd, C);
+  return a > b ? a : b;
 }
 
 extern "C" int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
@@ -29,5 +41,8 @@ extern "C" int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const 
   p.L = (int)L; p.H = (int)H; p.hd = (int)hd; p.C = (int)C; p.rows = (int)rows; p.N = (int)(L / C);
   p.bd = (int)feature_block(hd);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  return slot_simt_fwd(dtype, p, B, workspace, s);
+  const bool tc = dtype == HDC_BF16 && g_path_mode != 1 && slot_tc_supported(p, B, in_sb, in_st);
+  if (g_path_mode == 2 && !tc) return fail(HDC_E_SHAPE, "slot: tcgen05 path required but not applicable");
+  g_last_path = tc ? 1 : 0;
+  return tc ? slot_tc_fwd(p, B, in_sb, in_st, workspace, s) : slot_simt_fwd(dtype, p, B, workspace, s);
 }

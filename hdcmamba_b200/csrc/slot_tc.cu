@@ -1,0 +1,583 @@
+// Slot memory scan on tcgen05 tensor cores (bf16 activations, feature width 64), sm_100a.
+//
+// Math: the chunked decayed linear attention of the reference _slot_all_fused
+// (hdcmamba/model.py:236-272); see slot_simt.cu for the formulas.  Layout and schedule:
+//
+//   * Work unit: one CTA (4 warps) per (batch*head, segment of consecutive chunks).
+//     Pass A (slot_tc_state_kernel) computes every segment's local state (from zero)
+//     and decay product; pass B (slot_tc_out_kernel) folds the states of the earlier
+//     segments into its entering state, then walks its chunks producing outputs.
+//   * Per chunk, TMA loads K and V (C x 64 bf16, 128-byte swizzle) and Q per 128-row
+//     block into shared memory; phi and the reference's feature padding (ones for q/k,
+//     zeros for v beyond head_dim) are applied in place.
+//   * Tensor-core products (one elected thread issues tcgen05.mma, fp32 accumulators in
+//     TMEM, 256 columns per CTA):
+//       S   = phi(Q_blk) phi(K_cb)^T         M=rows, N=64, K=64    TMEM cols [0,64)
+//       Yi += P_cb V_cb                      M=rows, N=64, K=64    TMEM cols [64,128)
+//       Yx  = phi(Q_blk) bf16(R)             M=rows, N=64, K=64    TMEM cols [128,192)
+//       U   = bf16(phi(K) kdec)^T V          M=64,   N=64, K=C     TMEM cols [192,256)
+//     with P_cb = bf16(mask(S) * decay) written by the threads back to shared memory.
+//   * y = bf16(Yi + qdec_i * Yx); R <- gC * R + U in fp32 registers (rows of R are owned
+//     by the 64 threads that hold the M=64 accumulator rows).
+// The decays use a table pw[k] = exp(k * log(gamma)) (constant gamma, the same
+// expression the reference evaluates per element) or the chunk's cumulative log
+// decay c_i (per-step decay).
+#include "slot.cuh"
+#include "tc.cuh"
+
+namespace hdc {
+
+struct SlotTcParams {
+  const void* gamma;
+  const float* log_a;
+  void* y;
+  int64_t y_sb, y_sh, y_st;
+  const float* state_in;
+  float* state_out;
+  float* Rseg;  // [BH][nseg][64*64]
+  float* Dseg;  // [BH][nseg]
+  int L, H, hd, N, nseg, seg_len, y_vec;
+};
+
+constexpr int kThreads = 128;
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// phi in place on a [rows x 64] swizzled bf16 tile; columns >= hd become `pad`.
+__device__ __forceinline__ void prep_tile(uint8_t* tile, int rows, int hd, bool apply_phi, float pad) {
+  for (int idx = threadIdx.x; idx < rows * 8; idx += kThreads) {
+    const int row = idx >> 3, pc = idx & 7;
+    const int c0 = ((pc ^ (row & 7)) << 3);
+    uint4* p = reinterpret_cast<uint4*>(tile + row * 128 + pc * 16);
+    if (!apply_phi && c0 + 8 <= hd) continue;
+    float f[8];
+    unpack16<__nv_bfloat16>(*p, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = (c0 + e < hd) ? (apply_phi ? phi(f[e]) : f[e]) : pad;
+    *p = pack16<__nv_bfloat16>(f);
+  }
+}
+
+// chunk-local cumulative log decay (per-step mode) by warp 0:
+//   tab[i] = c_i = sum_{t=1..i} log_a[c0+t], tab[C] = c_{C-1} + log_a[c0] (chunk decay exponent)
+template <int CT>
+__device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float* tab) {
+  constexpr int E = CT / 32;
+  const int lane = threadIdx.x & 31;
+  float v[E];
+  float run = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = lane * E + e;
+    run += (i == 0) ? 0.f : la[(size_t)i * H];
+    v[e] = run;
+  }
+  float incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const float off = incl - run;
+#pragma unroll
+  for (int e = 0; e < E; ++e) tab[lane * E + e] = off + v[e];
+  __syncwarp();
+  if (lane == 0) tab[CT] = tab[CT - 1] + la[0];
+}
+
+// ---------------------------------------------------------------------------------
+// Pass A: per-segment local state Rseg = sum_m (prod_{m'>m} gC_m') U_m and Dseg = prod gC_m
+// ---------------------------------------------------------------------------------
+template <int CT, bool PERSTEP>
+__global__ void __launch_bounds__(kThreads, 1)
+    slot_tc_state_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
+                         SlotTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* sK = base;
+  uint8_t* sV = sK + CT * 128;
+  float* sTab = reinterpret_cast<float*>(sV + CT * 128);   // [CT + 4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + CT + 4);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nseg_a = p.nseg - 1;
+  const int bh = blockIdx.x / nseg_a, seg = blockIdx.x - bh * nseg_a;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
+
+  if (warp == 0) {
+    tmem_alloc(sTmem, 64);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+    tma_prefetch_map(&mapK);
+    tma_prefetch_map(&mapV);
+  }
+  float lg = 0.f;
+  if (!PERSTEP) {
+    lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
+    for (int k = tid; k <= CT; k += kThreads) sTab[k] = expf((float)k * lg);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tU = *sTmem;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t idU = idesc_bf16_f32(64, 64, true, true);
+
+  float R[64];
+#pragma unroll
+  for (int e = 0; e < 64; ++e) R[e] = 0.f;
+  float D = 1.f;
+  uint32_t tph = 0, mph = 0;
+  bool ok = true;
+
+  auto issue = [&](int n) {
+    mbar_expect_tx(&bars[0], 2 * CT * 128);
+    tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
+    tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
+  };
+  if (tid == 0 && n0 < n1) issue(n0);
+  for (int n = n0; n < n1 && ok; ++n) {
+    if (!mbar_wait(&bars[0], tph, 11)) { ok = false; break; }
+    tph ^= 1;
+    if (PERSTEP) {
+      if (warp == 0) chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
+      __syncthreads();
+    }
+    // k~ = bf16(bf16(phi(k)) * kdec_j) in place; v padding
+    for (int idx = tid; idx < CT * 8; idx += kThreads) {
+      const int row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
+      const float kd = PERSTEP ? expf(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
+      uint4* pk = reinterpret_cast<uint4*>(sK + row * 128 + pc * 16);
+      float f[8];
+      unpack16<__nv_bfloat16>(*pk, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = bf16_round((c0 + e < p.hd) ? bf16_round(phi(f[e])) : 1.f) * kd;
+      *pk = pack16<__nv_bfloat16>(f);
+    }
+    if (p.hd < 64) prep_tile(sV, CT, p.hd, false, 0.f);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < CT / 16; ++kk)
+        umma_bf16(tU, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024), sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024),
+                  idU, kk > 0 ? 1u : 0u);
+      umma_commit(&bars[1]);
+    }
+    if (!mbar_wait(&bars[1], mph, 12)) { ok = false; break; }
+    mph ^= 1;
+    tc_fence_after();
+    if (tid == 0 && n + 1 < n1) issue(n + 1);
+    const float gC = PERSTEP ? expf(sTab[CT]) : sTab[CT];
+    float u[32];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tmem_ld32(tU + lane_base + half * 32, u);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) R[half * 32 + e] = R[half * 32 + e] * gC + u[e];
+    }
+    D *= gC;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  if (ok && lane < 16) {
+    const int f = warp * 16 + lane;
+    float* dst = p.Rseg + ((size_t)bh * p.nseg + seg) * 4096 + f * 64;
+#pragma unroll
+    for (int e = 0; e < 64; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
+  }
+  if (ok && tid == 0) p.Dseg[(size_t)bh * p.nseg + seg] = D;
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tU, 64);
+}
+
+// ---------------------------------------------------------------------------------
+// Pass B: outputs
+// ---------------------------------------------------------------------------------
+template <int CT, bool PERSTEP>
+__global__ void __launch_bounds__(kThreads, 1)
+    slot_tc_out_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                       const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
+  constexpr int RB = CT < 128 ? CT : 128;  // rows per block (MMA M)
+  constexpr int NRB = CT / RB;
+  constexpr int CB = 64;                   // S column block (MMA N)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* sK = base;
+  uint8_t* sV = sK + CT * 128;
+  uint8_t* sQ = sV + CT * 128;
+  uint8_t* sP = sQ + RB * 128;
+  uint8_t* sR = sP + RB * 128;
+  float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + CT + 4);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.x / p.nseg, seg = blockIdx.x - bh * p.nseg;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
+  // row of the M=RB accumulators this thread holds (M=64: lanes 0-15 of each warp)
+  const int my_row = (RB == 128) ? tid : (lane < 16 ? warp * 16 + lane : -1);
+  const bool u_row = lane < 16;             // holds row (warp*16 + lane) of U and R
+  const int f_row = warp * 16 + lane;
+
+  if (warp == 0) {
+    tmem_alloc(sTmem, 256);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+    tma_prefetch_map(&mapQ);
+    tma_prefetch_map(&mapK);
+    tma_prefetch_map(&mapV);
+  }
+  float lg = 0.f;
+  if (!PERSTEP) {
+    lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
+    for (int k = tid; k <= CT; k += kThreads) sTab[k] = expf((float)k * lg);
+  }
+
+  // entering state: state_in folded with the earlier segments' local states
+  float R[64];
+#pragma unroll
+  for (int e = 0; e < 64; ++e) R[e] = 0.f;
+  if (u_row) {
+    if (p.state_in) {
+      const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) R[e] = src[e];
+    }
+    for (int s = 0; s < seg; ++s) {
+      const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+      const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) R[e] = Ds * R[e] + src[e];
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, c)) = pack16<__nv_bfloat16>(&R[c * 8]);
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t tS = tmem, tYi = tmem + 64, tYx = tmem + 128, tU = tmem + 192;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  constexpr uint32_t idS = idesc_bf16_f32(RB, CB, false, false);
+  constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
+  constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
+
+  uint32_t tph = 0, mph = 0;
+  bool ok = true;
+  auto issue = [&](int n) {
+    mbar_expect_tx(&bars[0], 2 * CT * 128 + RB * 128);
+    tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
+    tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
+    tma_load_3d(sQ, &mapQ, h * p.hd, n * CT, b, &bars[0]);
+  };
+  if (tid == 0 && n0 < n1) issue(n0);
+
+  for (int n = n0; n < n1 && ok; ++n) {
+    if (!mbar_wait(&bars[0], tph, 21)) { ok = false; break; }
+    tph ^= 1;
+    if (PERSTEP && warp == 0)
+      chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
+    prep_tile(sK, CT, p.hd, true, 1.f);
+    if (p.hd < 64) prep_tile(sV, CT, p.hd, false, 0.f);
+
+    for (int rb = 0; rb < NRB && ok; ++rb) {
+      const int r0 = rb * RB;
+      if (rb > 0) {
+        if (tid == 0) {
+          mbar_expect_tx(&bars[0], RB * 128);
+          tma_load_3d(sQ, &mapQ, h * p.hd, n * CT + r0, b, &bars[0]);
+        }
+        if (!mbar_wait(&bars[0], tph, 22)) { ok = false; break; }
+        tph ^= 1;
+      }
+      prep_tile(sQ, RB, p.hd, true, 1.f);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (tid == 0) {
+        // Yx = phi(Q) bf16(R)   (A K-major, B = R rows f with e contiguous: MN-major)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_bf16(tYx, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024),
+                    idPV, k > 0 ? 1u : 0u);
+      }
+      const int ncb = (r0 + RB) / CB;
+      for (int cb = 0; cb < ncb; ++cb) {
+        if (tid == 0) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(tS, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024),
+                      sdesc_sw128(smem_u32(sK) + cb * CB * 128 + k * 32, 16, 1024), idS, k > 0 ? 1u : 0u);
+          umma_commit(&bars[1]);
+        }
+        if (!mbar_wait(&bars[1], mph, 23)) { ok = false; break; }
+        mph ^= 1;
+        tc_fence_after();
+        // P = bf16(mask(S) * decay) -> sP (K-major, one 64-column swizzle atom)
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float s[32];
+          tmem_ld32(tS + lane_base + half * 32, s);
+          if (my_row >= 0) {
+            const int i = r0 + my_row;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float v[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int j = cb * CB + half * 32 + q * 8 + e;
+                float dm = 0.f;
+                if (j <= i) dm = PERSTEP ? expf(sTab[i] - sTab[j]) : sTab[i - j];
+                v[e] = (j <= i) ? s[q * 8 + e] * dm : 0.f;
+              }
+              *reinterpret_cast<uint4*>(sP + sw128_chunk(my_row, half * 4 + q)) = pack16<__nv_bfloat16>(v);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (tid == 0) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(tYi, sdesc_sw128(smem_u32(sP) + k * 32, 16, 1024),
+                      sdesc_sw128(smem_u32(sV) + (cb * CB + k * 16) * 128, 0, 1024), idPV,
+                      (cb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&bars[1]);
+        }
+        if (!mbar_wait(&bars[1], mph, 24)) { ok = false; break; }
+        mph ^= 1;
+        tc_fence_after();
+      }
+      if (!ok) break;
+      // epilogue: y = bf16(Yi + qdec_i * Yx)
+      {
+        float yi[32], yx[32];
+        const int i = r0 + (my_row >= 0 ? my_row : 0);
+        const float qd = PERSTEP ? expf(sTab[i]) : sTab[i];
+        const int t = n * CT + i;
+        __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                              (size_t)t * p.y_st;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(tYi + lane_base + half * 32, yi);
+          tmem_ld32(tYx + lane_base + half * 32, yx);
+          if (my_row >= 0) {
+            float o[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = yi[e] + qd * yx[e];
+            if (p.y_vec) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int d0 = half * 32 + q * 8;
+                if (d0 < p.hd) stg16(yrow + d0, pack16<__nv_bfloat16>(&o[q * 8]));
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (half * 32 + e < p.hd) yrow[half * 32 + e] = __float2bfloat16_rn(o[e]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+    }
+    if (!ok) break;
+    // state update: k~ = bf16(phi(k) * kdec_j) in place, U = k~^T V, R = gC R + U
+    for (int idx = tid; idx < CT * 8; idx += kThreads) {
+      const int row = idx >> 3, pc = idx & 7;
+      const float kd = PERSTEP ? expf(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
+      uint4* pk = reinterpret_cast<uint4*>(sK + row * 128 + pc * 16);
+      float f[8];
+      unpack16<__nv_bfloat16>(*pk, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= kd;
+      *pk = pack16<__nv_bfloat16>(f);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int kk = 0; kk < CT / 16; ++kk)
+        umma_bf16(tU, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024), sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024),
+                  idU, kk > 0 ? 1u : 0u);
+      umma_commit(&bars[1]);
+    }
+    if (!mbar_wait(&bars[1], mph, 25)) { ok = false; break; }
+    mph ^= 1;
+    tc_fence_after();
+    if (tid == 0 && n + 1 < n1) issue(n + 1);
+    const float gC = PERSTEP ? expf(sTab[CT]) : sTab[CT];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float u[32];
+      tmem_ld32(tU + lane_base + half * 32, u);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) R[half * 32 + e] = R[half * 32 + e] * gC + u[e];
+    }
+    if (u_row) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, c)) = pack16<__nv_bfloat16>(&R[c * 8]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  if (ok && seg == p.nseg - 1 && p.state_out && u_row) {
+    float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64;
+#pragma unroll
+    for (int e = 0; e < 64; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 3-D map (columns, positions, batch) over bf16 rows: `width` columns, rows
+// `row_stride` elements apart, batches `batch_stride` elements apart; box 64 x box_rows x 1.
+static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, int64_t B, int64_t row_stride,
+                    int64_t batch_stride, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(HDC_E_SHAPE, "slot_tc: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)width, (cuuint64_t)L, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2, (cuuint64_t)batch_stride * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HDC_E_SHAPE, "slot_tc: tensor map encode failed (%d)", (int)r);
+  return 0;
+}
+
+static size_t smem_out_bytes(int CT) {
+  const int RB = CT < 128 ? CT : 128;
+  return 1024 + 2 * CT * 128 + 2 * RB * 128 + 64 * 128 + (CT + 4) * 4 + 64;
+}
+static size_t smem_state_bytes(int CT) { return 1024 + 2 * CT * 128 + (CT + 4) * 4 + 64; }
+
+static void plan_segments(int64_t BH, int N, int* nseg, int* seg_len) {
+  const int slots = num_sms() * 2;
+  int s = (int)(slots / BH);
+  if (s < 1) s = 1;
+  if (s > N) s = N;
+  int len = (N + s - 1) / s;
+  *seg_len = len;
+  *nseg = (N + len - 1) / len;
+}
+
+size_t slot_tc_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C) {
+  int nseg, len;
+  plan_segments(B * H, (int)(L / C), &nseg, &len);
+  return (size_t)(B * H) * nseg * (4096 + 1) * sizeof(float) + 256;
+}
+
+bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st) {
+  if (p.bd != 64 || p.hd % 8 != 0) return false;
+  if (p.C != 64 && p.C != 128 && p.C != 256) return false;
+  if (p.rows != p.C) return false;
+  if (in_st % 8 != 0 || (B > 1 && in_sb % 8 != 0) || in_st < (int64_t)p.H * p.hd) return false;
+  if ((int64_t)p.H * p.hd < 64) return false;  // the TMA box is 64 columns wide
+  if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v)) return false;
+  return true;
+}
+
+template <int CT, bool PS>
+static int run_tc(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s) {
+  const int64_t BH = B * sp.H;
+  SlotTcParams p{};
+  p.gamma = sp.gamma; p.log_a = sp.log_a; p.y = sp.y; p.y_sb = sp.y_sb; p.y_sh = sp.y_sh; p.y_st = sp.y_st;
+  p.state_in = sp.state_in; p.state_out = sp.state_out;
+  p.L = sp.L; p.H = sp.H; p.hd = sp.hd; p.N = sp.N;
+  plan_segments(BH, sp.N, &p.nseg, &p.seg_len);
+  p.Rseg = static_cast<float*>(ws);
+  p.Dseg = p.Rseg + (size_t)BH * p.nseg * 4096;
+  p.y_vec = (aligned16(sp.y) && sp.y_sb % 8 == 0 && sp.y_sh % 8 == 0 && sp.y_st % 8 == 0 && sp.hd % 8 == 0) ? 1 : 0;
+  constexpr int RB = CT < 128 ? CT : 128;
+  const int64_t W = (int64_t)sp.H * sp.hd;
+  CUtensorMap mq, mk, mv;
+  const int64_t sb = B > 1 ? in_sb : (int64_t)sp.L * in_st;
+  if (int e = make_map(&mq, sp.q, W, sp.L, B, in_st, sb, RB)) return e;
+  if (int e = make_map(&mk, sp.k, W, sp.L, B, in_st, sb, CT)) return e;
+  if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
+  if (p.nseg > 1) {
+    const size_t sm = smem_state_bytes(CT);
+    cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * (p.nseg - 1)), kThreads, sm, s>>>(mk, mv, p);
+    if (int e = launch_status("slot_tc_state_kernel")) return e;
+  }
+  const size_t sm = smem_out_bytes(CT);
+  cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  slot_tc_out_kernel<CT, PS><<<(unsigned)(BH * p.nseg), kThreads, sm, s>>>(mq, mk, mv, p);
+  return launch_status("slot_tc_out_kernel");
+}
+
+int slot_tc_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s) {
+  const bool ps = p.log_a != nullptr;
+  switch (p.C) {
+    case 64: return ps ? run_tc<64, true>(p, B, in_sb, in_st, ws, s) : run_tc<64, false>(p, B, in_sb, in_st, ws, s);
+    case 128: return ps ? run_tc<128, true>(p, B, in_sb, in_st, ws, s) : run_tc<128, false>(p, B, in_sb, in_st, ws, s);
+    default: return ps ? run_tc<256, true>(p, B, in_sb, in_st, ws, s) : run_tc<256, false>(p, B, in_sb, in_st, ws, s);
+  }
+}
+
+}  // namespace hdc
+
+using namespace hdc;
+
+extern "C" int hdc_device_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v != 0) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
+  }
+  return v;
+}

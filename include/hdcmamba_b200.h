@@ -125,6 +125,24 @@ int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, in
                       int64_t hd, int64_t C, int64_t rows, hdc_stream_t stream);
 
 /*
+ * Slot-scan path control (tests / cross-checks): mode 0 = automatic (tcgen05 for bf16
+ * with feature width 64, chunk 64/128/256, 8-aligned head_dim and row-contiguous
+ * inputs; CUDA cores otherwise), 1 = always the CUDA-core kernel, 2 = require
+ * tcgen05 (calls that cannot use it fail with HDC_E_SHAPE).  Process-wide.
+ * hdc_slot_last_path(): 1 if the calling thread's last hdc_slot_scan_fwd ran the
+ * tcgen05 kernels, 0 for the CUDA-core kernels, -1 before any call.
+ */
+int hdc_slot_set_path(int mode);
+int hdc_slot_last_path(void);
+
+/*
+ * Device-side error word of the tcgen05 kernels: 0, or the code of a bounded wait
+ * (mbarrier) that timed out after ~2 s.  Synchronous; reset != 0 clears it.
+ * Returns -1 if the word could not be read.
+ */
+int hdc_device_error(int reset);
+
+/*
  * GroupNorm over each head of y_slot, times sigmoid(gate), concatenated after y_ssm.
  * Replaces _fused_gnorm_gate_cat_kernel (hdcmamba/model.py:274-295, launched at 375-380);
  * the stride arguments mirror that launch, so the reference's literal strides
