@@ -151,6 +151,26 @@ def kernel_c3(dev, iters, hbm):
             "algorithmic_flop": flops, "achieved_tflops": flops / ms / 1e9}
 
 
+def kernel_c5slot(dev, iters, hbm):
+    """One layer's slot scan with the fused GroupNorm * sigmoid(gate) epilogue at config-5
+    shapes (projs [1, 32768, 3264] bf16, d_model 768, 12 heads, chunk 256)."""
+    from hdcmamba_b200 import ops
+    B, L, ds, dm, H, C = 1, 32768, 64, 768, 12, 256
+    hd, P = dm // H, 3 * ds + 4 * dm
+    g = torch.Generator(device=dev).manual_seed(0)
+    projs = torch.randn(B, L, P, device=dev, generator=g).bfloat16()
+    gamma = torch.full((H,), 0.952, device=dev).bfloat16()
+    gw, gb = torch.ones(dm, device=dev).bfloat16(), torch.zeros(dm, device=dev).bfloat16()
+    comb = torch.empty(B, L, ds + dm, device=dev, dtype=torch.bfloat16)
+    so = 3 * ds
+    q, k, v, gt = (projs[..., so + i * dm:so + (i + 1) * dm] for i in range(4))
+    ms = _time_cuda(lambda: ops.slot_scan_gate(q, k, v, H, C, gt, gw, gb, comb[..., ds:],
+                                               (L * (ds + dm), hd, ds + dm), gamma=gamma), iters)
+    nbytes = 5 * B * L * dm * 2
+    return {"workload": "c5slot: slot scan + GN*sigmoid(gate) bf16, L32768 d768 H12 C256", "ms_per_launch": ms,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm}
+
+
 def cpu_oracle_tokens_per_s(cfg, tokens, repeats=2):
     """CPU oracle port (oracle/restate.py, fp32 math with the bf16 rounding points) on
     the first ``tokens`` ids, all layers and the full vocab head."""
@@ -218,7 +238,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
-    ap.add_argument("--workload", default=None, choices=["c2", "c3"],
+    ap.add_argument("--workload", default=None, choices=["c2", "c3", "c5slot"],
                     help="time one kernel workload alone (for profiling) and print its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -234,7 +254,7 @@ def main():
     if args.workload:
         torch.cuda.set_device(local)
         dev = torch.device("cuda", local)
-        fn = kernel_c2 if args.workload == "c2" else kernel_c3
+        fn = {"c2": kernel_c2, "c3": kernel_c3, "c5slot": kernel_c5slot}[args.workload]
         print(json.dumps(fn(dev, args.steps, peaks()[0])), flush=True)
         return
 
@@ -257,26 +277,27 @@ def main():
         with torch.no_grad():
             return lm(inp)
 
-    # instrument the slot scan (dominant custom kernel) with events on its stream
+    # instrument the slot scan (dominant custom kernel) with events on its launch stream
     slot_events = []
-    orig_slot = ops.slot_scan
+    originals = {name: getattr(ops, name) for name in ("slot_scan", "slot_scan_gate")}
 
-    def timed_slot(*a, **k):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        r = orig_slot(*a, **k)
-        e.record()
-        slot_events.append((s, e))
-        return r
+    def timed(fn):
+        def wrapper(*a, **k):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = fn(*a, **k)
+            e.record()
+            slot_events.append((s, e))
+            return r
+        return wrapper
 
     for _ in range(args.warmup):
         step(ids)
     torch.cuda.synchronize()
 
     sampler = ClockSampler(dev)
-    ops.slot_scan = timed_slot
-    import hdcmamba_b200.model as M
-    M.ops.slot_scan = timed_slot
+    for name, fn in originals.items():
+        setattr(ops, name, timed(fn))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -292,8 +313,8 @@ def main():
     clocks = sampler.stop()
     if world > 1:
         dist.barrier()
-    ops.slot_scan = orig_slot
-    M.ops.slot_scan = orig_slot
+    for name, fn in originals.items():
+        setattr(ops, name, fn)
     ms = t0.elapsed_time(t1) / args.steps
     slot_ms = statistics.mean(s.elapsed_time(e) for s, e in slot_events)
     slot_per_step = len(slot_events) / args.steps
@@ -318,7 +339,8 @@ def main():
 
     if rank == 0:
         hbm, src = peaks()
-        slot_bytes = 4 * cfg.batch * cfg.seq_len * cfg.d_model * 2   # q, k, v read + y written (bf16)
+        # q, k, v and gate read, the gated slot half of `combined` written (bf16)
+        slot_bytes = 5 * cfg.batch * cfg.seq_len * cfg.d_model * 2
         achieved = slot_bytes / (slot_ms * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": world * tokens_per_rank / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
@@ -330,7 +352,7 @@ def main():
                        "global_batch": cfg.batch * world, "seq_len": cfg.seq_len,
                        "parallelism": f"replicas{world}" if world > 1 else "single",
                        "l2": "working set > L2 (projs 214 MB/layer, weights 153 MB): no explicit flush"},
-            "roofline": {"kernel": "slot_scan", "bound": "hbm", "achieved": achieved, "peak": hbm,
+            "roofline": {"kernel": "slot_scan_gate (slot_tc_state + slot_tc_out)", "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
                          "traffic": SLOT_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": slot_bytes,
                          "ms_per_launch": slot_ms, "launches_per_step": slot_per_step},
@@ -341,7 +363,7 @@ def main():
             "clocks": clocks,
         }
         if world == 1 and not args.no_kernels:
-            line["kernels"] = [kernel_c2(dev, 20, hbm), kernel_c3(dev, 10, hbm)]
+            line["kernels"] = [kernel_c2(dev, 20, hbm), kernel_c3(dev, 10, hbm), kernel_c5slot(dev, 10, hbm)]
         if world == 1 and not args.no_cpu_baseline:
             v, cores = cpu_oracle_tokens_per_s(cfg, args.cpu_tokens)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",

@@ -37,7 +37,23 @@ int launch_status(const char* what) {
   return 0;
 }
 
+static int (*g_err_readers[16])(int) = {nullptr};
+static int g_n_err_readers = 0;
+
+void register_dev_error_reader(int (*reader)(int reset)) {
+  if (g_n_err_readers < 16) g_err_readers[g_n_err_readers++] = reader;
+}
+
 }  // namespace hdc
+
+extern "C" int hdc_device_error(int reset) {
+  int first = 0;
+  for (int i = 0; i < hdc::g_n_err_readers; ++i) {
+    const int v = hdc::g_err_readers[i](reset);
+    if (v != 0 && first == 0) first = v;
+  }
+  return first;
+}
 
 extern "C" int hdc_version(void) { return 100; }
 

@@ -14,6 +14,13 @@ struct SlotParams {
   int L, H, hd, C, rows, N, bd;
 };
 
+// Fused GroupNorm(head) * sigmoid(gate) epilogue of the tcgen05 kernel: gate element
+// (b, t, h, d) at gate + b*g_sb + t*g_st + h*hd + d; gn_w / gn_b are [H*hd].
+struct SlotGate {
+  const void* gate; int64_t g_sb, g_st;
+  const void* gn_w; const void* gn_b;
+};
+
 // phi(z) = z > 0 ? z + 1 : exp(z)  (hdcmamba/model.py:261-262)
 __device__ __forceinline__ float phi(float z) { return z > 0.f ? z + 1.f : expf(z); }
 
@@ -24,6 +31,7 @@ size_t slot_simt_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t 
 int slot_simt_fwd(int dtype, SlotParams p, int64_t B, void* ws, cudaStream_t s);
 size_t slot_tc_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
 bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st);
-int slot_tc_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s);
+int slot_tc_fwd(const SlotParams& p, const SlotGate* gate, int64_t B, int64_t in_sb, int64_t in_st, void* ws,
+                cudaStream_t s);
 
 }  // namespace hdc

@@ -3,25 +3,28 @@
 // Math: the chunked decayed linear attention of the reference _slot_all_fused
 // (hdcmamba/model.py:236-272); see slot_simt.cu for the formulas.  Layout and schedule:
 //
-//   * Work unit: one CTA (4 warps) per (batch*head, segment of consecutive chunks).
-//     Pass A (slot_tc_state_kernel) computes every segment's local state (from zero)
-//     and decay product; pass B (slot_tc_out_kernel) folds the states of the earlier
-//     segments into its entering state, then walks its chunks producing outputs.
+//   * Work unit: one CTA per (batch*head, segment of consecutive chunks).  Pass A
+//     (slot_tc_state_kernel) computes every segment's local state (from zero) and decay
+//     product; pass B (slot_tc_out_kernel) folds the states of the earlier segments into
+//     its entering state, then walks its chunks producing outputs.
 //   * Per chunk, TMA loads K and V (C x 64 bf16, 128-byte swizzle) and Q per 128-row
 //     block into shared memory; phi and the reference's feature padding (ones for q/k,
 //     zeros for v beyond head_dim) are applied in place.
-//   * Tensor-core products (one elected thread issues tcgen05.mma, fp32 accumulators in
-//     TMEM, 256 columns per CTA):
+//   * Tensor-core products (one thread issues tcgen05.mma; fp32 accumulators in TMEM,
+//     256 columns per CTA):
 //       S   = phi(Q_blk) phi(K_cb)^T         M=rows, N=64, K=64    TMEM cols [0,64)
 //       Yi += P_cb V_cb                      M=rows, N=64, K=64    TMEM cols [64,128)
 //       Yx  = phi(Q_blk) bf16(R)             M=rows, N=64, K=64    TMEM cols [128,192)
-//       U   = bf16(phi(K) kdec)^T V          M=64,   N=64, K=C     TMEM cols [192,256)
-//     with P_cb = bf16(mask(S) * decay) written by the threads back to shared memory.
-//   * y = bf16(Yi + qdec_i * Yx); R <- gC * R + U in fp32 registers (rows of R are owned
-//     by the 64 threads that hold the M=64 accumulator rows).
-// The decays use a table pw[k] = exp(k * log(gamma)) (constant gamma, the same
-// expression the reference evaluates per element) or the chunk's cumulative log
-// decay c_i (per-step decay).
+//       R  += bf16(phi(K) kdec)^T V          M=64,   N=64, K=C     TMEM cols [192,256)
+//     P_cb = bf16(mask(S) * decay) is written back to shared memory by the threads; the
+//     fp32 state R stays in TMEM (scaled by the chunk decay in place before the update).
+//   * Pass B runs two warpgroups: both cover all TMEM lanes (rows) and split the columns
+//     of each S block and of the epilogue (warpgroup w takes columns [32w, 32w+32)).
+//   * Epilogue: y = bf16(Yi + qdec_i * Yx), stored; or, with the fused gate epilogue,
+//     combined = bf16(GroupNorm_head(y) * sigmoid(gate)) (hdcmamba/model.py:286-293)
+//     written straight into the concatenated row.
+// Decays: a table pw[k] = exp(k * log(gamma)) (constant gamma: the same expression the
+// reference evaluates per element) or the chunk's cumulative log decay c_i (per-step).
 #include "slot.cuh"
 #include "tc.cuh"
 
@@ -36,18 +39,24 @@ struct SlotTcParams {
   float* state_out;
   float* Rseg;  // [BH][nseg][64*64]
   float* Dseg;  // [BH][nseg]
+  // fused GroupNorm * sigmoid(gate) epilogue (gate == nullptr: plain y)
+  const void* gate;
+  int64_t g_sb, g_st;
+  const void* gn_w;
+  const void* gn_b;
   int L, H, hd, N, nseg, seg_len, y_vec;
 };
-
-constexpr int kThreads = 128;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
+__device__ __forceinline__ float phi_fast(float z) { return z > 0.f ? z + 1.f : fast_exp(z); }
+
 // phi in place on a [rows x 64] swizzled bf16 tile; columns >= hd become `pad`.
+template <int NT>
 __device__ __forceinline__ void prep_tile(uint8_t* tile, int rows, int hd, bool apply_phi, float pad) {
-  for (int idx = threadIdx.x; idx < rows * 8; idx += kThreads) {
+  for (int idx = threadIdx.x; idx < rows * 8; idx += NT) {
     const int row = idx >> 3, pc = idx & 7;
     const int c0 = ((pc ^ (row & 7)) << 3);
     uint4* p = reinterpret_cast<uint4*>(tile + row * 128 + pc * 16);
@@ -55,12 +64,12 @@ __device__ __forceinline__ void prep_tile(uint8_t* tile, int rows, int hd, bool 
     float f[8];
     unpack16<__nv_bfloat16>(*p, f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = (c0 + e < hd) ? (apply_phi ? phi(f[e]) : f[e]) : pad;
+    for (int e = 0; e < 8; ++e) f[e] = (c0 + e < hd) ? (apply_phi ? phi_fast(f[e]) : f[e]) : pad;
     *p = pack16<__nv_bfloat16>(f);
   }
 }
 
-// chunk-local cumulative log decay (per-step mode) by warp 0:
+// chunk-local cumulative log decay (per-step mode) by one warp:
 //   tab[i] = c_i = sum_{t=1..i} log_a[c0+t], tab[C] = c_{C-1} + log_a[c0] (chunk decay exponent)
 template <int CT>
 __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float* tab) {
@@ -91,9 +100,10 @@ __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float*
 // Pass A: per-segment local state Rseg = sum_m (prod_{m'>m} gC_m') U_m and Dseg = prod gC_m
 // ---------------------------------------------------------------------------------
 template <int CT, bool PERSTEP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(128, 3)
     slot_tc_state_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
                          SlotTcParams p) {
+  constexpr int NT = 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sK = base;
@@ -119,17 +129,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_map(&mapK);
     tma_prefetch_map(&mapV);
   }
-  float lg = 0.f;
   if (!PERSTEP) {
-    lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
-    for (int k = tid; k <= CT; k += kThreads) sTab[k] = expf((float)k * lg);
+    const float lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
+    for (int k = tid; k <= CT; k += NT) sTab[k] = expf((float)k * lg);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tU = *sTmem;
   const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const uint32_t idU = idesc_bf16_f32(64, 64, true, true);
+  constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
 
   float R[64];
 #pragma unroll
@@ -152,17 +161,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncthreads();
     }
     // k~ = bf16(bf16(phi(k)) * kdec_j) in place; v padding
-    for (int idx = tid; idx < CT * 8; idx += kThreads) {
+    for (int idx = tid; idx < CT * 8; idx += NT) {
       const int row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
-      const float kd = PERSTEP ? expf(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
+      const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
       uint4* pk = reinterpret_cast<uint4*>(sK + row * 128 + pc * 16);
       float f[8];
       unpack16<__nv_bfloat16>(*pk, f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = bf16_round((c0 + e < p.hd) ? bf16_round(phi(f[e])) : 1.f) * kd;
+      for (int e = 0; e < 8; ++e) f[e] = ((c0 + e < p.hd) ? bf16_round(phi_fast(f[e])) : 1.f) * kd;
       *pk = pack16<__nv_bfloat16>(f);
     }
-    if (p.hd < 64) prep_tile(sV, CT, p.hd, false, 0.f);
+    if (p.hd < 64) prep_tile<NT>(sV, CT, p.hd, false, 0.f);
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -178,13 +187,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     mph ^= 1;
     tc_fence_after();
     if (tid == 0 && n + 1 < n1) issue(n + 1);
-    const float gC = PERSTEP ? expf(sTab[CT]) : sTab[CT];
+    const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
     float u[32];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      tmem_ld32(tU + lane_base + half * 32, u);
+    for (int hf = 0; hf < 2; ++hf) {
+      tmem_ld32(tU + lane_base + hf * 32, u);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) R[half * 32 + e] = R[half * 32 + e] * gC + u[e];
+      for (int e = 0; e < 32; ++e) R[hf * 32 + e] = R[hf * 32 + e] * gC + u[e];
     }
     D *= gC;
     tc_fence_before();
@@ -204,12 +213,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------
-// Pass B: outputs
+// Pass B: outputs (256 threads: two warpgroups splitting columns)
 // ---------------------------------------------------------------------------------
-template <int CT, bool PERSTEP>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int CT, bool PERSTEP, bool GATE>
+__global__ void __launch_bounds__(256, 2)
     slot_tc_out_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                        const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
+  constexpr int NT = 256;
   constexpr int RB = CT < 128 ? CT : 128;  // rows per block (MMA M)
   constexpr int NRB = CT / RB;
   constexpr int CB = 64;                   // S column block (MMA N)
@@ -221,68 +231,86 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sP = sQ + RB * 128;
   uint8_t* sR = sP + RB * 128;
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + CT + 4);
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 2);
+  float* sGn = sTab + CT + 4;                              // [128] gn weight | bias of this head
+  float* sRed = sGn + 128;                                 // [RB][4]: sum / sq partials per column half
+  // mbarriers: [0] TMA loads, [1] S products, [2] P.V products, [3] state update.  Each
+  // MMA stream has its own barrier and every commit follows a CTA barrier, so no thread
+  // can fall two phases behind on a barrier (which would alias the parity it waits for).
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + RB * 4);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
   const int bh = blockIdx.x / p.nseg, seg = blockIdx.x - bh * p.nseg;
   const int b = bh / p.H, h = bh - b * p.H;
   const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
-  // row of the M=RB accumulators this thread holds (M=64: lanes 0-15 of each warp)
-  const int my_row = (RB == 128) ? tid : (lane < 16 ? warp * 16 + lane : -1);
-  const bool u_row = lane < 16;             // holds row (warp*16 + lane) of U and R
-  const int f_row = warp * 16 + lane;
+  // row of the M=RB accumulators held by this thread (M=64: lanes 0-15 of each quarter)
+  const int my_row = (RB == 128) ? quarter * 32 + lane : (lane < 16 ? quarter * 16 + lane : -1);
+  const bool f_valid = lane < 16;  // holds row f_row of the M=64 state R
+  const int f_row = quarter * 16 + lane;
+  const int col0 = half * 32;      // this thread's 32 accumulator columns
 
   if (warp == 0) {
     tmem_alloc(sTmem, 256);
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     tma_prefetch_map(&mapQ);
     tma_prefetch_map(&mapK);
     tma_prefetch_map(&mapV);
   }
-  float lg = 0.f;
   if (!PERSTEP) {
-    lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
-    for (int k = tid; k <= CT; k += kThreads) sTab[k] = expf((float)k * lg);
+    const float lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
+    for (int k = tid; k <= CT; k += NT) sTab[k] = expf((float)k * lg);
   }
+  if (GATE) {
+    for (int d = tid; d < 64; d += NT) {
+      const bool in = d < p.hd;
+      sGn[d] = in ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_w)[h * p.hd + d]) : 0.f;
+      sGn[64 + d] = in ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_b)[h * p.hd + d]) : 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+  const uint32_t tS = tmem + lane_base, tYi = tS + 64, tYx = tS + 128, tR = tS + 192;
 
-  // entering state: state_in folded with the earlier segments' local states
-  float R[64];
+  // entering state: state_in folded with the earlier segments' local states -> TMEM + sR
+  {
+    float Rp[32];
 #pragma unroll
-  for (int e = 0; e < 64; ++e) R[e] = 0.f;
-  if (u_row) {
-    if (p.state_in) {
-      const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64;
+    for (int e = 0; e < 32; ++e) Rp[e] = 0.f;
+    if (f_valid) {
+      if (p.state_in) {
+        const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + col0;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) R[e] = src[e];
+        for (int e = 0; e < 32; ++e) Rp[e] = src[e];
+      }
+      for (int s = 0; s < seg; ++s) {
+        const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+        const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + col0;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) Rp[e] = Ds * Rp[e] + src[e];
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, half * 4 + c)) = pack16<__nv_bfloat16>(&Rp[c * 8]);
     }
-    for (int s = 0; s < seg; ++s) {
-      const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
-      const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64;
-#pragma unroll
-      for (int e = 0; e < 64; ++e) R[e] = Ds * R[e] + src[e];
-    }
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, c)) = pack16<__nv_bfloat16>(&R[c * 8]);
+    tmem_st32(tR + col0, Rp);
   }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *sTmem;
-  const uint32_t tS = tmem, tYi = tmem + 64, tYx = tmem + 128, tU = tmem + 192;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
   constexpr uint32_t idS = idesc_bf16_f32(RB, CB, false, false);
   constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
   constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
 
-  uint32_t tph = 0, mph = 0;
+  uint32_t tph = 0, sph = 0, pph = 0, uph = 0;
   bool ok = true;
   auto issue = [&](int n) {
     mbar_expect_tx(&bars[0], 2 * CT * 128 + RB * 128);
@@ -297,8 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tph ^= 1;
     if (PERSTEP && warp == 0)
       chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
-    prep_tile(sK, CT, p.hd, true, 1.f);
-    if (p.hd < 64) prep_tile(sV, CT, p.hd, false, 0.f);
+    prep_tile<NT>(sK, CT, p.hd, true, 1.f);
+    if (p.hd < 64) prep_tile<NT>(sV, CT, p.hd, false, 0.f);
 
     for (int rb = 0; rb < NRB && ok; ++rb) {
       const int r0 = rb * RB;
@@ -310,45 +338,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&bars[0], tph, 22)) { ok = false; break; }
         tph ^= 1;
       }
-      prep_tile(sQ, RB, p.hd, true, 1.f);
+      prep_tile<NT>(sQ, RB, p.hd, true, 1.f);
+      // gate values of this thread's row and columns, loaded early (fused epilogue)
+      const int i_row = r0 + (my_row >= 0 ? my_row : 0);
+      const int t_row = n * CT + i_row;
+      uint4 graw[4];
+      if (GATE) {
+        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) + (size_t)b * p.g_sb +
+                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + col0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          graw[c] = (my_row >= 0 && col0 + c * 8 < p.hd) ? ldg16(gp + c * 8) : make_uint4(0, 0, 0, 0);
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
       if (tid == 0) {
-        // Yx = phi(Q) bf16(R)   (A K-major, B = R rows f with e contiguous: MN-major)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_bf16(tYx, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024),
-                    idPV, k > 0 ? 1u : 0u);
+          umma_bf16(tmem + 128, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024),
+                    sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV, k > 0 ? 1u : 0u);
       }
       const int ncb = (r0 + RB) / CB;
       for (int cb = 0; cb < ncb; ++cb) {
         if (tid == 0) {
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_bf16(tS, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024),
+            umma_bf16(tmem, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024),
                       sdesc_sw128(smem_u32(sK) + cb * CB * 128 + k * 32, 16, 1024), idS, k > 0 ? 1u : 0u);
           umma_commit(&bars[1]);
         }
-        if (!mbar_wait(&bars[1], mph, 23)) { ok = false; break; }
-        mph ^= 1;
+        if (!mbar_wait(&bars[1], sph, 23)) { ok = false; break; }
+        sph ^= 1;
         tc_fence_after();
-        // P = bf16(mask(S) * decay) -> sP (K-major, one 64-column swizzle atom)
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
+        // P = bf16(mask(S) * decay) for this thread's row and 32 columns -> sP
+        {
           float s[32];
-          tmem_ld32(tS + lane_base + half * 32, s);
+          tmem_ld32(tS + col0, s);
           if (my_row >= 0) {
             const int i = r0 + my_row;
+            const float ci = PERSTEP ? sTab[i] : 0.f;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               float v[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
-                const int j = cb * CB + half * 32 + q * 8 + e;
+                const int j = cb * CB + col0 + q * 8 + e;
                 float dm = 0.f;
-                if (j <= i) dm = PERSTEP ? expf(sTab[i] - sTab[j]) : sTab[i - j];
+                if (j <= i) dm = PERSTEP ? fast_exp(ci - sTab[j]) : sTab[i - j];
                 v[e] = (j <= i) ? s[q * 8 + e] * dm : 0.f;
               }
               *reinterpret_cast<uint4*>(sP + sw128_chunk(my_row, half * 4 + q)) = pack16<__nv_bfloat16>(v);
@@ -362,43 +400,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tid == 0) {
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_bf16(tYi, sdesc_sw128(smem_u32(sP) + k * 32, 16, 1024),
+            umma_bf16(tmem + 64, sdesc_sw128(smem_u32(sP) + k * 32, 16, 1024),
                       sdesc_sw128(smem_u32(sV) + (cb * CB + k * 16) * 128, 0, 1024), idPV,
                       (cb > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&bars[1]);
+          umma_commit(&bars[2]);
         }
-        if (!mbar_wait(&bars[1], mph, 24)) { ok = false; break; }
-        mph ^= 1;
+        if (!mbar_wait(&bars[2], pph, 24)) { ok = false; break; }
+        pph ^= 1;
         tc_fence_after();
       }
       if (!ok) break;
-      // epilogue: y = bf16(Yi + qdec_i * Yx)
+      // epilogue
       {
         float yi[32], yx[32];
-        const int i = r0 + (my_row >= 0 ? my_row : 0);
-        const float qd = PERSTEP ? expf(sTab[i]) : sTab[i];
-        const int t = n * CT + i;
-        __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
-                              (size_t)t * p.y_st;
+        tmem_ld32(tYi + col0, yi);
+        tmem_ld32(tYx + col0, yx);
+        const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
+        float o[32];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld32(tYi + lane_base + half * 32, yi);
-          tmem_ld32(tYx + lane_base + half * 32, yx);
+        for (int e = 0; e < 32; ++e) o[e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is stored in bf16
+        if (GATE) {
+          // GroupNorm over the head: hd values split between the two column halves
+          float s = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s += (col0 + e < p.hd) ? o[e] : 0.f;
+          if (my_row >= 0) sRed[my_row * 4 + half] = s;
+          __syncthreads();
+          const float mean = my_row >= 0 ? (sRed[my_row * 4] + sRed[my_row * 4 + 1]) / (float)p.hd : 0.f;
+          float q2 = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float d = o[e] - mean;
+            q2 += (col0 + e < p.hd) ? d * d : 0.f;
+          }
+          if (my_row >= 0) sRed[my_row * 4 + 2 + half] = q2;
+          __syncthreads();
           if (my_row >= 0) {
-            float o[32];
+            const float bdpad = (float)(64 - p.hd);  // the reference's padded lanes (block width 64)
+            const float var = (sRed[my_row * 4 + 2] + sRed[my_row * 4 + 3] + bdpad * mean * mean) / (float)p.hd;
+            const float den = sqrtf(var + 1e-5f);
+            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                                (size_t)t_row * p.y_st + col0;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = yi[e] + qd * yx[e];
-            if (p.y_vec) {
+            for (int c = 0; c < 4; ++c) {
+              if (col0 + c * 8 >= p.hd) continue;
+              float g[8], r[8];
+              unpack16<__nv_bfloat16>(graw[c], g);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int d0 = half * 32 + q * 8;
-                if (d0 < p.hd) stg16(yrow + d0, pack16<__nv_bfloat16>(&o[q * 8]));
+              for (int e = 0; e < 8; ++e) {
+                const int d = col0 + c * 8 + e;
+                const float ygn = ((o[c * 8 + e] - mean) / den) * sGn[d] + sGn[64 + d];
+                r[e] = ygn * (1.0f / (1.0f + fast_exp(-g[e])));
               }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (half * 32 + e < p.hd) yrow[half * 32 + e] = __float2bfloat16_rn(o[e]);
+              stg16(op + c * 8, pack16<__nv_bfloat16>(r));
             }
+          }
+        } else if (my_row >= 0) {
+          __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                                (size_t)t_row * p.y_st + col0;
+          if (p.y_vec) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              if (col0 + c * 8 < p.hd) stg16(yrow + c * 8, pack16<__nv_bfloat16>(&o[c * 8]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (col0 + e < p.hd) yrow[e] = __float2bfloat16_rn(o[e]);
           }
         }
       }
@@ -407,16 +474,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
     }
     if (!ok) break;
-    // state update: k~ = bf16(phi(k) * kdec_j) in place, U = k~^T V, R = gC R + U
-    for (int idx = tid; idx < CT * 8; idx += kThreads) {
+    // state update: k~ = bf16(phi(k) * kdec_j) in place; R <- gC * R (in TMEM); R += k~^T V
+    for (int idx = tid; idx < CT * 8; idx += NT) {
       const int row = idx >> 3, pc = idx & 7;
-      const float kd = PERSTEP ? expf(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
+      const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
       uint4* pk = reinterpret_cast<uint4*>(sK + row * 128 + pc * 16);
       float f[8];
       unpack16<__nv_bfloat16>(*pk, f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] *= kd;
       *pk = pack16<__nv_bfloat16>(f);
+    }
+    {
+      const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
+      float r[32];
+      tmem_ld32(tR + col0, r);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) r[e] *= gC;
+      tmem_st32(tR + col0, r);
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -425,36 +500,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < CT / 16; ++kk)
-        umma_bf16(tU, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024), sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024),
-                  idU, kk > 0 ? 1u : 0u);
-      umma_commit(&bars[1]);
+        umma_bf16(tmem + 192, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
+                  sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, 1u);
+      umma_commit(&bars[3]);
     }
-    if (!mbar_wait(&bars[1], mph, 25)) { ok = false; break; }
-    mph ^= 1;
+    if (!mbar_wait(&bars[3], uph, 25)) { ok = false; break; }
+    uph ^= 1;
     tc_fence_after();
     if (tid == 0 && n + 1 < n1) issue(n + 1);
-    const float gC = PERSTEP ? expf(sTab[CT]) : sTab[CT];
+    {
+      float r[32];
+      tmem_ld32(tR + col0, r);
+      if (f_valid) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      float u[32];
-      tmem_ld32(tU + lane_base + half * 32, u);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) R[half * 32 + e] = R[half * 32 + e] * gC + u[e];
-    }
-    if (u_row) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, c)) = pack16<__nv_bfloat16>(&R[c * 8]);
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, half * 4 + c)) = pack16<__nv_bfloat16>(&r[c * 8]);
+      }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
   }
-  if (ok && seg == p.nseg - 1 && p.state_out && u_row) {
-    float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64;
+  if (ok && seg == p.nseg - 1 && p.state_out) {
+    float r[32];
+    tmem_ld32(tR + col0, r);
+    if (f_valid) {
+      float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + col0;
 #pragma unroll
-    for (int e = 0; e < 64; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
+      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -499,7 +574,7 @@ static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, 
 
 static size_t smem_out_bytes(int CT) {
   const int RB = CT < 128 ? CT : 128;
-  return 1024 + 2 * CT * 128 + 2 * RB * 128 + 64 * 128 + (CT + 4) * 4 + 64;
+  return 1024 + 2 * CT * 128 + 2 * RB * 128 + 64 * 128 + (CT + 4 + 128 + RB * 4) * 4 + 64 + 32;
 }
 static size_t smem_state_bytes(int CT) { return 1024 + 2 * CT * 128 + (CT + 4) * 4 + 64; }
 
@@ -529,13 +604,17 @@ bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in
   return true;
 }
 
-template <int CT, bool PS>
-static int run_tc(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s) {
+template <int CT, bool PS, bool GATE>
+static int run_tc(const SlotParams& sp, const SlotGate* gt, int64_t B, int64_t in_sb, int64_t in_st, void* ws,
+                  cudaStream_t s) {
   const int64_t BH = B * sp.H;
   SlotTcParams p{};
   p.gamma = sp.gamma; p.log_a = sp.log_a; p.y = sp.y; p.y_sb = sp.y_sb; p.y_sh = sp.y_sh; p.y_st = sp.y_st;
   p.state_in = sp.state_in; p.state_out = sp.state_out;
   p.L = sp.L; p.H = sp.H; p.hd = sp.hd; p.N = sp.N;
+  if (gt) {
+    p.gate = gt->gate; p.g_sb = gt->g_sb; p.g_st = gt->g_st; p.gn_w = gt->gn_w; p.gn_b = gt->gn_b;
+  }
   plan_segments(BH, sp.N, &p.nseg, &p.seg_len);
   p.Rseg = static_cast<float*>(ws);
   p.Dseg = p.Rseg + (size_t)BH * p.nseg * 4096;
@@ -550,34 +629,36 @@ static int run_tc(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st,
   if (p.nseg > 1) {
     const size_t sm = smem_state_bytes(CT);
     cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * (p.nseg - 1)), kThreads, sm, s>>>(mk, mv, p);
+    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * (p.nseg - 1)), 128, sm, s>>>(mk, mv, p);
     if (int e = launch_status("slot_tc_state_kernel")) return e;
   }
   const size_t sm = smem_out_bytes(CT);
-  cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  slot_tc_out_kernel<CT, PS><<<(unsigned)(BH * p.nseg), kThreads, sm, s>>>(mq, mk, mv, p);
+  cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  slot_tc_out_kernel<CT, PS, GATE><<<(unsigned)(BH * p.nseg), 256, sm, s>>>(mq, mk, mv, p);
   return launch_status("slot_tc_out_kernel");
 }
 
-int slot_tc_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s) {
+template <bool GATE>
+static int slot_tc_dispatch(const SlotParams& p, const SlotGate* gt, int64_t B, int64_t in_sb, int64_t in_st,
+                            void* ws, cudaStream_t s) {
   const bool ps = p.log_a != nullptr;
   switch (p.C) {
-    case 64: return ps ? run_tc<64, true>(p, B, in_sb, in_st, ws, s) : run_tc<64, false>(p, B, in_sb, in_st, ws, s);
-    case 128: return ps ? run_tc<128, true>(p, B, in_sb, in_st, ws, s) : run_tc<128, false>(p, B, in_sb, in_st, ws, s);
-    default: return ps ? run_tc<256, true>(p, B, in_sb, in_st, ws, s) : run_tc<256, false>(p, B, in_sb, in_st, ws, s);
+    case 64:
+      return ps ? run_tc<64, true, GATE>(p, gt, B, in_sb, in_st, ws, s)
+                : run_tc<64, false, GATE>(p, gt, B, in_sb, in_st, ws, s);
+    case 128:
+      return ps ? run_tc<128, true, GATE>(p, gt, B, in_sb, in_st, ws, s)
+                : run_tc<128, false, GATE>(p, gt, B, in_sb, in_st, ws, s);
+    default:
+      return ps ? run_tc<256, true, GATE>(p, gt, B, in_sb, in_st, ws, s)
+                : run_tc<256, false, GATE>(p, gt, B, in_sb, in_st, ws, s);
   }
+}
+
+int slot_tc_fwd(const SlotParams& p, const SlotGate* gt, int64_t B, int64_t in_sb, int64_t in_st, void* ws,
+                cudaStream_t s) {
+  return gt ? slot_tc_dispatch<true>(p, gt, B, in_sb, in_st, ws, s)
+            : slot_tc_dispatch<false>(p, gt, B, in_sb, in_st, ws, s);
 }
 
 }  // namespace hdc
-
-using namespace hdc;
-
-extern "C" int hdc_device_error(int reset) {
-  int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)) != cudaSuccess) return -1;
-  if (reset && v != 0) {
-    const int z = 0;
-    cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
-  }
-  return v;
-}

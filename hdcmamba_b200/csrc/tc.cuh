@@ -11,10 +11,26 @@
 
 namespace hdc {
 
-// device error word: 0 = ok, otherwise a code identifying the failed wait.  One copy
-// per translation unit (no relocatable device code); the tcgen05 kernels and the
-// accessor hdc_device_error live in slot_tc.cu.
+// Device error word: 0 = ok, otherwise the code of a bounded wait that timed out.
+// There is one copy per translation unit (no relocatable device code); each unit
+// registers a reader at load time and hdc_device_error() consults all of them.
 static __device__ int g_dev_error = 0;
+void register_dev_error_reader(int (*reader)(int reset));
+static int read_tu_dev_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v != 0) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_dev_error, &z, sizeof(int));
+  }
+  return v;
+}
+namespace {
+struct DevErrorReaderRegistration {
+  DevErrorReaderRegistration() { register_dev_error_reader(&read_tu_dev_error); }
+};
+static DevErrorReaderRegistration g_dev_error_registration;
+}  // namespace
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -123,6 +139,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Store 32 consecutive 32-bit columns of the warp's 32 lanes (thread t -> lane t), then wait.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+      "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+      "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// exp(x) through the SFU: ex2.approx(x * log2(e)) (relative error ~2^-22, far below the
+// bf16 rounding that follows every use here).
+__device__ __forceinline__ float fast_exp(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
 }
 
 // ---------------------------------------------------------------- UMMA

@@ -122,7 +122,13 @@ class HdcMamba9v3Block(nn.Module):
         q, k, v = projs[..., so:so + dm], projs[..., so + dm:so + 2 * dm], projs[..., so + 2 * dm:so + 3 * dm]
         combined = torch.empty(B, L, ds + dm, device=x.device, dtype=x.dtype)
         P = projs.shape[-1]
-        if self.semantics == "fixed":
+        if self.semantics == "fixed" and ops.slot_gate_supported(q, H, C):
+            # SSM written into combined[..., :ds]; slot scan with GroupNorm * sigmoid(gate)
+            # fused into its epilogue, written into combined[..., ds:]
+            ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
+            ops.slot_scan_gate(q, k, v, H, C, projs[..., so + 3 * dm:], self.group_norm.weight,
+                               self.group_norm.bias, combined[..., ds:], (L * (ds + dm), hd, ds + dm), gamma=gamma)
+        elif self.semantics == "fixed":
             y_ssm = ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
             y_slot = torch.empty(B * H, N, C, hd, device=x.device, dtype=x.dtype)
             ops.slot_scan(q, k, v, H, C, gamma=gamma, y=y_slot, y_strides=(H * L * hd, L * hd, hd))

@@ -178,6 +178,46 @@ def slot_scan(q, k, v, num_heads, chunk, gamma=None, log_a=None, rows=None, y=No
     return (y, state_out) if return_state else y
 
 
+def slot_gate_supported(q, num_heads, chunk):
+    """True when hdc_slot_gate_fwd (tcgen05, fused gate epilogue) accepts these inputs."""
+    B, L, W = q.shape
+    hd = W // num_heads
+    return (q.dtype == torch.bfloat16 and hd <= 64 and hd % 8 == 0 and W >= 64 and chunk in (64, 128, 256)
+            and L % chunk == 0 and q.stride(2) == 1 and q.stride(1) % 8 == 0 and q.data_ptr() % 16 == 0)
+
+
+def slot_scan_gate(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_strides, gamma=None, log_a=None,
+                   state_in=None, return_state=False):
+    """Slot scan with GroupNorm(head) * sigmoid(gate) fused into its epilogue
+    (replaces ``_slot_all_fused`` plus the slot half of ``_fused_gnorm_gate_cat_kernel``,
+    hdcmamba/model.py:236-293).  gate: [B, L, H*hd] view (unit last stride); out:
+    tensor with element strides ``out_strides = (sb, sh, st)``."""
+    _cuda(q, k, v, gamma, log_a, gate, gn_w, gn_b, out, state_in)
+    _same_dtype(q, k, v, gate, out)
+    B, L, W = q.shape
+    H = num_heads
+    hd = W // H
+    if q.stride() != k.stride() or q.stride() != v.stride() or gate.stride(2) != 1:
+        raise ValueError("q, k, v must share strides; gate needs a unit last stride")
+    if (gamma is None) == (log_a is None):
+        raise ValueError("give exactly one of gamma or log_a")
+    if gamma is not None:
+        gamma = gamma.to(q.dtype).contiguous()
+    if log_a is not None:
+        log_a = log_a.float().contiguous()
+    gw = gn_w.to(q.dtype).contiguous()
+    gb = gn_b.to(q.dtype).contiguous()
+    bd = feature_block(hd)
+    state_out = torch.empty(B, H, bd, bd, device=q.device, dtype=torch.float32) if return_state else None
+    if state_in is not None:
+        state_in = state_in.float().contiguous()
+    ws = torch.empty(max(slot_workspace_bytes(B, L, H, hd, chunk), 16), device=q.device, dtype=torch.uint8)
+    _lib.call("hdc_slot_gate_fwd", _code(q), _p(q), _p(k), _p(v), q.stride(0), q.stride(1), _p(gamma), _p(log_a),
+              _p(gate), gate.stride(0), gate.stride(1), _p(gw), _p(gb), _p(out), out_strides[0], out_strides[1],
+              out_strides[2], _p(state_in), _p(state_out), _p(ws), ws.numel(), B, L, H, hd, chunk, _stream(q))
+    return (out, state_out) if return_state else out
+
+
 # ------------------------------------------------------------------ gate / concat / LN
 def gate_cat(y_slot, slot_strides, slot_rows, y_ssm, ssm_strides, gate, gate_strides, gn_w, gn_b, out,
              out_strides, B, L, H, hd, ds):

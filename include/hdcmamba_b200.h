@@ -58,7 +58,8 @@ long long hdc_launch_count(void);
  *               LayerNorm is norm_b (hdcmamba/model.py:47-57).
  *   mean,rstd : NULL, or [B, L] bf16 per-row statistics (hdcmamba/model.py:67-68).
  *   act       : HDC_ACT_NONE (the reference) or HDC_ACT_SILU.
- * D must be a multiple of 8 (bf16) / 4 (fp32), D <= 8192; pointers 16-byte aligned.
+ * D must be a multiple of 8 (bf16) / 4 (fp32), D <= 4096 (bf16) / 2048 (fp32); pointers
+ * 16-byte aligned.
  */
 int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* norm_b,
                     const void* conv_w, const void* conv_b, const void* halo, void* out,
@@ -123,6 +124,26 @@ int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, in
                       int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
                       void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
                       int64_t hd, int64_t C, int64_t rows, hdc_stream_t stream);
+
+/*
+ * Slot memory scan with the GroupNorm * sigmoid(gate) epilogue fused in: writes
+ *   out(b,t,h,:) = bf16( GroupNorm_h(y(b,t,h,:)) * sigmoid(gate(b,t,h,:)) )
+ * with y the hdc_slot_scan_fwd output (rounded to bf16 first, as the reference stores
+ * y_slot) and the GroupNorm of the reference gate kernel (eps 1e-5, the padded-lane
+ * variance term for head_dim < 64).  Together replaces _slot_all_fused and the slot half
+ * of _fused_gnorm_gate_cat_kernel (hdcmamba/model.py:236-293) for the corrected launch
+ * strides; for the Block, out = combined + d_state with out_sh = head_dim.
+ *   gate element (b,t,h,d) at gate + b*gate_sb + t*gate_st + h*hd + d;
+ *   out  element (b,t,h,d) at out + b*out_sb + h*out_sh + t*out_st + d.
+ * bf16 only, tcgen05 path only (head_dim <= 64 and a multiple of 8, chunk 64/128/256);
+ * other shapes return HDC_E_SHAPE.
+ */
+int hdc_slot_gate_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                      int64_t in_st, const void* gamma, const float* log_a, const void* gate,
+                      int64_t gate_sb, int64_t gate_st, const void* gn_w, const void* gn_b, void* out,
+                      int64_t out_sb, int64_t out_sh, int64_t out_st, const float* state_in,
+                      float* state_out, void* workspace, size_t workspace_bytes, int64_t B, int64_t L,
+                      int64_t H, int64_t hd, int64_t C, hdc_stream_t stream);
 
 /*
  * Slot-scan path control (tests / cross-checks): mode 0 = automatic (tcgen05 for bf16

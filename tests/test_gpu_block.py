@@ -6,7 +6,7 @@ import torch
 
 import golden
 import oracle as O
-from hdcmamba_b200 import FusedNormConv1dFunction, HdcMamba9v3Block, HdcMamba9v3Model
+from hdcmamba_b200 import FusedNormConv1dFunction, HdcMamba9v3Block, HdcMamba9v3Model, _lib
 from hdcmamba_b200.lm import CONFIGS, HdcMambaLM, build_lm, reinit_, synthetic_ids
 
 pytestmark = pytest.mark.gpu
@@ -58,6 +58,8 @@ def test_block_fixed_bf16_vs_oracle(B, L, dm, H, ds, C):
     x = torch.randn(B, L, dm).bfloat16()
     with torch.no_grad():
         y, _ = blk(x.to(DEV))
+    torch.cuda.synchronize()
+    assert _lib.load().hdc_device_error(1) == 0
     ref = O.block_forward({k: v.bfloat16() for k, v in sd.items()}, x, ds, H, C, mode="fixed")
     ref32 = O.block_forward({k: v.float() for k, v in sd.items()}, x.float(), ds, H, C, mode="fixed")
     assert rel(y, ref) < BF16_TOL
@@ -142,3 +144,18 @@ def test_fused_norm_conv_function_backward():
     ref.backward(go)
     for a, b in zip([x, nw, nb, cw, cb], [xs, *ps]):
         torch.testing.assert_close(a.grad, b.grad, rtol=1e-4, atol=1e-4)
+
+
+def test_repeated_forward_has_no_device_timeouts():
+    """Many back-to-back bf16 forwards (the bench's pattern): every bounded device wait
+    must complete, and repeated calls must agree exactly."""
+    torch.manual_seed(4)
+    blk = HdcMamba9v3Block(d_model=768, d_state=64, num_heads=12, chunk_size=256).to(DEV).bfloat16().eval()
+    x = torch.randn(1, 8192, 768, device=DEV).bfloat16()
+    with torch.no_grad():
+        y0, _ = blk(x)
+        for _ in range(20):
+            y, _ = blk(x)
+    torch.cuda.synchronize()
+    assert _lib.load().hdc_device_error(1) == 0
+    assert torch.equal(y, y0)

@@ -143,3 +143,29 @@ def test_tc_large_config3_shape_properties():
     yr, _ = O.slot_scan_decay_fwd(q[:, :n].cpu().reshape(B, n, H, hd), k[:, :n].cpu().reshape(B, n, H, hd),
                                   v[:, :n].cpu().reshape(B, n, H, hd), log_a[:, :n].cpu(), C)
     assert rel(y[:, :n], yr) < BF16_TOL
+
+
+@pytest.mark.parametrize("B,L,ds,dm,H,C", [(2, 1024, 64, 256, 4, 256), (1, 512, 64, 128, 4, 64),
+                                           (2, 512, 16, 384, 6, 128)])
+def test_fused_gate_epilogue_vs_oracle(B, L, ds, dm, H, C):
+    """slot scan + GroupNorm * sigmoid(gate) fused (hdc_slot_gate_fwd) against the oracle's
+    slot_fwd followed by gnorm_gate_cat with the corrected launch strides."""
+    hd = dm // H
+    P = 3 * ds + 4 * dm
+    g = torch.Generator().manual_seed(51 + C)
+    projs = (0.6 * torch.randn(B, L, P, generator=g)).bfloat16()
+    gamma = torch.exp(-torch.nn.functional.softplus(torch.randn(H, generator=g) - 3.0)).bfloat16()
+    gw = (1 + 0.2 * torch.randn(dm, generator=g)).bfloat16()
+    gb = (0.2 * torch.randn(dm, generator=g)).bfloat16()
+    pj = projs.to(DEV)
+    so = 3 * ds
+    comb = torch.zeros(B, L, ds + dm, device=DEV, dtype=torch.bfloat16)
+    ops.slot_scan_gate(pj[..., so:so + dm], pj[..., so + dm:so + 2 * dm], pj[..., so + 2 * dm:so + 3 * dm], H, C,
+                       pj[..., so + 3 * dm:], gw.to(DEV), gb.to(DEV), comb[..., ds:], (L * (ds + dm), hd, ds + dm),
+                       gamma=gamma.to(DEV))
+    torch.cuda.synchronize()
+    assert no_device_error()
+    y_slot = O.slot_fwd(projs, gamma, dm, H, C, so, block_c=C)
+    ref = O.gnorm_gate_cat(y_slot, torch.zeros(B, L, ds).bfloat16(), projs, gw, gb, ds, H, C, mode="fixed")
+    assert rel(comb[..., ds:], ref[..., ds:]) < BF16_TOL, rel(comb[..., ds:], ref[..., ds:])
+    assert float(comb[..., :ds].abs().max()) == 0.0  # the epilogue writes only its own columns
