@@ -69,6 +69,29 @@ __device__ __forceinline__ void prep_tile(uint8_t* tile, int rows, int hd, bool 
   }
 }
 
+// phi in place on a [ROWS x 64] swizzled bf16 tile (ROWS*8 16-byte chunks split evenly over NT
+// threads); columns >= hd become `pad`.  All loads are issued before any compute.
+template <int NT, int ROWS, bool PHI>
+__device__ __forceinline__ void prep_tile_u(uint8_t* tile, int hd, float pad) {
+  constexpr int IT = ROWS * 8 / NT;
+  static_assert(IT * NT == ROWS * 8, "tile chunks must split evenly");
+  uint4 v[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) v[it] = reinterpret_cast<const uint4*>(tile)[threadIdx.x + it * NT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int idx = threadIdx.x + it * NT;
+    const int row = idx >> 3, pc = idx & 7;
+    const int c0 = ((pc ^ (row & 7)) << 3);
+    if (!PHI && c0 + 8 <= hd) continue;
+    float f[8];
+    unpack16<__nv_bfloat16>(v[it], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = (c0 + e < hd) ? (PHI ? phi_fast(f[e]) : f[e]) : pad;
+    reinterpret_cast<uint4*>(tile)[idx] = pack16<__nv_bfloat16>(f);
+  }
+}
+
 // chunk-local cumulative log decay (per-step mode) by one warp:
 //   tab[i] = c_i = sum_{t=1..i} log_a[c0+t], tab[C] = c_{C-1} + log_a[c0] (chunk decay exponent)
 template <int CT>
@@ -213,45 +236,56 @@ __global__ void __launch_bounds__(128, 3)
 }
 
 // ---------------------------------------------------------------------------------
-// Pass B: outputs (256 threads: two warpgroups splitting columns)
+// Pass B: outputs.  NWG warpgroups (NWG*128 threads); all of them cover every TMEM lane
+// (row) and split the columns: S columns of the current row block, the 64 columns of
+// the Yi / Yx / R accumulators.  Each row block needs one S MMA group (N up to 256) and
+// one P.V MMA group, so a chunk takes 2 * (C / 128) + 1 tensor-core round trips.
 // ---------------------------------------------------------------------------------
+template <int CT>
+struct OutCfg {
+  static constexpr int RB = CT < 128 ? CT : 128;                 // rows per block (MMA M)
+  static constexpr int NWG = CT == 64 ? 2 : 4;                   // warpgroups
+  static constexpr int NT = NWG * 128;
+  static constexpr int TMEM_COLS = CT == 64 ? 256 : 512;         // S (CT) + Yi + Yx + R (64 each)
+  static constexpr int EPW = 64 / NWG;                           // accumulator columns per warpgroup
+  static constexpr int MINB = CT == 64 ? 2 : 1;                  // resident CTAs per SM
+};
+
 template <int CT, bool PERSTEP, bool GATE>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     slot_tc_out_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                        const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
-  constexpr int NT = 256;
-  constexpr int RB = CT < 128 ? CT : 128;  // rows per block (MMA M)
-  constexpr int NRB = CT / RB;
-  constexpr int CB = 64;                   // S column block (MMA N)
+  using Cfg = OutCfg<CT>;
+  constexpr int NT = Cfg::NT, RB = Cfg::RB, NRB = CT / RB, NWG = Cfg::NWG, EPW = Cfg::EPW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sK = base;
   uint8_t* sV = sK + CT * 128;
   uint8_t* sQ = sV + CT * 128;
-  uint8_t* sP = sQ + RB * 128;
-  uint8_t* sR = sP + RB * 128;
+  uint8_t* sP = sQ + CT * 128;              // [CT/64 atoms][RB rows][128 B]
+  uint8_t* sR = sP + CT * RB * 2;           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
   float* sGn = sTab + CT + 4;                              // [128] gn weight | bias of this head
-  float* sRed = sGn + 128;                                 // [RB][4]: sum / sq partials per column half
-  // mbarriers: [0] TMA loads, [1] S products, [2] P.V products, [3] state update.  Each
-  // MMA stream has its own barrier and every commit follows a CTA barrier, so no thread
-  // can fall two phases behind on a barrier (which would alias the parity it waits for).
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + RB * 4);
+  float* sRed = sGn + 128;                                 // [RB][8] GroupNorm partial sums
+  // mbarriers: [0] TMA loads, [1] S (+Yx) products, [2] P.V products, [3] state update.
+  // Each MMA stream has its own barrier and every commit follows a CTA barrier, so no
+  // thread can fall two phases behind on a barrier (which would alias the parity).
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + RB * 8);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
+  const int quarter = warp & 3, wg = warp >> 2;
   const int bh = blockIdx.x / p.nseg, seg = blockIdx.x - bh * p.nseg;
   const int b = bh / p.H, h = bh - b * p.H;
   const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
-  // row of the M=RB accumulators held by this thread (M=64: lanes 0-15 of each quarter)
+  // accumulator row held by this thread (M=64 accumulators: lanes 0-15 of each quarter)
   const int my_row = (RB == 128) ? quarter * 32 + lane : (lane < 16 ? quarter * 16 + lane : -1);
   const bool f_valid = lane < 16;  // holds row f_row of the M=64 state R
   const int f_row = quarter * 16 + lane;
-  const int col0 = half * 32;      // this thread's 32 accumulator columns
+  const int e0 = wg * EPW;         // this thread's accumulator columns [e0, e0 + EPW)
 
   if (warp == 0) {
-    tmem_alloc(sTmem, 256);
+    tmem_alloc(sTmem, Cfg::TMEM_COLS);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -277,43 +311,44 @@ __global__ void __launch_bounds__(256, 2)
   tc_fence_after();
   const uint32_t tmem = *sTmem;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-  const uint32_t tS = tmem + lane_base, tYi = tS + 64, tYx = tS + 128, tR = tS + 192;
+  const uint32_t tS = tmem + lane_base, tYi = tS + CT, tYx = tS + CT + 64, tR = tS + CT + 128;
 
   // entering state: state_in folded with the earlier segments' local states -> TMEM + sR
-  {
-    float Rp[32];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) Rp[e] = 0.f;
+  for (int pc = 0; pc < EPW / 16; ++pc) {
+    float Rp[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) Rp[e] = 0.f;
+    const int c0 = e0 + pc * 16;
     if (f_valid) {
       if (p.state_in) {
-        const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + col0;
+        const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + c0;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) Rp[e] = src[e];
+        for (int e = 0; e < 16; ++e) Rp[e] = src[e];
       }
       for (int s = 0; s < seg; ++s) {
         const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
-        const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + col0;
+        const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + c0;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) Rp[e] = Ds * Rp[e] + src[e];
+        for (int e = 0; e < 16; ++e) Rp[e] = Ds * Rp[e] + src[e];
       }
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, half * 4 + c)) = pack16<__nv_bfloat16>(&Rp[c * 8]);
+      for (int c = 0; c < 2; ++c)
+        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (c0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rp[c * 8]);
     }
-    tmem_st32(tR + col0, Rp);
+    tmem_st16(tR + c0, Rp);
   }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  constexpr uint32_t idS = idesc_bf16_f32(RB, CB, false, false);
   constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
   constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
 
   uint32_t tph = 0, sph = 0, pph = 0, uph = 0;
   bool ok = true;
   auto issue = [&](int n) {
-    mbar_expect_tx(&bars[0], 2 * CT * 128 + RB * 128);
+    mbar_expect_tx(&bars[0], 3 * CT * 128);
     tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
     tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
     tma_load_3d(sQ, &mapQ, h * p.hd, n * CT, b, &bars[0]);
@@ -325,147 +360,154 @@ __global__ void __launch_bounds__(256, 2)
     tph ^= 1;
     if (PERSTEP && warp == 0)
       chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
-    prep_tile<NT>(sK, CT, p.hd, true, 1.f);
-    if (p.hd < 64) prep_tile<NT>(sV, CT, p.hd, false, 0.f);
+    prep_tile_u<NT, CT, true>(sK, p.hd, 1.f);
+    prep_tile_u<NT, CT, true>(sQ, p.hd, 1.f);
+    if (p.hd < 64) prep_tile_u<NT, CT, false>(sV, p.hd, 0.f);
 
-    for (int rb = 0; rb < NRB && ok; ++rb) {
+#pragma unroll
+    for (int rb = 0; rb < NRB; ++rb) {
+      if (!ok) break;
       const int r0 = rb * RB;
-      if (rb > 0) {
-        if (tid == 0) {
-          mbar_expect_tx(&bars[0], RB * 128);
-          tma_load_3d(sQ, &mapQ, h * p.hd, n * CT + r0, b, &bars[0]);
-        }
-        if (!mbar_wait(&bars[0], tph, 22)) { ok = false; break; }
-        tph ^= 1;
-      }
-      prep_tile<NT>(sQ, RB, p.hd, true, 1.f);
-      // gate values of this thread's row and columns, loaded early (fused epilogue)
+      const int nrb = (RB == 128) ? min(CT, r0 + RB) : CT;  // S columns needed by this row block
+      const int cpw = nrb / NWG;                             // S columns per warpgroup (32 or 64)
       const int i_row = r0 + (my_row >= 0 ? my_row : 0);
       const int t_row = n * CT + i_row;
-      uint4 graw[4];
-      if (GATE) {
+      uint4 graw[EPW / 8];
+      if (GATE) {  // gate values of this thread's row and columns, loaded early
         const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) + (size_t)b * p.g_sb +
-                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + col0;
+                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + e0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          graw[c] = (my_row >= 0 && col0 + c * 8 < p.hd) ? ldg16(gp + c * 8) : make_uint4(0, 0, 0, 0);
+        for (int c = 0; c < EPW / 8; ++c)
+          graw[c] = (my_row >= 0 && e0 + c * 8 < p.hd) ? ldg16(gp + c * 8) : make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
       if (tid == 0) {
+        const uint32_t aq = smem_u32(sQ) + r0 * 128;
+        // Yx = phi(Q) bf16(R) (B = R rows f, e contiguous: MN-major)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_bf16(tmem + 128, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024),
-                    sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV, k > 0 ? 1u : 0u);
+          umma_bf16(tmem + CT + 64, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024),
+                    idPV, k > 0 ? 1u : 0u);
+        // S = phi(Q_blk) phi(K[0:nrb])^T
+        const uint32_t idS = idesc_bf16_f32(RB, nrb, false, false);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_bf16(tmem, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sK) + k * 32, 16, 1024), idS,
+                    k > 0 ? 1u : 0u);
+        umma_commit(&bars[1]);
       }
-      const int ncb = (r0 + RB) / CB;
-      for (int cb = 0; cb < ncb; ++cb) {
-        if (tid == 0) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(tmem, sdesc_sw128(smem_u32(sQ) + k * 32, 16, 1024),
-                      sdesc_sw128(smem_u32(sK) + cb * CB * 128 + k * 32, 16, 1024), idS, k > 0 ? 1u : 0u);
-          umma_commit(&bars[1]);
-        }
-        if (!mbar_wait(&bars[1], sph, 23)) { ok = false; break; }
-        sph ^= 1;
-        tc_fence_after();
-        // P = bf16(mask(S) * decay) for this thread's row and 32 columns -> sP
-        {
-          float s[32];
-          tmem_ld32(tS + col0, s);
-          if (my_row >= 0) {
-            const int i = r0 + my_row;
-            const float ci = PERSTEP ? sTab[i] : 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float v[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int j = cb * CB + col0 + q * 8 + e;
-                float dm = 0.f;
-                if (j <= i) dm = PERSTEP ? fast_exp(ci - sTab[j]) : sTab[i - j];
-                v[e] = (j <= i) ? s[q * 8 + e] * dm : 0.f;
-              }
-              *reinterpret_cast<uint4*>(sP + sw128_chunk(my_row, half * 4 + q)) = pack16<__nv_bfloat16>(v);
-            }
-          }
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (tid == 0) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(tmem + 64, sdesc_sw128(smem_u32(sP) + k * 32, 16, 1024),
-                      sdesc_sw128(smem_u32(sV) + (cb * CB + k * 16) * 128, 0, 1024), idPV,
-                      (cb > 0 || k > 0) ? 1u : 0u);
-          umma_commit(&bars[2]);
-        }
-        if (!mbar_wait(&bars[2], pph, 24)) { ok = false; break; }
-        pph ^= 1;
-        tc_fence_after();
-      }
-      if (!ok) break;
-      // epilogue
+      if (!mbar_wait(&bars[1], sph, 23)) { ok = false; break; }
+      sph ^= 1;
+      tc_fence_after();
+      // P = bf16(mask(S) * decay): this warpgroup's cpw columns of every row -> sP
       {
-        float yi[32], yx[32];
-        tmem_ld32(tYi + col0, yi);
-        tmem_ld32(tYx + col0, yx);
-        const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
-        float o[32];
+        float sv[64];
+        const int jb = wg * cpw;
+        if (cpw == 64) tmem_ld32x2(tS + jb, tS + jb + 32, sv, sv + 32);
+        else tmem_ld32(tS + jb, sv);
+        if (my_row >= 0) {
+          const int i = r0 + my_row;
+          const float ci = PERSTEP ? sTab[i] : 0.f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is stored in bf16
-        if (GATE) {
-          // GroupNorm over the head: hd values split between the two column halves
-          float s = 0.f;
+          for (int q = 0; q < 8; ++q) {
+            if (q * 8 >= cpw) break;
+            float v[8];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) s += (col0 + e < p.hd) ? o[e] : 0.f;
-          if (my_row >= 0) sRed[my_row * 4 + half] = s;
-          __syncthreads();
-          const float mean = my_row >= 0 ? (sRed[my_row * 4] + sRed[my_row * 4 + 1]) / (float)p.hd : 0.f;
-          float q2 = 0.f;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float d = o[e] - mean;
-            q2 += (col0 + e < p.hd) ? d * d : 0.f;
+            for (int e = 0; e < 8; ++e) {
+              const int j = jb + q * 8 + e;
+              float dm = 0.f;
+              if (j <= i) dm = PERSTEP ? fast_exp(ci - sTab[j]) : sTab[i - j];
+              v[e] = (j <= i) ? sv[q * 8 + e] * dm : 0.f;
+            }
+            const int j0 = jb + q * 8;
+            *reinterpret_cast<uint4*>(sP + (j0 >> 6) * (RB * 128) + sw128_chunk(my_row, (j0 & 63) >> 3)) =
+                pack16<__nv_bfloat16>(v);
           }
-          if (my_row >= 0) sRed[my_row * 4 + 2 + half] = q2;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      tc_fence_after();
+      if (tid == 0) {
+        for (int kk = 0; kk < nrb / 16; ++kk)
+          umma_bf16(tmem + CT,
+                    sdesc_sw128(smem_u32(sP) + ((kk * 16) >> 6) * (RB * 128) + ((kk * 16) & 63) * 2, 16, 1024),
+                    sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, kk > 0 ? 1u : 0u);
+        umma_commit(&bars[2]);
+      }
+      if (!mbar_wait(&bars[2], pph, 24)) { ok = false; break; }
+      pph ^= 1;
+      tc_fence_after();
+      // epilogue: y = bf16(Yi + qdec_i * Yx), plain or GroupNorm * sigmoid(gate)
+      {
+        float o[EPW];
+#pragma unroll
+        for (int pc = 0; pc < EPW / 16; ++pc) {
+          float yi[16], yx[16];
+          tmem_ld16(tYi + e0 + pc * 16, yi);
+          tmem_ld16(tYx + e0 + pc * 16, yx);
+          const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[pc * 16 + e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is bf16
+        }
+        if (GATE) {
+          float sum = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPW; ++e) sum += (e0 + e < p.hd) ? o[e] : 0.f;
+          if (my_row >= 0) sRed[my_row * 8 + wg] = sum;
+          __syncthreads();
+          float mean = 0.f;
+          if (my_row >= 0) {
+#pragma unroll
+            for (int w = 0; w < NWG; ++w) mean += sRed[my_row * 8 + w];
+            mean *= fast_rcp((float)p.hd);
+          }
+          float sq = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPW; ++e) {
+            const float d = o[e] - mean;
+            sq += (e0 + e < p.hd) ? d * d : 0.f;
+          }
+          if (my_row >= 0) sRed[my_row * 8 + 4 + wg] = sq;
           __syncthreads();
           if (my_row >= 0) {
-            const float bdpad = (float)(64 - p.hd);  // the reference's padded lanes (block width 64)
-            const float var = (sRed[my_row * 4 + 2] + sRed[my_row * 4 + 3] + bdpad * mean * mean) / (float)p.hd;
-            const float den = sqrtf(var + 1e-5f);
-            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
-                                (size_t)t_row * p.y_st + col0;
+            float ssq = 0.f;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              if (col0 + c * 8 >= p.hd) continue;
+            for (int w = 0; w < NWG; ++w) ssq += sRed[my_row * 8 + 4 + w];
+            // the reference's padded lanes (block width 64) add (64 - hd) * mean^2
+            const float var = (ssq + (float)(64 - p.hd) * mean * mean) / (float)p.hd;
+            const float inv = rsqrtf(var + 1e-5f);
+            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                                (size_t)t_row * p.y_st + e0;
+#pragma unroll
+            for (int c = 0; c < EPW / 8; ++c) {
+              if (e0 + c * 8 >= p.hd) continue;
               float g[8], r[8];
               unpack16<__nv_bfloat16>(graw[c], g);
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
-                const int d = col0 + c * 8 + e;
-                const float ygn = ((o[c * 8 + e] - mean) / den) * sGn[d] + sGn[64 + d];
-                r[e] = ygn * (1.0f / (1.0f + fast_exp(-g[e])));
+                const int d = e0 + c * 8 + e;
+                const float ygn = ((o[c * 8 + e] - mean) * inv) * sGn[d] + sGn[64 + d];
+                r[e] = ygn * fast_sigmoid(g[e]);
               }
               stg16(op + c * 8, pack16<__nv_bfloat16>(r));
             }
           }
         } else if (my_row >= 0) {
           __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
-                                (size_t)t_row * p.y_st + col0;
+                                (size_t)t_row * p.y_st + e0;
           if (p.y_vec) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              if (col0 + c * 8 < p.hd) stg16(yrow + c * 8, pack16<__nv_bfloat16>(&o[c * 8]));
+            for (int c = 0; c < EPW / 8; ++c)
+              if (e0 + c * 8 < p.hd) stg16(yrow + c * 8, pack16<__nv_bfloat16>(&o[c * 8]));
           } else {
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (col0 + e < p.hd) yrow[e] = __float2bfloat16_rn(o[e]);
+            for (int e = 0; e < EPW; ++e)
+              if (e0 + e < p.hd) yrow[e] = __float2bfloat16_rn(o[e]);
           }
         }
       }
@@ -474,7 +516,7 @@ __global__ void __launch_bounds__(256, 2)
       tc_fence_after();
     }
     if (!ok) break;
-    // state update: k~ = bf16(phi(k) * kdec_j) in place; R <- gC * R (in TMEM); R += k~^T V
+    // state update: k~ = bf16(phi(k) * kdec_j) in place; R <- gC * R (TMEM); R += k~^T V
     for (int idx = tid; idx < CT * 8; idx += NT) {
       const int row = idx >> 3, pc = idx & 7;
       const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
@@ -487,11 +529,14 @@ __global__ void __launch_bounds__(256, 2)
     }
     {
       const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
-      float r[32];
-      tmem_ld32(tR + col0, r);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) r[e] *= gC;
-      tmem_st32(tR + col0, r);
+      for (int pc = 0; pc < EPW / 16; ++pc) {
+        float r[16];
+        tmem_ld16(tR + e0 + pc * 16, r);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) r[e] *= gC;
+        tmem_st16(tR + e0 + pc * 16, r);
+      }
     }
     fence_proxy_async_smem();
     tc_fence_before();
@@ -500,7 +545,7 @@ __global__ void __launch_bounds__(256, 2)
     if (tid == 0) {
 #pragma unroll
       for (int kk = 0; kk < CT / 16; ++kk)
-        umma_bf16(tmem + 192, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
+        umma_bf16(tmem + CT + 128, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
                   sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, 1u);
       umma_commit(&bars[3]);
     }
@@ -508,13 +553,15 @@ __global__ void __launch_bounds__(256, 2)
     uph ^= 1;
     tc_fence_after();
     if (tid == 0 && n + 1 < n1) issue(n + 1);
-    {
-      float r[32];
-      tmem_ld32(tR + col0, r);
+#pragma unroll
+    for (int pc = 0; pc < EPW / 16; ++pc) {
+      float r[16];
+      tmem_ld16(tR + e0 + pc * 16, r);
       if (f_valid) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, half * 4 + c)) = pack16<__nv_bfloat16>(&r[c * 8]);
+        for (int c = 0; c < 2; ++c)
+          *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, ((e0 + pc * 16) >> 3) + c)) =
+              pack16<__nv_bfloat16>(&r[c * 8]);
       }
     }
     fence_proxy_async_smem();
@@ -523,17 +570,21 @@ __global__ void __launch_bounds__(256, 2)
     tc_fence_after();
   }
   if (ok && seg == p.nseg - 1 && p.state_out) {
-    float r[32];
-    tmem_ld32(tR + col0, r);
-    if (f_valid) {
-      float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + col0;
 #pragma unroll
-      for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+    for (int pc = 0; pc < EPW / 16; ++pc) {
+      float r[16];
+      tmem_ld16(tR + e0 + pc * 16, r);
+      if (f_valid) {
+        float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0 + pc * 16;
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+          *reinterpret_cast<float4*>(dst + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 0) tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
 // ---------------------------------------------------------------------------------
@@ -574,12 +625,13 @@ static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, 
 
 static size_t smem_out_bytes(int CT) {
   const int RB = CT < 128 ? CT : 128;
-  return 1024 + 2 * CT * 128 + 2 * RB * 128 + 64 * 128 + (CT + 4 + 128 + RB * 4) * 4 + 64 + 32;
+  return 1024 + 3 * CT * 128 + CT * RB * 2 + 64 * 128 + (CT + 4 + 128 + RB * 8) * 4 + 64;
 }
 static size_t smem_state_bytes(int CT) { return 1024 + 2 * CT * 128 + (CT + 4) * 4 + 64; }
 
-static void plan_segments(int64_t BH, int N, int* nseg, int* seg_len) {
-  const int slots = num_sms() * 2;
+// One output CTA per SM for chunk 128 / 256 (512 TMEM columns), two for chunk 64.
+static void plan_segments(int64_t BH, int N, int C, int* nseg, int* seg_len) {
+  const int slots = num_sms() * (C == 64 ? 2 : 1);
   int s = (int)(slots / BH);
   if (s < 1) s = 1;
   if (s > N) s = N;
@@ -590,7 +642,7 @@ static void plan_segments(int64_t BH, int N, int* nseg, int* seg_len) {
 
 size_t slot_tc_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C) {
   int nseg, len;
-  plan_segments(B * H, (int)(L / C), &nseg, &len);
+  plan_segments(B * H, (int)(L / C), (int)C, &nseg, &len);
   return (size_t)(B * H) * nseg * (4096 + 1) * sizeof(float) + 256;
 }
 
@@ -615,15 +667,14 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, int64_t B, int64_t i
   if (gt) {
     p.gate = gt->gate; p.g_sb = gt->g_sb; p.g_st = gt->g_st; p.gn_w = gt->gn_w; p.gn_b = gt->gn_b;
   }
-  plan_segments(BH, sp.N, &p.nseg, &p.seg_len);
+  plan_segments(BH, sp.N, sp.C, &p.nseg, &p.seg_len);
   p.Rseg = static_cast<float*>(ws);
   p.Dseg = p.Rseg + (size_t)BH * p.nseg * 4096;
   p.y_vec = (aligned16(sp.y) && sp.y_sb % 8 == 0 && sp.y_sh % 8 == 0 && sp.y_st % 8 == 0 && sp.hd % 8 == 0) ? 1 : 0;
-  constexpr int RB = CT < 128 ? CT : 128;
   const int64_t W = (int64_t)sp.H * sp.hd;
   CUtensorMap mq, mk, mv;
   const int64_t sb = B > 1 ? in_sb : (int64_t)sp.L * in_st;
-  if (int e = make_map(&mq, sp.q, W, sp.L, B, in_st, sb, RB)) return e;
+  if (int e = make_map(&mq, sp.q, W, sp.L, B, in_st, sb, CT)) return e;
   if (int e = make_map(&mk, sp.k, W, sp.L, B, in_st, sb, CT)) return e;
   if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
   if (p.nseg > 1) {
@@ -634,7 +685,7 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, int64_t B, int64_t i
   }
   const size_t sm = smem_out_bytes(CT);
   cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  slot_tc_out_kernel<CT, PS, GATE><<<(unsigned)(BH * p.nseg), 256, sm, s>>>(mq, mk, mv, p);
+  slot_tc_out_kernel<CT, PS, GATE><<<(unsigned)(BH * p.nseg), OutCfg<CT>::NT, sm, s>>>(mq, mk, mv, p);
   return launch_status("slot_tc_out_kernel");
 }
 
