@@ -31,6 +31,9 @@ SIGNATURES = {
     "hdc_ssm_chunk_stats": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_ssm_scan_out": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64,
                                  c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hdc_ssm_scan_fwd_noalloc": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                         c_i64, c_vp]),
+    "hdc_ssm_noalloc_capacity": (c_i64, []),
     "hdc_slot_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64, c_i64]),
     "hdc_slot_scan_fwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,
                                   c_vp, c_vp, c_vp, c_size, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),

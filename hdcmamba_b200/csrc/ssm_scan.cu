@@ -15,6 +15,8 @@
 //   pass 2 (hdc_ssm_scan_out):    exclusive prefix over all earlier chunks (including
 //                                 n_prev chunks of earlier sequence segments),
 //                                 then the outputs, written with caller strides.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace hdc {
@@ -172,4 +174,70 @@ extern "C" int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, i
   if (dtype == HDC_F32) ssm_scan_out_kernel<float><<<grid, p.S * ds, smem, s>>>(p);
   else ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * ds, smem, s>>>(p);
   return launch_status("ssm_scan_out_kernel");
+}
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant of the whole chunked scan (no counterpart in the reference).
+//
+// Some callers cannot allocate device memory for the chunk statistics: a host that hands
+// this library only the tensors it owns (for example an inference server or a plugin
+// behind a foreign-function boundary with its own memory manager), or code that must not
+// call cudaMalloc while the device is in a state where allocation would synchronise or
+// fail.  hdc_ssm_scan_fwd_noalloc keeps the statistics in a fixed device array that the
+// library reserves when it is loaded, so the caller passes only inputs and outputs.
+//
+//  * Capacity: kNoAllocStatsFloats fp32 values = B * (L / C) * 2 * d_state at most (4 MiB);
+//    every GPU that loads the library reserves this array until the process exits.
+//  * The array's device address is looked up once per device (cudaGetSymbolAddress, with
+//    that device current) on the first call there; make that first call before any CUDA
+//    stream capture.
+//  * All calls share the one array.  The statistics kernel rewrites every value the
+//    output kernel reads, so nothing needs clearing between calls, but two calls whose
+//    work overlaps on the GPU (different streams without ordering) race on the array.
+// ---------------------------------------------------------------------------------
+namespace hdc {
+
+constexpr int64_t kNoAllocStatsFloats = int64_t(1) << 20;
+static __device__ __align__(256) float g_noalloc_stats[kNoAllocStatsFloats];
+
+static float* noalloc_stats_ptr(int* err) {
+  static std::mutex mu;
+  static float* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = fail(HDC_E_SHAPE, "ssm_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_stats);
+    if (e != cudaSuccess || ptr == nullptr) {
+      *err = fail((int)e ? (int)e : HDC_E_NULL, "ssm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    cache[dev] = static_cast<float*>(ptr);
+  }
+  return cache[dev];
+}
+
+}  // namespace hdc
+
+extern "C" int64_t hdc_ssm_noalloc_capacity(void) { return hdc::kNoAllocStatsFloats; }
+
+extern "C" int hdc_ssm_scan_fwd_noalloc(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                                        const void* A_log, void* y, int64_t y_sb, int64_t y_st, int64_t B,
+                                        int64_t L, int64_t ds, int64_t C, hdc_stream_t stream) {
+  if (int e = ssm_check(dtype, projs, A_log, B, L, ds, C)) return e;
+  if (!y) return fail(HDC_E_NULL, "ssm_noalloc: null y");
+  const int64_t need = B * (L / C) * 2 * ds;
+  if (need > kNoAllocStatsFloats)
+    return fail(HDC_E_WORKSPACE, "ssm_noalloc: B*(L/C)*2*d_state = %lld exceeds the fixed capacity %lld",
+                (long long)need, (long long)kNoAllocStatsFloats);
+  int err = 0;
+  float* stats = noalloc_stats_ptr(&err);
+  if (!stats) return err;
+  if (int e = hdc_ssm_chunk_stats(dtype, projs, proj_sb, proj_st, A_log, stats, B, L, ds, C, stream)) return e;
+  return hdc_ssm_scan_out(dtype, projs, proj_sb, proj_st, A_log, stats, (L / C) * 2 * ds, 0, y, y_sb, y_st, B, L, ds,
+                          C, stream);
 }

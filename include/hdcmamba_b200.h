@@ -97,6 +97,23 @@ int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj
                      int64_t C, hdc_stream_t stream);
 
 /*
+ * The whole diagonal-SSM chunked scan (hdc_ssm_chunk_stats + hdc_ssm_scan_out, n_prev = 0)
+ * without any device allocation by the caller or the library.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory (a host that only hands the
+ * library the tensors it owns, or code that must not call cudaMalloc at that point):
+ * the chunk statistics live in a fixed device array of hdc_ssm_noalloc_capacity() fp32
+ * values (4 MiB, reserved on every GPU that loads the library until process exit), so
+ * B * (L / C) * 2 * ds must not exceed it (HDC_E_WORKSPACE otherwise).  The first call
+ * on a device looks the array's address up (cudaGetSymbolAddress); make it before any
+ * stream capture.  Calls share the array: every value read is rewritten by the same
+ * call, but calls that overlap on the GPU race.
+ */
+int hdc_ssm_scan_fwd_noalloc(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                             const void* A_log, void* y, int64_t y_sb, int64_t y_st, int64_t B,
+                             int64_t L, int64_t ds, int64_t C, hdc_stream_t stream);
+int64_t hdc_ssm_noalloc_capacity(void);
+
+/*
  * Slot memory: size in bytes of the fp32 workspace hdc_slot_scan_fwd needs.
  */
 size_t hdc_slot_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
