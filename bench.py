@@ -34,8 +34,9 @@ sys.path.insert(0, ROOT)
 MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "prefill tokens/sec at L=32768"
-# DRAM bytes per slot-scan launch from an ncu capture (profiles/slot_scan_c5.md); None until captured
-SLOT_TRAFFIC_BYTES = None
+# DRAM bytes (read + write) of one config-5 slot op (slot_tc_state + slot_tc_out) from an ncu
+# --set full capture of `bench.py --workload c5slot` (profiles/slot_scan_c5.md)
+SLOT_TRAFFIC_BYTES = 97.16e6 + 3.24e6 + 203.58e6 + 36.44e6
 
 
 def peaks():
@@ -238,6 +239,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
+    ap.add_argument("--eager", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--workload", default=None, choices=["c2", "c3", "c5slot"],
                     help="time one kernel workload alone (for profiling) and print its line")
     args = ap.parse_args()
@@ -273,9 +275,24 @@ def main():
     ids = ids_host.to(dev)
     tokens_per_rank = ids.numel()
 
-    def step(inp):
-        with torch.no_grad():
-            return lm(inp)
+    if args.eager:
+        def step():
+            with torch.no_grad():
+                return lm(ids)
+
+        def step_host():
+            with torch.no_grad():
+                return lm(ids_host.to(dev, non_blocking=True))
+    else:
+        from hdcmamba_b200.graph import GraphedForward
+        graphed = GraphedForward(lm, ids)
+        ids = graphed.static_in
+
+        def step():
+            return graphed.replay()
+
+        def step_host():
+            return graphed(ids_host)  # pinned host -> static input (H2D), then replay
 
     # instrument the slot scan (dominant custom kernel) with events on its launch stream
     slot_events = []
@@ -292,12 +309,10 @@ def main():
         return wrapper
 
     for _ in range(args.warmup):
-        step(ids)
+        step()
     torch.cuda.synchronize()
 
     sampler = ClockSampler(dev)
-    for name, fn in originals.items():
-        setattr(ops, name, timed(fn))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -306,18 +321,28 @@ def main():
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
-        step(ids)
+        step()
     t1.record()
     torch.cuda.synchronize()
     launches = _lib.launch_count() - n0
+    if not args.eager:
+        launches = graphed.launches_per_replay * args.steps  # replays issue the captured launches
     clocks = sampler.stop()
     if world > 1:
         dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    # per-launch time of the slot op (the roofline kernel): CUDA events around each call on
+    # its launch stream, over eager forward passes of the same inputs
+    for name, fn in originals.items():
+        setattr(ops, name, timed(fn))
+    with torch.no_grad():
+        for _ in range(2):
+            lm(ids)
+    torch.cuda.synchronize()
     for name, fn in originals.items():
         setattr(ops, name, fn)
-    ms = t0.elapsed_time(t1) / args.steps
     slot_ms = statistics.mean(s.elapsed_time(e) for s, e in slot_events)
-    slot_per_step = len(slot_events) / args.steps
+    slot_per_step = len(slot_events) / 2
 
     # end to end through the public call: pinned host ids -> device, logits[:, -1] -> host
     out_host = torch.empty(cfg.batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
@@ -325,8 +350,7 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        inp = ids_host.to(dev, non_blocking=True)
-        logits = step(inp)
+        logits = step_host()
         out_host.copy_(logits[:, -1], non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -351,6 +375,7 @@ def main():
                                    f"C{cfg.chunk_size}, vocab {cfg.vocab}, B{cfg.batch} L{cfg.seq_len}, full logits",
                        "global_batch": cfg.batch * world, "seq_len": cfg.seq_len,
                        "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "launch": "eager" if args.eager else "cuda_graph",
                        "l2": "working set > L2 (projs 214 MB/layer, weights 153 MB): no explicit flush"},
             "roofline": {"kernel": "slot_scan_gate (slot_tc_state + slot_tc_out)", "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,

@@ -159,3 +159,24 @@ def test_repeated_forward_has_no_device_timeouts():
     torch.cuda.synchronize()
     assert _lib.load().hdc_device_error(1) == 0
     assert torch.equal(y, y0)
+
+
+def test_graphed_forward_matches_eager():
+    """GraphedForward (CUDA-graph capture of the LM forward) equals the eager forward,
+    including after the static input changes."""
+    from hdcmamba_b200.graph import GraphedForward
+    torch.manual_seed(6)
+    lm = reinit_(HdcMambaLM(1000, 256, 2, 64, 4, use_model=True)).eval().to(DEV).bfloat16()
+    ids = torch.randint(0, 1000, (2, 1024), device=DEV)
+    g = GraphedForward(lm, ids)
+    assert g.launches_per_replay > 0
+    with torch.no_grad():
+        eager = lm(ids)
+    assert torch.equal(g.replay(), eager)
+    ids2 = torch.randint(0, 1000, (2, 1024)).pin_memory()
+    out = g(ids2).clone()
+    with torch.no_grad():
+        eager2 = lm(ids2.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager2)
+    assert _lib.load().hdc_device_error(1) == 0
