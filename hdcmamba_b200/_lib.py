@@ -40,6 +40,8 @@ SIGNATURES = {
     "hdc_slot_gate_fwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp,
                                   c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_size, c_i64, c_i64, c_i64, c_i64,
                                   c_i64, c_vp]),
+    "hdc_slot_state_fwd": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_i64,
+                                   c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_slot_set_path": (c_int, [c_int]),
     "hdc_slot_last_path": (c_int, []),
     "hdc_device_error": (c_int, [c_int]),

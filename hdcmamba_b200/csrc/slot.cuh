@@ -31,6 +31,8 @@ size_t slot_simt_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t 
 int slot_simt_fwd(int dtype, SlotParams p, int64_t B, void* ws, cudaStream_t s);
 size_t slot_tc_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);
 bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st);
+int slot_tc_state_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st, void* ws, float* decay_out,
+                      cudaStream_t s);
 int slot_tc_fwd(const SlotParams& p, const SlotGate* gate, int64_t B, int64_t in_sb, int64_t in_st, void* ws,
                 cudaStream_t s);
 

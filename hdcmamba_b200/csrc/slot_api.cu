@@ -76,3 +76,26 @@ extern "C" int hdc_slot_gate_fwd(int dtype, const void* q, const void* k, const 
   SlotGate g{gate, gate_sb, gate_st, gn_w, gn_b};
   return slot_tc_fwd(p, &g, B, in_sb, in_st, workspace, reinterpret_cast<cudaStream_t>(stream));
 }
+
+extern "C" int hdc_slot_state_fwd(int dtype, const void* k, const void* v, int64_t in_sb, int64_t in_st,
+                                  const void* gamma, const float* log_a, float* state_out, float* decay_out,
+                                  void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                                  int64_t hd, int64_t C, hdc_stream_t stream) {
+  if (dtype != HDC_BF16) return fail(HDC_E_DTYPE, "slot_state: bf16 activations only");
+  if (!k || !v || !state_out || !decay_out || !workspace || (!gamma && !log_a))
+    return fail(HDC_E_NULL, "slot_state: null pointer");
+  if (B < 1 || H < 1 || hd < 1 || hd > 64 || C < 1 || L < C || L % C != 0)
+    return fail(HDC_E_SHAPE, "slot_state: B=%lld L=%lld H=%lld hd=%lld C=%lld", (long long)B, (long long)L,
+                (long long)H, (long long)hd, (long long)C);
+  const size_t need = hdc_slot_workspace_bytes(B, L, H, hd, C);
+  if (workspace_bytes < need)
+    return fail(HDC_E_WORKSPACE, "slot_state: workspace %zu < %zu bytes", workspace_bytes, need);
+  SlotParams p{};
+  p.q = k; p.k = k; p.v = v; p.in_sb = in_sb; p.in_st = in_st; p.gamma = gamma; p.log_a = log_a;
+  p.state_out = state_out;
+  p.L = (int)L; p.H = (int)H; p.hd = (int)hd; p.C = (int)C; p.rows = (int)C; p.N = (int)(L / C);
+  p.bd = (int)feature_block(hd);
+  if (!slot_tc_supported(p, B, in_sb, in_st))
+    return fail(HDC_E_SHAPE, "slot_state: needs the tcgen05 path (head_dim %% 8 == 0, chunk 64/128/256)");
+  return slot_tc_state_fwd(p, B, in_sb, in_st, workspace, decay_out, reinterpret_cast<cudaStream_t>(stream));
+}

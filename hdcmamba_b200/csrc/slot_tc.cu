@@ -45,6 +45,7 @@ struct SlotTcParams {
   const void* gn_w;
   const void* gn_b;
   int L, H, hd, N, nseg, seg_len, y_vec;
+  int nseg_a;  // segments computed by pass A (nseg - 1 before pass B; nseg for the state-only call)
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(128, 3)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nseg_a = p.nseg - 1;
+  const int nseg_a = p.nseg_a;
   const int bh = blockIdx.x / nseg_a, seg = blockIdx.x - bh * nseg_a;
   const int b = bh / p.H, h = bh - b * p.H;
   const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
@@ -678,15 +679,74 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, int64_t B, int64_t i
   if (int e = make_map(&mk, sp.k, W, sp.L, B, in_st, sb, CT)) return e;
   if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
   if (p.nseg > 1) {
+    p.nseg_a = p.nseg - 1;
     const size_t sm = smem_state_bytes(CT);
     cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * (p.nseg - 1)), 128, sm, s>>>(mk, mv, p);
+    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), 128, sm, s>>>(mk, mv, p);
     if (int e = launch_status("slot_tc_state_kernel")) return e;
   }
   const size_t sm = smem_out_bytes(CT);
   cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   slot_tc_out_kernel<CT, PS, GATE><<<(unsigned)(BH * p.nseg), OutCfg<CT>::NT, sm, s>>>(mq, mk, mv, p);
   return launch_status("slot_tc_out_kernel");
+}
+
+// Fold the segment states of each (batch, head) into the state after the whole sequence
+// (from zero) and the product of all chunk decays.
+__global__ void __launch_bounds__(256) slot_fold_kernel(SlotTcParams p) {
+  const int bh = blockIdx.x;
+  float R[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) R[e] = 0.f;
+  float D = 1.f;
+  for (int s = 0; s < p.nseg; ++s) {
+    const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+    const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + threadIdx.x * 16;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) R[e] = Ds * R[e] + src[e];
+    D *= Ds;
+  }
+  float* dst = p.state_out + (size_t)bh * 4096 + threadIdx.x * 16;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) dst[e] = R[e];
+  if (threadIdx.x == 0 && p.y) static_cast<float*>(p.y)[bh] = D;
+}
+
+template <int CT, bool PS>
+static int run_tc_state(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, void* ws, float* decay_out,
+                        cudaStream_t s) {
+  const int64_t BH = B * sp.H;
+  SlotTcParams p{};
+  p.gamma = sp.gamma; p.log_a = sp.log_a; p.state_out = sp.state_out; p.y = decay_out;
+  p.L = sp.L; p.H = sp.H; p.hd = sp.hd; p.N = sp.N;
+  plan_segments(BH, sp.N, sp.C, &p.nseg, &p.seg_len);
+  p.nseg_a = p.nseg;
+  p.Rseg = static_cast<float*>(ws);
+  p.Dseg = p.Rseg + (size_t)BH * p.nseg * 4096;
+  const int64_t W = (int64_t)sp.H * sp.hd;
+  CUtensorMap mk, mv;
+  const int64_t sb = B > 1 ? in_sb : (int64_t)sp.L * in_st;
+  if (int e = make_map(&mk, sp.k, W, sp.L, B, in_st, sb, CT)) return e;
+  if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
+  const size_t sm = smem_state_bytes(CT);
+  cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg), 128, sm, s>>>(mk, mv, p);
+  if (int e = launch_status("slot_tc_state_kernel")) return e;
+  slot_fold_kernel<<<(unsigned)BH, 256, 0, s>>>(p);
+  return launch_status("slot_fold_kernel");
+}
+
+int slot_tc_state_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_st, void* ws, float* decay_out,
+                      cudaStream_t s) {
+  const bool ps = p.log_a != nullptr;
+  switch (p.C) {
+    case 64: return ps ? run_tc_state<64, true>(p, B, in_sb, in_st, ws, decay_out, s)
+                       : run_tc_state<64, false>(p, B, in_sb, in_st, ws, decay_out, s);
+    case 128: return ps ? run_tc_state<128, true>(p, B, in_sb, in_st, ws, decay_out, s)
+                        : run_tc_state<128, false>(p, B, in_sb, in_st, ws, decay_out, s);
+    default: return ps ? run_tc_state<256, true>(p, B, in_sb, in_st, ws, decay_out, s)
+                       : run_tc_state<256, false>(p, B, in_sb, in_st, ws, decay_out, s);
+  }
 }
 
 template <bool GATE>

@@ -218,6 +218,28 @@ def slot_scan_gate(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_strides
     return (out, state_out) if return_state else out
 
 
+def slot_state(k, v, num_heads, chunk, gamma=None, log_a=None):
+    """State after the whole sequence from a zero start, fp32 [B, H, 64, 64], and the
+    product of all chunk decays [B, H] (for sequence-parallel carries)."""
+    _cuda(k, v, gamma, log_a)
+    _same_dtype(k, v)
+    B, L, W = k.shape
+    H = num_heads
+    hd = W // H
+    if k.stride() != v.stride() or k.stride(2) != 1:
+        raise ValueError("k, v must share strides with unit last-dim stride")
+    if gamma is not None:
+        gamma = gamma.to(k.dtype).contiguous()
+    if log_a is not None:
+        log_a = log_a.float().contiguous()
+    state = torch.empty(B, H, 64, 64, device=k.device, dtype=torch.float32)
+    decay = torch.empty(B, H, device=k.device, dtype=torch.float32)
+    ws = torch.empty(max(slot_workspace_bytes(B, L, H, hd, chunk), 16), device=k.device, dtype=torch.uint8)
+    _lib.call("hdc_slot_state_fwd", _code(k), _p(k), _p(v), k.stride(0), k.stride(1), _p(gamma), _p(log_a),
+              _p(state), _p(decay), _p(ws), ws.numel(), B, L, H, hd, chunk, _stream(k))
+    return state, decay
+
+
 # ------------------------------------------------------------------ gate / concat / LN
 def gate_cat(y_slot, slot_strides, slot_rows, y_ssm, ssm_strides, gate, gate_strides, gn_w, gn_b, out,
              out_strides, B, L, H, hd, ds):

@@ -1,0 +1,116 @@
+"""Sequence parallelism for long prefill: one process per GPU.
+
+Rank r of W holds the contiguous positions [r*L/W, (r+1)*L/W) of every sequence, so each
+rank runs the whole layer on its own segment.  The layer has two cross-segment
+dependencies, and each is exchanged once per layer with ``all_gather`` (NCCL over NVLink):
+
+1. Halo.  The causal conv of LN+conv reads the three rows before the segment, i.e. the
+   last three input rows of rank r-1 (rank 0 sees the reference's zero rows).
+2. Carries, gathered in one call:
+   * SSM: every chunk's statistics (bf16-rounded last state and summed log decay).  Each
+     rank then folds the same chunks in the same order as one GPU would, so its SSM prefix
+     is bit-identical to the single-GPU one (``hdc_ssm_scan_out`` with ``n_prev``).
+   * Slot memory: each rank's local state (fp32 64x64 per head, from a zero start) and the
+     product of its chunk decays.  Rank r folds those of ranks < r into its entering
+     state, R_in(r) = D_{r-1} R_in(r-1) + A_{r-1}; this is the associativity of the
+     per-chunk recurrence R <- gamma^C R + U (hdcmamba/model.py:272).
+
+The kernels are those of the single-GPU Block (fixed semantics).  Only batch-independent
+work crosses ranks, so batch sharding (config 4) needs no collective at all and uses the
+plain module on each rank.
+"""
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import ops
+
+
+class CudaKernels:
+    """The per-rank layer kernels (libhdcmamba_b200)."""
+
+    ln_conv = staticmethod(ops.ln_conv)
+    ssm_chunk_stats = staticmethod(ops.ssm_chunk_stats)
+    ssm_scan_out = staticmethod(ops.ssm_scan_out)
+    slot_state = staticmethod(ops.slot_state)
+    slot_scan_gate = staticmethod(ops.slot_scan_gate)
+    row_layernorm = staticmethod(ops.row_layernorm)
+
+
+def _all_gather(t, group):
+    """[W, *t.shape] stack of every rank's t (flat buffers, as every backend accepts)."""
+    world = dist.get_world_size(group)
+    flat = t.contiguous().reshape(-1)
+    out = torch.empty(world * flat.numel(), device=t.device, dtype=t.dtype)
+    dist.all_gather_into_tensor(out, flat, group=group)
+    return out.reshape((world,) + tuple(t.shape))
+
+
+class SequenceParallel:
+    """Runs HdcMamba blocks / LMs on this rank's segment of the sequence."""
+
+    def __init__(self, group=None, kernels=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.k = kernels if kernels is not None else CudaKernels()
+
+    def block(self, blk, h):
+        """One HdcMamba9v3Block on the local segment h [B, Ls, dm] (Ls a multiple of the
+        chunk size; fixed semantics).  Returns the block output for the segment."""
+        if blk.semantics != "fixed":
+            raise ValueError("sequence parallelism needs semantics='fixed'")
+        K = self.k
+        B, Ls, dm = h.shape
+        C, H, hd, ds = blk.chunk_size, blk.num_heads, blk.head_dim, blk.d_state
+        if Ls % C != 0:
+            raise ValueError(f"segment length {Ls} is not a multiple of the chunk size {C}")
+        N = Ls // C
+        h = h.contiguous()
+        # (1) halo: last three input rows of every rank; rank r uses rank r-1's
+        last3 = _all_gather(h[:, -3:, :], self.group)
+        halo = last3[self.rank - 1] if self.rank > 0 else None
+        x_conv = K.ln_conv(h, blk.norm.weight, blk.norm.bias, blk.conv1d.weight.squeeze(1), blk.conv1d.bias,
+                           blk.norm.eps, halo=halo)
+        projs = F.linear(x_conv, blk.in_proj.weight, blk.in_proj.bias)
+        so = 3 * ds
+        q, k, v = projs[..., so:so + dm], projs[..., so + dm:so + 2 * dm], projs[..., so + 2 * dm:so + 3 * dm]
+        gate = projs[..., so + 3 * dm:]
+        gamma = blk.gamma_buf.to(h.dtype)
+        # (2) carries: SSM chunk statistics, slot local state and decay product
+        stats = K.ssm_chunk_stats(projs, blk.A_log, ds, C)                  # [B, N, 2ds]
+        state, decay = K.slot_state(k, v, H, C, gamma=gamma)                # [B, H, 64, 64], [B, H]
+        flat = torch.cat([stats.reshape(-1), state.reshape(-1), decay.reshape(-1)])
+        g = _all_gather(flat, self.group)                                   # [W, n]
+        n_st, n_sl = stats.numel(), state.numel()
+        stats_all = g[:, :n_st].reshape(self.world, B, N, 2 * ds).permute(1, 0, 2, 3).reshape(B, self.world * N, 2 * ds)
+        states = g[:, n_st:n_st + n_sl].reshape(self.world, B, H, 64, 64)
+        decays = g[:, n_st + n_sl:].reshape(self.world, B, H)
+        R_in = torch.zeros_like(state)
+        for s in range(self.rank):
+            R_in = decays[s][..., None, None] * R_in + states[s]
+        combined = torch.empty(B, Ls, ds + dm, device=h.device, dtype=h.dtype)
+        K.ssm_scan_out(projs, blk.A_log, stats_all[:, :(self.rank + 1) * N].contiguous(), self.rank * N, ds, C,
+                       out=combined[..., :ds])
+        K.slot_scan_gate(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias, combined[..., ds:],
+                         (Ls * (ds + dm), hd, ds + dm), gamma=gamma, state_in=R_in)
+        combined = K.row_layernorm(combined, 1e-5, out=combined)
+        return torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
+
+    def model(self, model, h):
+        """HdcMamba9v3Model.forward on the local segment (hdcmamba/model.py:402-404)."""
+        for blk in model.layers:
+            h = self.block(blk, h)
+        return model.norm_final(h)
+
+    def lm(self, lm, ids_local):
+        """HdcMambaLM.forward (embedding -> backbone -> LayerNorm -> tied head) on the local
+        segment of token ids [B, Ls]; returns the segment's logits [B, Ls, vocab]."""
+        with torch.no_grad():
+            h = lm.embedding(ids_local)
+            if lm.use_model:
+                h = self.model(lm.backbone, h)
+            else:
+                for blk in lm.layers:
+                    h = self.block(blk, h)
+            return F.linear(lm.norm(h), lm.embedding.weight)

@@ -163,6 +163,18 @@ int hdc_slot_gate_fwd(int dtype, const void* q, const void* k, const void* v, in
                       int64_t H, int64_t hd, int64_t C, hdc_stream_t stream);
 
 /*
+ * Slot memory state only: the fp32 state after the whole sequence, started from zero
+ * (state_out [B*H, 64, 64]), and the product of all chunk decays (decay_out [B*H]), with
+ * no outputs.  The sequence-parallel runner exchanges these per rank and folds them into
+ * the next rank's state_in (hdc_slot_scan_fwd / hdc_slot_gate_fwd).  Same chunk recurrence
+ * as _slot_all_fused's `running` (hdcmamba/model.py:252, 271-272).  bf16, tcgen05 path only.
+ */
+int hdc_slot_state_fwd(int dtype, const void* k, const void* v, int64_t in_sb, int64_t in_st,
+                       const void* gamma, const float* log_a, float* state_out, float* decay_out,
+                       void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                       int64_t hd, int64_t C, hdc_stream_t stream);
+
+/*
  * Slot-scan path control (tests / cross-checks): mode 0 = automatic (tcgen05 for bf16
  * with feature width 64, chunk 64/128/256, 8-aligned head_dim and row-contiguous
  * inputs; CUDA cores otherwise), 1 = always the CUDA-core kernel, 2 = require
