@@ -311,15 +311,17 @@ def main():
 
     # instrument the slot scan (dominant custom kernel) with events on its launch stream
     slot_events = []
-    originals = {name: getattr(ops, name) for name in ("slot_scan", "slot_scan_gate")}
+    # (sequence parallel: slot_state + slot_scan_gate_carry make up one layer's slot op)
+    originals = {name: getattr(ops, name) for name in ("slot_scan", "slot_scan_gate", "slot_state",
+                                                      "slot_scan_gate_carry")}
 
-    def timed(fn):
+    def timed(fn, name):
         def wrapper(*a, **k):
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             r = fn(*a, **k)
             e.record()
-            slot_events.append((s, e))
+            slot_events.append((name, s, e))
             return r
         return wrapper
 
@@ -349,15 +351,16 @@ def main():
     # per-launch time of the slot op (the roofline kernel): CUDA events around each call on
     # its launch stream, over eager forward passes of the same inputs
     for name, fn in originals.items():
-        setattr(ops, name, timed(fn))
+        setattr(ops, name, timed(fn, name))
     with torch.no_grad():
         for _ in range(2):
             forward(ids)
     torch.cuda.synchronize()
     for name, fn in originals.items():
         setattr(ops, name, fn)
-    slot_ms = statistics.mean(s.elapsed_time(e) for s, e in slot_events)
-    slot_per_step = len(slot_events) / 2
+    n_ops = sum(1 for name, _, _ in slot_events if name != "slot_state")
+    slot_ms = sum(s.elapsed_time(e) for _, s, e in slot_events) / n_ops
+    slot_per_step = n_ops / 2
 
     # end to end through the public call: pinned host ids -> device, logits[:, -1] -> host
     out_host = torch.empty(cfg.batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
@@ -392,7 +395,8 @@ def main():
                        "parallelism": f"sp{world} (sequence-parallel segments, NCCL carries)" if world > 1 else "single",
                        "launch": "eager" if args.eager else "cuda_graph",
                        "l2": "working set > L2 (projs 214 MB/layer, weights 153 MB): no explicit flush"},
-            "roofline": {"kernel": "slot_scan_gate (slot_tc_state + slot_tc_out)", "bound": "hbm", "achieved": achieved, "peak": hbm,
+            "roofline": {"kernel": ("slot_state + slot_scan_gate_carry (slot_tc_state + slot_fold + slot_tc_out)"
+                                    if world > 1 else "slot_scan_gate (slot_tc_state + slot_tc_out)"), "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
                          "traffic": SLOT_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": slot_bytes,
                          "ms_per_launch": slot_ms, "launches_per_step": slot_per_step},

@@ -31,6 +31,8 @@ SIGNATURES = {
     "hdc_ssm_chunk_stats": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_ssm_scan_out": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64,
                                  c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hdc_ssm_scan_out_blocked": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp,
+                                         c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_ssm_scan_fwd_noalloc": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
                                          c_i64, c_vp]),
     "hdc_ssm_noalloc_capacity": (c_i64, []),
@@ -42,6 +44,9 @@ SIGNATURES = {
                                   c_i64, c_vp]),
     "hdc_slot_state_fwd": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_size, c_i64,
                                    c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hdc_slot_gate_carry_fwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp,
+                                        c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_size,
+                                        c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_slot_set_path": (c_int, [c_int]),
     "hdc_slot_last_path": (c_int, []),
     "hdc_device_error": (c_int, [c_int]),

@@ -46,6 +46,12 @@ struct SlotTcParams {
   const void* gn_b;
   int L, H, hd, N, nseg, seg_len, y_vec;
   int nseg_a;  // segments computed by pass A (nseg - 1 before pass B; nseg for the state-only call)
+  // states of earlier sequence parts (other ranks), folded first: part s has its state at
+  // prev_R + s*prev_stride + bh*4096 and its decay product at prev_D + s*prev_stride + bh
+  const float* prev_R;
+  const float* prev_D;
+  int64_t prev_stride;
+  int nprev;
 };
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -326,6 +332,12 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + c0;
 #pragma unroll
         for (int e = 0; e < 16; ++e) Rp[e] = src[e];
+      }
+      for (int s = 0; s < p.nprev; ++s) {
+        const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
+        const float* src = p.prev_R + (size_t)s * p.prev_stride + (size_t)bh * 4096 + f_row * 64 + c0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) Rp[e] = Ds * Rp[e] + src[e];
       }
       for (int s = 0; s < seg; ++s) {
         const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
@@ -658,8 +670,8 @@ bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in
 }
 
 template <int CT, bool PS, bool GATE>
-static int run_tc(const SlotParams& sp, const SlotGate* gt, int64_t B, int64_t in_sb, int64_t in_st, void* ws,
-                  cudaStream_t s) {
+static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* carry, int64_t B, int64_t in_sb,
+                  int64_t in_st, void* ws, cudaStream_t s) {
   const int64_t BH = B * sp.H;
   SlotTcParams p{};
   p.gamma = sp.gamma; p.log_a = sp.log_a; p.y = sp.y; p.y_sb = sp.y_sb; p.y_sh = sp.y_sh; p.y_st = sp.y_st;
@@ -678,7 +690,11 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, int64_t B, int64_t i
   if (int e = make_map(&mq, sp.q, W, sp.L, B, in_st, sb, CT)) return e;
   if (int e = make_map(&mk, sp.k, W, sp.L, B, in_st, sb, CT)) return e;
   if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
-  if (p.nseg > 1) {
+  if (carry) {
+    p.prev_R = carry->prev_R; p.prev_D = carry->prev_D; p.prev_stride = carry->prev_stride; p.nprev = carry->nprev;
+  }
+  // with a carry the workspace already holds every segment's state (hdc_slot_state_fwd)
+  if (p.nseg > 1 && !carry) {
     p.nseg_a = p.nseg - 1;
     const size_t sm = smem_state_bytes(CT);
     cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
@@ -750,26 +766,26 @@ int slot_tc_state_fwd(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in_
 }
 
 template <bool GATE>
-static int slot_tc_dispatch(const SlotParams& p, const SlotGate* gt, int64_t B, int64_t in_sb, int64_t in_st,
-                            void* ws, cudaStream_t s) {
+static int slot_tc_dispatch(const SlotParams& p, const SlotGate* gt, const SlotCarry* cy, int64_t B, int64_t in_sb,
+                            int64_t in_st, void* ws, cudaStream_t s) {
   const bool ps = p.log_a != nullptr;
   switch (p.C) {
     case 64:
-      return ps ? run_tc<64, true, GATE>(p, gt, B, in_sb, in_st, ws, s)
-                : run_tc<64, false, GATE>(p, gt, B, in_sb, in_st, ws, s);
+      return ps ? run_tc<64, true, GATE>(p, gt, cy, B, in_sb, in_st, ws, s)
+                : run_tc<64, false, GATE>(p, gt, cy, B, in_sb, in_st, ws, s);
     case 128:
-      return ps ? run_tc<128, true, GATE>(p, gt, B, in_sb, in_st, ws, s)
-                : run_tc<128, false, GATE>(p, gt, B, in_sb, in_st, ws, s);
+      return ps ? run_tc<128, true, GATE>(p, gt, cy, B, in_sb, in_st, ws, s)
+                : run_tc<128, false, GATE>(p, gt, cy, B, in_sb, in_st, ws, s);
     default:
-      return ps ? run_tc<256, true, GATE>(p, gt, B, in_sb, in_st, ws, s)
-                : run_tc<256, false, GATE>(p, gt, B, in_sb, in_st, ws, s);
+      return ps ? run_tc<256, true, GATE>(p, gt, cy, B, in_sb, in_st, ws, s)
+                : run_tc<256, false, GATE>(p, gt, cy, B, in_sb, in_st, ws, s);
   }
 }
 
-int slot_tc_fwd(const SlotParams& p, const SlotGate* gt, int64_t B, int64_t in_sb, int64_t in_st, void* ws,
-                cudaStream_t s) {
-  return gt ? slot_tc_dispatch<true>(p, gt, B, in_sb, in_st, ws, s)
-            : slot_tc_dispatch<false>(p, gt, B, in_sb, in_st, ws, s);
+int slot_tc_fwd(const SlotParams& p, const SlotGate* gt, const SlotCarry* carry, int64_t B, int64_t in_sb,
+                int64_t in_st, void* ws, cudaStream_t s) {
+  return gt ? slot_tc_dispatch<true>(p, gt, carry, B, in_sb, in_st, ws, s)
+            : slot_tc_dispatch<false>(p, gt, carry, B, in_sb, in_st, ws, s);
 }
 
 }  // namespace hdc

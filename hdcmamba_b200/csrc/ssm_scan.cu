@@ -17,6 +17,8 @@
 //                                 then the outputs, written with caller strides.
 #include <mutex>
 
+#include <climits>
+
 #include "common.cuh"
 
 namespace hdc {
@@ -25,6 +27,9 @@ struct SsmParams {
   const void* projs; int64_t psb, pst;
   const void* A_log;
   float* stats_w; const float* stats_r; int64_t stats_sb; int n_prev;
+  // statistics read in blocks of `blk` chunks, blocks `blk_stride` floats apart (the
+  // rank-major layout of gathered per-rank statistics); blk = INT_MAX: one block
+  int blk; int64_t blk_stride;
   void* y; int64_t ysb, yst;
   int L, ds, C, S;
 };
@@ -89,10 +94,15 @@ __global__ void ssm_scan_out_kernel(SsmParams p) {
 
   // exclusive prefix over chunks [0, n_prev + n) -- fp32, sequential (the reference order)
   if (s == 0) {
-    const float* st = p.stats_r + (size_t)b * p.stats_sb;
     const int m_end = p.n_prev + n;
     float G = 0.f;
-    for (int m = 0; m < m_end; ++m) G = G * expf(st[(size_t)m * 2 * p.ds + p.ds + j]) + st[(size_t)m * 2 * p.ds + j];
+    for (int m0 = 0, blkno = 0; m0 < m_end; ++blkno) {
+      const float* st = p.stats_r + (size_t)blkno * p.blk_stride + (size_t)b * p.stats_sb;
+      const int m1 = min(m_end - m0, p.blk);
+      for (int m = 0; m < m1; ++m)
+        G = G * expf(st[(size_t)m * 2 * p.ds + p.ds + j]) + st[(size_t)m * 2 * p.ds + j];
+      m0 += m1;
+    }
     shG[j] = bf16_round(G);
   }
   float h, sl;
@@ -157,16 +167,16 @@ extern "C" int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb
   return launch_status("ssm_chunk_stats_kernel");
 }
 
-extern "C" int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
-                                const void* A_log, const float* stats, int64_t stats_sb, int64_t n_prev,
-                                void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds,
-                                int64_t C, hdc_stream_t stream) {
+static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st, const void* A_log,
+                               const float* stats, int64_t stats_sb, int64_t blk, int64_t blk_stride,
+                               int64_t n_prev, void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L,
+                               int64_t ds, int64_t C, hdc_stream_t stream) {
   if (int e = ssm_check(dtype, projs, A_log, B, L, ds, C)) return e;
   if (!stats || !y) return fail(HDC_E_NULL, "ssm: null stats / y");
-  if (n_prev < 0 || stats_sb < (n_prev + L / C) * 2 * ds) return fail(HDC_E_SHAPE, "ssm: stats batch stride too small");
   SsmParams p{};
   p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_r = stats;
   p.stats_sb = stats_sb; p.n_prev = (int)n_prev; p.y = y; p.ysb = y_sb; p.yst = y_st;
+  p.blk = (int)blk; p.blk_stride = blk_stride;
   p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C);
   dim3 grid((unsigned)(L / C), (unsigned)B);
   const size_t smem = (2 * p.S + 1) * ds * sizeof(float);
@@ -174,6 +184,31 @@ extern "C" int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, i
   if (dtype == HDC_F32) ssm_scan_out_kernel<float><<<grid, p.S * ds, smem, s>>>(p);
   else ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * ds, smem, s>>>(p);
   return launch_status("ssm_scan_out_kernel");
+}
+
+extern "C" int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                                const void* A_log, const float* stats, int64_t stats_sb, int64_t n_prev,
+                                void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds,
+                                int64_t C, hdc_stream_t stream) {
+  if (n_prev < 0 || (C > 0 && stats_sb < (n_prev + L / C) * 2 * ds))
+    return fail(HDC_E_SHAPE, "ssm: stats batch stride too small");
+  return ssm_scan_out_launch(dtype, projs, proj_sb, proj_st, A_log, stats, stats_sb, INT_MAX, 0, n_prev, y, y_sb,
+                             y_st, B, L, ds, C, stream);
+}
+
+extern "C" int hdc_ssm_scan_out_blocked(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                                        const void* A_log, const float* stats, int64_t stats_sb,
+                                        int64_t block_chunks, int64_t block_stride, int64_t n_prev, void* y,
+                                        int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds, int64_t C,
+                                        hdc_stream_t stream) {
+  if (n_prev < 0 || block_chunks < 1 || block_chunks > INT_MAX)
+    return fail(HDC_E_SHAPE, "ssm: n_prev=%lld block_chunks=%lld", (long long)n_prev, (long long)block_chunks);
+  if (stats_sb < 0 || (B > 1 && stats_sb < block_chunks * 2 * ds) ||
+      ((n_prev + (C > 0 ? L / C : 0)) > block_chunks && block_stride < B * block_chunks * 2 * ds))
+    return fail(HDC_E_SHAPE, "ssm: statistics blocks overlap (stats_sb %lld, block_stride %lld)",
+                (long long)stats_sb, (long long)block_stride);
+  return ssm_scan_out_launch(dtype, projs, proj_sb, proj_st, A_log, stats, stats_sb, block_chunks, block_stride,
+                             n_prev, y, y_sb, y_st, B, L, ds, C, stream);
 }
 
 // ---------------------------------------------------------------------------------

@@ -76,17 +76,21 @@ def _row_view(t, what):
     return t.stride(0), t.stride(1)
 
 
-def ssm_chunk_stats(projs, A_log, d_state, chunk):
+def ssm_chunk_stats(projs, A_log, d_state, chunk, out=None):
     """Per-chunk statistics [B, N, 2*ds] fp32 (last state, summed log decay), bf16-rounded.
 
-    Replaces the last_state / chunk_decay outputs of ``_ssm_intra_v2`` (hdcmamba/model.py:175-198)."""
-    _cuda(projs, A_log)
+    Replaces the last_state / chunk_decay outputs of ``_ssm_intra_v2`` (hdcmamba/model.py:175-198).
+    ``out``: optional contiguous fp32 [B, N, 2*ds] tensor to write into."""
+    _cuda(projs, A_log, out)
     B, L, P = projs.shape
     if P < 3 * d_state or L % chunk != 0:
         raise ValueError(f"projs [B, L, {P}] needs >= 3*d_state columns and L % chunk == 0")
     sb, st = _row_view(projs, "projs")
     a = A_log.to(projs.dtype).contiguous()
-    stats = torch.empty(B, L // chunk, 2 * d_state, device=projs.device, dtype=torch.float32)
+    shape = (B, L // chunk, 2 * d_state)
+    if out is not None and (tuple(out.shape) != shape or out.dtype != torch.float32 or not out.is_contiguous()):
+        raise ValueError(f"out must be a contiguous fp32 {list(shape)} tensor")
+    stats = out if out is not None else torch.empty(shape, device=projs.device, dtype=torch.float32)
     _lib.call("hdc_ssm_chunk_stats", _code(projs), _p(projs), sb, st, _p(a), _p(stats), B, L, d_state, chunk,
               _stream(projs))
     return stats
@@ -112,6 +116,35 @@ def ssm_scan_out(projs, A_log, stats, n_prev, d_state, chunk, out=None):
         raise ValueError("stats must be fp32 [B, n_prev + L/chunk, 2*d_state]")
     _lib.call("hdc_ssm_scan_out", _code(projs), _p(projs), sb, st, _p(a), _p(stats), stats.stride(0), n_prev,
               _p(out), osb, ost, B, L, d_state, chunk, _stream(projs))
+    return out
+
+
+def ssm_scan_out_blocked(projs, A_log, stats, stats_sb, block_chunks, block_stride, n_prev, d_state, chunk,
+                         out=None):
+    """ssm_scan_out reading the statistics of chunks [0, n_prev + N) in place from a
+    rank-major gathered buffer: ``stats`` is a 1-D fp32 tensor whose element 0 is chunk 0
+    of block 0; chunk m of batch b is at (m // block_chunks) * block_stride + b * stats_sb
+    + (m % block_chunks) * 2 * ds (hdc_ssm_scan_out_blocked)."""
+    _cuda(projs, A_log, stats, out)
+    B, L, P = projs.shape
+    if P < 3 * d_state or L % chunk != 0:
+        raise ValueError(f"projs [B, L, {P}] needs >= 3*d_state columns and L % chunk == 0")
+    if stats.dtype != torch.float32 or stats.dim() != 1 or stats.stride(0) != 1:
+        raise ValueError("stats must be a 1-D contiguous fp32 tensor")
+    m_end = n_prev + L // chunk
+    last_blk = (m_end - 1) // block_chunks
+    rows_in_last = m_end - last_blk * block_chunks
+    need = last_blk * block_stride + (B - 1) * stats_sb + rows_in_last * 2 * d_state
+    if need > stats.numel():
+        raise ValueError(f"stats holds {stats.numel()} floats, the layout reads up to {need}")
+    sb, st = _row_view(projs, "projs")
+    a = A_log.to(projs.dtype).contiguous()
+    if out is None:
+        out = torch.empty(B, L, d_state, device=projs.device, dtype=projs.dtype)
+    _same_dtype(projs, out)
+    osb, ost = _row_view(out, "out")
+    _lib.call("hdc_ssm_scan_out_blocked", _code(projs), _p(projs), sb, st, _p(a), _p(stats), stats_sb, block_chunks,
+              block_stride, n_prev, _p(out), osb, ost, B, L, d_state, chunk, _stream(projs))
     return out
 
 
@@ -218,10 +251,22 @@ def slot_scan_gate(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_strides
     return (out, state_out) if return_state else out
 
 
-def slot_state(k, v, num_heads, chunk, gamma=None, log_a=None):
+def slot_workspace(B, L, num_heads, head_dim, chunk, device):
+    """A device workspace for one slot call of this shape (uint8)."""
+    return torch.empty(max(slot_workspace_bytes(B, L, num_heads, head_dim, chunk), 16), device=device,
+                       dtype=torch.uint8)
+
+
+def _f32_out(t, shape, what):
+    if t is not None and (tuple(t.shape) != tuple(shape) or t.dtype != torch.float32 or not t.is_contiguous()):
+        raise ValueError(f"{what} must be a contiguous fp32 {list(shape)} tensor")
+
+
+def slot_state(k, v, num_heads, chunk, gamma=None, log_a=None, state_out=None, decay_out=None, workspace=None):
     """State after the whole sequence from a zero start, fp32 [B, H, 64, 64], and the
-    product of all chunk decays [B, H] (for sequence-parallel carries)."""
-    _cuda(k, v, gamma, log_a)
+    product of all chunk decays [B, H] (for sequence-parallel carries).  ``workspace``
+    (from ``slot_workspace``) keeps the segment states for ``slot_scan_gate_carry``."""
+    _cuda(k, v, gamma, log_a, state_out, decay_out, workspace)
     _same_dtype(k, v)
     B, L, W = k.shape
     H = num_heads
@@ -232,12 +277,48 @@ def slot_state(k, v, num_heads, chunk, gamma=None, log_a=None):
         gamma = gamma.to(k.dtype).contiguous()
     if log_a is not None:
         log_a = log_a.float().contiguous()
-    state = torch.empty(B, H, 64, 64, device=k.device, dtype=torch.float32)
-    decay = torch.empty(B, H, device=k.device, dtype=torch.float32)
-    ws = torch.empty(max(slot_workspace_bytes(B, L, H, hd, chunk), 16), device=k.device, dtype=torch.uint8)
+    _f32_out(state_out, (B, H, 64, 64), "state_out")
+    _f32_out(decay_out, (B, H), "decay_out")
+    state = state_out if state_out is not None else torch.empty(B, H, 64, 64, device=k.device, dtype=torch.float32)
+    decay = decay_out if decay_out is not None else torch.empty(B, H, device=k.device, dtype=torch.float32)
+    ws = workspace if workspace is not None else slot_workspace(B, L, H, hd, chunk, k.device)
     _lib.call("hdc_slot_state_fwd", _code(k), _p(k), _p(v), k.stride(0), k.stride(1), _p(gamma), _p(log_a),
               _p(state), _p(decay), _p(ws), ws.numel(), B, L, H, hd, chunk, _stream(k))
     return state, decay
+
+
+def slot_scan_gate_carry(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_strides, prev_state, prev_decay,
+                         prev_stride, n_prev, workspace, gamma=None, log_a=None):
+    """``slot_scan_gate`` for one rank's part of the sequence (hdc_slot_gate_carry_fwd):
+    the entering state folds the n_prev earlier parts, part s with its fp32 state at
+    prev_state[s*prev_stride:] ([B, H, 64, 64]) and decay at prev_decay[s*prev_stride:]
+    ([B, H]); ``workspace`` is the one ``slot_state`` filled for the same k, v."""
+    _cuda(q, k, v, gamma, log_a, gate, gn_w, gn_b, out, prev_state, prev_decay, workspace)
+    _same_dtype(q, k, v, gate, out)
+    B, L, W = q.shape
+    H = num_heads
+    hd = W // H
+    if q.stride() != k.stride() or q.stride() != v.stride() or gate.stride(2) != 1:
+        raise ValueError("q, k, v must share strides; gate needs a unit last stride")
+    if (gamma is None) == (log_a is None):
+        raise ValueError("give exactly one of gamma or log_a")
+    if n_prev > 0:
+        for t, per in ((prev_state, B * H * 4096), (prev_decay, B * H)):
+            if t.dtype != torch.float32 or t.dim() != 1 or t.stride(0) != 1:
+                raise ValueError("prev_state / prev_decay must be 1-D contiguous fp32 tensors")
+            if (n_prev - 1) * prev_stride + per > t.numel():
+                raise ValueError("prev_state / prev_decay too short for n_prev parts")
+    if gamma is not None:
+        gamma = gamma.to(q.dtype).contiguous()
+    if log_a is not None:
+        log_a = log_a.float().contiguous()
+    gw = gn_w.to(q.dtype).contiguous()
+    gb = gn_b.to(q.dtype).contiguous()
+    _lib.call("hdc_slot_gate_carry_fwd", _code(q), _p(q), _p(k), _p(v), q.stride(0), q.stride(1), _p(gamma),
+              _p(log_a), _p(gate), gate.stride(0), gate.stride(1), _p(gw), _p(gb), _p(out), out_strides[0],
+              out_strides[1], out_strides[2], _p(prev_state if n_prev else None), _p(prev_decay if n_prev else None),
+              prev_stride, n_prev, None, _p(workspace), workspace.numel(), B, L, H, hd, chunk, _stream(q))
+    return out
 
 
 # ------------------------------------------------------------------ gate / concat / LN

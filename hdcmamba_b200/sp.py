@@ -6,14 +6,17 @@ dependencies, and each is exchanged once per layer with ``all_gather`` (NCCL ove
 
 1. Halo.  The causal conv of LN+conv reads the three rows before the segment, i.e. the
    last three input rows of rank r-1 (rank 0 sees the reference's zero rows).
-2. Carries, gathered in one call:
+2. Carries, gathered in one call of one flat fp32 buffer that the kernels write directly:
    * SSM: every chunk's statistics (bf16-rounded last state and summed log decay).  Each
      rank then folds the same chunks in the same order as one GPU would, so its SSM prefix
-     is bit-identical to the single-GPU one (``hdc_ssm_scan_out`` with ``n_prev``).
+     is bit-identical to the single-GPU one (``hdc_ssm_scan_out_blocked`` reads them in
+     place from the gathered rank-major buffer).
    * Slot memory: each rank's local state (fp32 64x64 per head, from a zero start) and the
      product of its chunk decays.  Rank r folds those of ranks < r into its entering
      state, R_in(r) = D_{r-1} R_in(r-1) + A_{r-1}; this is the associativity of the
-     per-chunk recurrence R <- gamma^C R + U (hdcmamba/model.py:272).
+     per-chunk recurrence R <- gamma^C R + U (hdcmamba/model.py:272).  The fold runs inside
+     the output kernel (``hdc_slot_gate_carry_fwd``), which also reuses the segment states
+     that ``hdc_slot_state_fwd`` left in the workspace.
 
 The kernels are those of the single-GPU Block (fixed semantics).  Only batch-independent
 work crosses ranks, so batch sharding (config 4) needs no collective at all and uses the
@@ -27,14 +30,10 @@ from . import ops
 
 
 class CudaKernels:
-    """The per-rank layer kernels (libhdcmamba_b200)."""
+    """The per-rank layer kernels (libhdcmamba_b200), looked up in ``ops`` at call time."""
 
-    ln_conv = staticmethod(ops.ln_conv)
-    ssm_chunk_stats = staticmethod(ops.ssm_chunk_stats)
-    ssm_scan_out = staticmethod(ops.ssm_scan_out)
-    slot_state = staticmethod(ops.slot_state)
-    slot_scan_gate = staticmethod(ops.slot_scan_gate)
-    row_layernorm = staticmethod(ops.row_layernorm)
+    def __getattr__(self, name):
+        return getattr(ops, name)
 
 
 def _all_gather(t, group):
@@ -77,23 +76,23 @@ class SequenceParallel:
         q, k, v = projs[..., so:so + dm], projs[..., so + dm:so + 2 * dm], projs[..., so + 2 * dm:so + 3 * dm]
         gate = projs[..., so + 3 * dm:]
         gamma = blk.gamma_buf.to(h.dtype)
-        # (2) carries: SSM chunk statistics, slot local state and decay product
-        stats = K.ssm_chunk_stats(projs, blk.A_log, ds, C)                  # [B, N, 2ds]
-        state, decay = K.slot_state(k, v, H, C, gamma=gamma)                # [B, H, 64, 64], [B, H]
-        flat = torch.cat([stats.reshape(-1), state.reshape(-1), decay.reshape(-1)])
-        g = _all_gather(flat, self.group)                                   # [W, n]
-        n_st, n_sl = stats.numel(), state.numel()
-        stats_all = g[:, :n_st].reshape(self.world, B, N, 2 * ds).permute(1, 0, 2, 3).reshape(B, self.world * N, 2 * ds)
-        states = g[:, n_st:n_st + n_sl].reshape(self.world, B, H, 64, 64)
-        decays = g[:, n_st + n_sl:].reshape(self.world, B, H)
-        R_in = torch.zeros_like(state)
-        for s in range(self.rank):
-            R_in = decays[s][..., None, None] * R_in + states[s]
+        # (2) carries, written by the kernels straight into one flat fp32 buffer per rank:
+        #     [SSM chunk statistics B*N*2ds | slot state B*H*4096 | slot decay B*H | pad]
+        n_st, n_sl, n_dc = B * N * 2 * ds, B * H * 4096, B * H
+        n = (n_st + n_sl + n_dc + 3) // 4 * 4
+        flat = torch.empty(n, device=h.device, dtype=torch.float32)
+        K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
+        ws = K.slot_workspace(B, Ls, H, hd, C, h.device)
+        K.slot_state(k, v, H, C, gamma=gamma, state_out=flat[n_st:n_st + n_sl].view(B, H, 64, 64),
+                     decay_out=flat[n_st + n_sl:n_st + n_sl + n_dc].view(B, H), workspace=ws)
+        g = _all_gather(flat, self.group).reshape(-1)                        # [W * n], rank-major
         combined = torch.empty(B, Ls, ds + dm, device=h.device, dtype=h.dtype)
-        K.ssm_scan_out(projs, blk.A_log, stats_all[:, :(self.rank + 1) * N].contiguous(), self.rank * N, ds, C,
-                       out=combined[..., :ds])
-        K.slot_scan_gate(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias, combined[..., ds:],
-                         (Ls * (ds + dm), hd, ds + dm), gamma=gamma, state_in=R_in)
+        # SSM: exclusive prefix over the chunks of ranks < r, then this rank's, in place
+        K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C, out=combined[..., :ds])
+        # slot: fold the states of ranks < r in rank order, then the local segments
+        K.slot_scan_gate_carry(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias, combined[..., ds:],
+                               (Ls * (ds + dm), hd, ds + dm), g[n_st:], g[n_st + n_sl:], n, self.rank, ws,
+                               gamma=gamma)
         combined = K.row_layernorm(combined, 1e-5, out=combined)
         return torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
 

@@ -97,6 +97,19 @@ int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj
                      int64_t C, hdc_stream_t stream);
 
 /*
+ * hdc_ssm_scan_out with the statistics stored in blocks of block_chunks chunks, block i
+ * at stats + i*block_stride (batch b of a block at + b*stats_sb): the rank-major layout of
+ * per-rank statistics gathered under sequence parallelism, read in place.  Chunk m of
+ * batch b is at stats + (m / block_chunks)*block_stride + b*stats_sb +
+ * (m % block_chunks)*2*ds.  Same prefix order and results as hdc_ssm_scan_out.
+ */
+int hdc_ssm_scan_out_blocked(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                             const void* A_log, const float* stats, int64_t stats_sb,
+                             int64_t block_chunks, int64_t block_stride, int64_t n_prev, void* y,
+                             int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds, int64_t C,
+                             hdc_stream_t stream);
+
+/*
  * The whole diagonal-SSM chunked scan (hdc_ssm_chunk_stats + hdc_ssm_scan_out, n_prev = 0)
  * without any device allocation by the caller or the library.  No counterpart in the
  * reference.  For callers that cannot allocate device memory (a host that only hands the
@@ -168,11 +181,33 @@ int hdc_slot_gate_fwd(int dtype, const void* q, const void* k, const void* v, in
  * no outputs.  The sequence-parallel runner exchanges these per rank and folds them into
  * the next rank's state_in (hdc_slot_scan_fwd / hdc_slot_gate_fwd).  Same chunk recurrence
  * as _slot_all_fused's `running` (hdcmamba/model.py:252, 271-272).  bf16, tcgen05 path only.
+ * On return `workspace` also holds every segment's local state, which
+ * hdc_slot_gate_carry_fwd reuses.
  */
 int hdc_slot_state_fwd(int dtype, const void* k, const void* v, int64_t in_sb, int64_t in_st,
                        const void* gamma, const float* log_a, float* state_out, float* decay_out,
                        void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
                        int64_t hd, int64_t C, hdc_stream_t stream);
+
+/*
+ * hdc_slot_gate_fwd for one rank's part of a sequence under sequence parallelism: the
+ * entering state is folded from the n_prev earlier parts, R <- D_s R + R_s for s = 0 ..
+ * n_prev-1 (R from zero), where part s has R_s at prev_state + s*prev_stride (fp32
+ * [B*H, 64, 64]) and D_s at prev_decay + s*prev_stride (fp32 [B*H]): the gathered
+ * state_out / decay_out of hdc_slot_state_fwd on the earlier ranks.  `workspace` must be
+ * the one that this rank's hdc_slot_state_fwd over the same k, v and shape filled (its
+ * segment states are reused; only the output pass runs).  No single-launch counterpart in
+ * the reference: it replaces _slot_all_fused's carry of `running` across chunks
+ * (hdcmamba/model.py:252, 271-272) across ranks.
+ */
+int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                            int64_t in_st, const void* gamma, const float* log_a, const void* gate,
+                            int64_t gate_sb, int64_t gate_st, const void* gn_w, const void* gn_b,
+                            void* out, int64_t out_sb, int64_t out_sh, int64_t out_st,
+                            const float* prev_state, const float* prev_decay, int64_t prev_stride,
+                            int64_t n_prev, float* state_out, void* workspace, size_t workspace_bytes,
+                            int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C,
+                            hdc_stream_t stream);
 
 /*
  * Slot-scan path control (tests / cross-checks): mode 0 = automatic (tcgen05 for bf16

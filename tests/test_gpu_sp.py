@@ -75,3 +75,70 @@ def test_sequence_parallel_two_gpus_matches_one_gpu():
     assert dev_err == 0
     assert err < BF16_TOL, err
     assert all(p.exitcode == 0 for p in procs)
+
+
+# ------------------------------------------------------------------ one GPU, ranks emulated
+def _rel(a, b):
+    a, b = a.detach().float().cpu(), b.detach().float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-6))
+
+
+@pytest.mark.parametrize("W,B,N,ds,C", [(4, 1, 8, 64, 256), (3, 2, 4, 32, 128)])
+def test_ssm_scan_out_blocked_equals_contiguous_stats(W, B, N, ds, C):
+    """hdc_ssm_scan_out_blocked over a rank-major buffer of per-part statistics gives the
+    same bits as hdc_ssm_scan_out over the contiguous statistics of the whole sequence."""
+    from hdcmamba_b200 import _lib, ops
+    L = W * N * C
+    g = torch.Generator().manual_seed(7 + W)
+    projs = (0.7 * torch.randn(B, L, 3 * ds + 64, generator=g)).bfloat16().cuda()
+    A_log = (0.3 * torch.randn(ds, generator=g)).cuda()
+    y_ref = ops.ssm_scan(projs, A_log, ds, C)
+    n = B * N * 2 * ds + 12  # a padded per-rank row, as the sequence-parallel buffer has
+    gathered = torch.full((W * n,), float("nan"), device="cuda")
+    Ls = N * C
+    for r in range(W):
+        ops.ssm_chunk_stats(projs[:, r * Ls:(r + 1) * Ls], A_log, ds, C,
+                            out=gathered[r * n:r * n + B * N * 2 * ds].view(B, N, 2 * ds))
+    for r in range(W):
+        y = ops.ssm_scan_out_blocked(projs[:, r * Ls:(r + 1) * Ls], A_log, gathered, N * 2 * ds, N, n, r * N, ds, C)
+        assert torch.equal(y, y_ref[:, r * Ls:(r + 1) * Ls]), r
+    torch.cuda.synchronize()
+    assert _lib.load().hdc_device_error(1) == 0
+
+
+@pytest.mark.parametrize("W,B,L,H,C", [(4, 1, 4096, 4, 256), (2, 2, 1024, 4, 64), (3, 1, 3 * 512, 2, 128)])
+def test_slot_gate_carry_matches_whole_sequence(W, B, L, H, C):
+    """Per-part hdc_slot_state_fwd into a rank-major buffer, then hdc_slot_gate_carry_fwd
+    for each part, equals hdc_slot_gate_fwd over the whole sequence."""
+    from hdcmamba_b200 import _lib, ops
+    dm, ds = 64 * H, 64
+    hd = dm // H
+    g = torch.Generator().manual_seed(90 + W)
+    projs = (0.6 * torch.randn(B, L, 4 * dm, generator=g)).bfloat16().cuda()
+    q, k, v, gate = (projs[..., i * dm:(i + 1) * dm] for i in range(4))
+    gamma = torch.exp(-torch.nn.functional.softplus(torch.randn(H, generator=g) - 3.0)).bfloat16().cuda()
+    gw = (1 + 0.2 * torch.randn(dm, generator=g)).bfloat16().cuda()
+    gb = (0.2 * torch.randn(dm, generator=g)).bfloat16().cuda()
+    strides = lambda Lx: (Lx * dm, hd, dm)  # noqa: E731
+    ref = torch.empty(B, L, dm, device="cuda", dtype=torch.bfloat16)
+    ops.slot_scan_gate(q, k, v, H, C, gate, gw, gb, ref, strides(L), gamma=gamma)
+    Ls = L // W
+    n_sl, n_dc = B * H * 4096, B * H
+    n = n_sl + n_dc + 4
+    gathered = torch.full((W * n,), float("nan"), device="cuda")
+    wss = []
+    for r in range(W):
+        sl = slice(r * Ls, (r + 1) * Ls)
+        ws = ops.slot_workspace(B, Ls, H, hd, C, "cuda")
+        ops.slot_state(k[:, sl], v[:, sl], H, C, gamma=gamma, state_out=gathered[r * n:r * n + n_sl].view(B, H, 64, 64),
+                       decay_out=gathered[r * n + n_sl:r * n + n_sl + n_dc].view(B, H), workspace=ws)
+        wss.append(ws)
+    out = torch.empty(B, L, dm, device="cuda", dtype=torch.bfloat16)
+    for r in range(W):
+        sl = slice(r * Ls, (r + 1) * Ls)
+        # out[:, sl] is a view into the whole [B, L, dm] output: batch stride L*dm
+        ops.slot_scan_gate_carry(q[:, sl], k[:, sl], v[:, sl], H, C, gate[:, sl], gw, gb, out[:, sl], strides(L),
+                                 gathered, gathered[n_sl:], n, r, wss[r], gamma=gamma)
+    torch.cuda.synchronize()
+    assert _lib.load().hdc_device_error(1) == 0
+    assert _rel(out, ref) < BF16_TOL, _rel(out, ref)

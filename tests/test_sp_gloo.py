@@ -24,15 +24,31 @@ class OracleKernels:
         return O.ln_conv_fwd(x, nw, nb, cw, cb, eps, halo=halo)[0]
 
     @staticmethod
-    def ssm_chunk_stats(projs, A_log, ds, C):
+    def ssm_chunk_stats(projs, A_log, ds, C, out=None):
         _, _, last, cdec = O.ssm_chunk_states(projs, A_log.to(projs.dtype), ds, C)
-        return torch.cat([last, cdec], -1)
+        st = torch.cat([last, cdec], -1)
+        if out is None:
+            return st
+        out.copy_(st)
+        return out
 
     @staticmethod
-    def ssm_scan_out(projs, A_log, stats, n_prev, ds, C, out):
+    def ssm_scan_out_blocked(projs, A_log, stats, stats_sb, block_chunks, block_stride, n_prev, ds, C, out):
+        """Reads chunk m of batch b at (m // block_chunks) * block_stride + b * stats_sb +
+        (m % block_chunks) * 2ds, as hdc_ssm_scan_out_blocked does."""
         Bb, Ls, _ = projs.shape
+        m_end = n_prev + Ls // C
+        rows = []
+        for b in range(Bb):
+            per_b = []
+            for m in range(m_end):
+                blk, i = divmod(m, block_chunks)
+                o = blk * block_stride + b * stats_sb + i * 2 * ds
+                per_b.append(stats[o:o + 2 * ds])
+            rows.append(torch.stack(per_b))
+        stats_all = torch.stack(rows)
         y_intra, cum, _, _ = O.ssm_chunk_states(projs, A_log.to(projs.dtype), ds, C)
-        G_all, _ = O.ssm_prefix(stats[..., :ds], stats[..., ds:])
+        G_all, _ = O.ssm_prefix(stats_all[..., :ds], stats_all[..., ds:])
         G = G_all[:, n_prev:]
         y = O.kbf16(y_intra + G[:, :, None] * torch.exp(cum)).reshape(Bb, Ls, ds)
         out.copy_(y.to(out.dtype))
@@ -44,19 +60,33 @@ class OracleKernels:
         return torch.cat([torch.zeros(Bb, Ls, 3 * ds, dtype=q.dtype), q, k, v, gate], -1)
 
     @staticmethod
-    def slot_state(k, v, H, C, gamma):
+    def slot_workspace(B, L, H, hd, C, device):
+        return None
+
+    @staticmethod
+    def slot_state(k, v, H, C, gamma, state_out, decay_out, workspace):
         Bb, Ls, dm = k.shape
         pj = torch.cat([k, k, v, torch.zeros_like(v)], -1)
         _, R = O.slot_fwd(pj, gamma, dm, H, C, 0, block_c=max(128, C), return_state=True)
         lg = torch.log(gamma.float())
         decay = torch.exp(C * lg).repeat(Bb).reshape(Bb, H) ** (Ls // C)
-        return R.reshape(Bb, H, 64, 64), decay
+        state_out.copy_(R.reshape(Bb, H, 64, 64))
+        decay_out.copy_(decay)
+        return state_out, decay_out
 
     @staticmethod
-    def slot_scan_gate(q, k, v, H, C, gate, gn_w, gn_b, out, strides, gamma, state_in):
+    def slot_scan_gate_carry(q, k, v, H, C, gate, gn_w, gn_b, out, strides, prev_state, prev_decay, prev_stride,
+                             n_prev, workspace, gamma):
+        """Folds part s (state at prev_state[s*prev_stride:], decay at prev_decay[s*prev_stride:])
+        into the entering state in order, as hdc_slot_gate_carry_fwd does."""
         Bb, Ls, dm = q.shape
+        R_in = torch.zeros(Bb, H, 64, 64)
+        for s in range(n_prev):
+            o = s * prev_stride
+            R_in = (prev_decay[o:o + Bb * H].view(Bb, H)[..., None, None] * R_in
+                    + prev_state[o:o + Bb * H * 4096].view(Bb, H, 64, 64))
         pj = OracleKernels._projs(q, k, v, gate, D_STATE)
-        y = O.slot_fwd(pj, gamma, dm, H, C, 3 * D_STATE, block_c=max(128, C), R0=state_in.reshape(Bb * H, 64, 64))
+        y = O.slot_fwd(pj, gamma, dm, H, C, 3 * D_STATE, block_c=max(128, C), R0=R_in.reshape(Bb * H, 64, 64))
         comb = O.gnorm_gate_cat(y, torch.zeros(Bb, Ls, D_STATE, dtype=q.dtype), pj, gn_w, gn_b, D_STATE, H, C,
                                 mode="fixed")
         out.copy_(comb[..., D_STATE:])
