@@ -57,14 +57,17 @@ class ClockSampler:
     def __init__(self, device):
         self.proc = None
         self.lines = []
+        self.marks = []
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
             self.gid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
         except Exception:
             self.gid = None
 
-    def start(self):
-        cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "100"]
+    def start(self, ready_timeout=5.0):
+        """Start sampling every 50 ms and wait (bounded) for the first sample, so that a
+        short timed region that follows is covered."""
+        cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "50"]
         if self.gid:
             cmd += ["-i", self.gid]
         try:
@@ -73,10 +76,18 @@ class ClockSampler:
             self.t.start()
         except Exception:
             self.proc = None
+            return
+        t_end = time.monotonic() + ready_timeout
+        while not self.lines and time.monotonic() < t_end:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark(self):
+        """Host time of a timed-region boundary (taken after a device synchronize)."""
+        self.marks.append(time.monotonic())
 
     def stop(self):
         if not self.proc:
@@ -87,9 +98,14 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.t.join(timeout=2)
+        window = "timed region"
+        lines = [ln for t, ln in self.lines if len(self.marks) >= 2 and self.marks[0] <= t <= self.marks[1] + 0.06]
+        if not lines:  # timed region shorter than the sampling period: warm-up and timed steps
+            window = "warm-up + timed steps (timed region shorter than the 50 ms sampling period)"
+            lines = [ln for t, ln in self.lines if not self.marks or t <= self.marks[-1] + 0.06]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 8:
                 continue
@@ -102,7 +118,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 def _time_cuda(fn, iters, warmup=3):
@@ -309,31 +325,28 @@ def main():
         def step_host():
             return graphed(ids_host)  # pinned host -> static input (H2D), then replay
 
-    # instrument the slot scan (dominant custom kernel) with events on its launch stream
-    slot_events = []
-    # (sequence parallel: slot_state + slot_scan_gate_carry make up one layer's slot op)
-    originals = {name: getattr(ops, name) for name in ("slot_scan", "slot_scan_gate", "slot_state",
-                                                      "slot_scan_gate_carry")}
+    # the slot op (roofline kernel) of one layer: its arguments are captured from an eager
+    # forward; sequence parallel runs slot_state + slot_scan_gate_carry for one layer's op
+    slot_names = ("slot_scan", "slot_scan_gate", "slot_state", "slot_scan_gate_carry")
+    originals = {name: getattr(ops, name) for name in slot_names}
+    slot_calls = []
 
-    def timed(fn, name):
+    def grab(fn, name):
         def wrapper(*a, **k):
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            r = fn(*a, **k)
-            e.record()
-            slot_events.append((name, s, e))
-            return r
+            slot_calls.append((fn, a, k))
+            return fn(*a, **k)
         return wrapper
 
+    sampler = ClockSampler(dev)
+    sampler.start()  # samples the warm-up too, for timed regions shorter than its period
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
 
-    sampler = ClockSampler(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler.start()
+    sampler.mark()
     n0 = _lib.launch_count()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -341,6 +354,7 @@ def main():
         step()
     t1.record()
     torch.cuda.synchronize()
+    sampler.mark()
     launches = _lib.launch_count() - n0
     if not args.eager:
         launches = graphed.launches_per_replay * args.steps  # replays issue the captured launches
@@ -348,19 +362,38 @@ def main():
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1) / args.steps
-    # per-launch time of the slot op (the roofline kernel): CUDA events around each call on
-    # its launch stream, over eager forward passes of the same inputs
-    for name, fn in originals.items():
-        setattr(ops, name, timed(fn, name))
+    # per-launch time of the slot op: one layer's slot calls (arguments captured from an
+    # eager forward) replayed as a CUDA graph between CUDA events on the replay stream, each
+    # replay preceded by a 512 MB write that evicts L2
+    for name in slot_names:
+        setattr(ops, name, grab(originals[name], name))
     with torch.no_grad():
-        for _ in range(2):
-            forward(ids)
+        forward(ids)
+    for name in slot_names:
+        setattr(ops, name, originals[name])
+    per_layer = 2 if world > 1 else 1
+    layer_calls = slot_calls[:per_layer]
+    slot_per_step = len(slot_calls) / per_layer
+
+    def slot_layer():
+        for fn, a, k in layer_calls:
+            fn(*a, **k)
+
+    slot_graph = torch.cuda.CUDAGraph()
+    with torch.no_grad(), torch.cuda.graph(slot_graph):
+        slot_layer()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    durations = []
+    for it in range(11):
+        flush.zero_()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        slot_graph.replay()
+        s1.record()
+        durations.append((s0, s1))
     torch.cuda.synchronize()
-    for name, fn in originals.items():
-        setattr(ops, name, fn)
-    n_ops = sum(1 for name, _, _ in slot_events if name != "slot_state")
-    slot_ms = sum(s.elapsed_time(e) for _, s, e in slot_events) / n_ops
-    slot_per_step = n_ops / 2
+    slot_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in durations[1:])
+    del flush, slot_calls, layer_calls, slot_graph
 
     # end to end through the public call: pinned host ids -> device, logits[:, -1] -> host
     out_host = torch.empty(cfg.batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
@@ -398,7 +431,12 @@ def main():
             "roofline": {"kernel": ("slot_state + slot_scan_gate_carry (slot_tc_state + slot_fold + slot_tc_out)"
                                     if world > 1 else "slot_scan_gate (slot_tc_state + slot_tc_out)"), "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
-                         "traffic": SLOT_TRAFFIC_BYTES, "algorithmic_bytes_per_launch": slot_bytes,
+                         "traffic": SLOT_TRAFFIC_BYTES * tokens_per_rank / (cfg.batch * cfg.seq_len),
+                         "traffic_source": "ncu capture of the 1-GPU op" + (
+                             ", scaled by this rank's share of the tokens" if world > 1 else ""),
+                         "timing": "CUDA events around a CUDA-graph replay of one layer's slot calls, "
+                                   "L2 flushed before each, mean of 10",
+                         "algorithmic_bytes_per_launch": slot_bytes,
                          "ms_per_launch": slot_ms, "launches_per_step": slot_per_step},
             "e2e": {"value": world * tokens_per_rank / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": world * ids_host.numel() * ids_host.element_size(),

@@ -89,6 +89,56 @@ __global__ void row_layernorm_kernel(const T* in, T* out, int64_t rows, int widt
   for (int c = lane; c < width; c += 32) o[c] = from_f<T>((to_f(r[c]) - mean) * rstd);
 }
 
+// Vectorized variant: one warp per row, the row held in registers as 16-byte vectors
+// (lane l holds vectors l, l+32, ...), so the row is read once and written once.
+// Needs width % 8 == 0 (bf16), 16-byte aligned rows and width <= 8 * 32 * MAXV.
+template <int MAXV>
+__global__ void row_layernorm_vec_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, int64_t rows, int width,
+                                         float eps) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int nv = width >> 3;
+  const __nv_bfloat16* r = in + row * width;
+  __nv_bfloat16* o = out + row * width;
+  uint4 raw[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i)
+    if (lane + 32 * i < nv) raw[i] = *reinterpret_cast<const uint4*>(r + (lane + 32 * i) * 8);  // may alias out
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (lane + 32 * i < nv) {
+      float f[8];
+      unpack16<__nv_bfloat16>(raw[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += f[e];
+    }
+  }
+  const float mean = warp_sum(s) / (float)width;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (lane + 32 * i < nv) {
+      float f[8];
+      unpack16<__nv_bfloat16>(raw[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q += (f[e] - mean) * (f[e] - mean);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / (float)width + eps);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    if (lane + 32 * i < nv) {
+      float f[8];
+      unpack16<__nv_bfloat16>(raw[i], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = (f[e] - mean) * rstd;
+      stg16(o + (lane + 32 * i) * 8, pack16<__nv_bfloat16>(f));
+    }
+  }
+}
+
 }  // namespace hdc
 
 using namespace hdc;
@@ -123,6 +173,13 @@ extern "C" int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t r
   const int wpb = 8;
   const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == HDC_BF16 && width % 8 == 0 && width <= 8 * 32 * 8 && aligned16(in) && aligned16(out)) {
+    auto i = static_cast<const __nv_bfloat16*>(in);
+    auto o = static_cast<__nv_bfloat16*>(out);
+    if (width <= 8 * 32 * 4) row_layernorm_vec_kernel<4><<<grid, 32 * wpb, 0, s>>>(i, o, rows, (int)width, eps);
+    else row_layernorm_vec_kernel<8><<<grid, 32 * wpb, 0, s>>>(i, o, rows, (int)width, eps);
+    return launch_status("row_layernorm_vec_kernel");
+  }
   if (dtype == HDC_F32)
     row_layernorm_kernel<float><<<grid, 32 * wpb, 0, s>>>(static_cast<const float*>(in), static_cast<float*>(out), rows, (int)width, eps);
   else

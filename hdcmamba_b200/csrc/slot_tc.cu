@@ -128,21 +128,26 @@ __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float*
 
 // ---------------------------------------------------------------------------------
 // Pass A: per-segment local state Rseg = sum_m (prod_{m'>m} gC_m') U_m and Dseg = prod gC_m
+// 16 warps; K and V of the next two chunks are in flight (two-stage TMA ring) while the
+// current chunk is prepared and multiplied.  Warp w reads U rows (quarter w & 3) and the
+// 16 columns [16 (w >> 2), +16) and keeps that part of R in registers.
 // ---------------------------------------------------------------------------------
+constexpr int kStateThreads = 512;
+
 template <int CT, bool PERSTEP>
-__global__ void __launch_bounds__(128, 3)
+__global__ void __launch_bounds__(kStateThreads, 1)
     slot_tc_state_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
                          SlotTcParams p) {
-  constexpr int NT = 128;
+  constexpr int NT = kStateThreads;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
-  uint8_t* sK = base;
-  uint8_t* sV = sK + CT * 128;
-  float* sTab = reinterpret_cast<float*>(sV + CT * 128);   // [CT + 4]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + CT + 4);
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 2);
+  // stage st: K at base + st * 2 * CT * 128, V right after it
+  float* sTab = reinterpret_cast<float*>(base + 4 * CT * 128);  // [CT + 4]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + CT + 4);   // [0], [1] stage loads, [2] MMA
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 3);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, cgrp = warp >> 2;
   const int nseg_a = p.nseg_a;
   const int bh = blockIdx.x / nseg_a, seg = blockIdx.x - bh * nseg_a;
   const int b = bh / p.H, h = bh - b * p.H;
@@ -153,8 +158,7 @@ __global__ void __launch_bounds__(128, 3)
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     tma_prefetch_map(&mapK);
     tma_prefetch_map(&mapV);
@@ -167,30 +171,41 @@ __global__ void __launch_bounds__(128, 3)
   __syncthreads();
   tc_fence_after();
   const uint32_t tU = *sTmem;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
   constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
 
-  float R[64];
+  float R[16];
 #pragma unroll
-  for (int e = 0; e < 64; ++e) R[e] = 0.f;
+  for (int e = 0; e < 16; ++e) R[e] = 0.f;
   float D = 1.f;
-  uint32_t tph = 0, mph = 0;
+  uint32_t fph0 = 0, fph1 = 0, mph = 0;
+  int pending = 0;  // thread 0: bit st set while stage st has a load in flight
   bool ok = true;
 
-  auto issue = [&](int n) {
-    mbar_expect_tx(&bars[0], 2 * CT * 128);
-    tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
-    tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
+  auto issue = [&](int n, int st) {
+    uint8_t* sK = base + st * 2 * CT * 128;
+    mbar_expect_tx(&bars[st], 2 * CT * 128);
+    tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[st]);
+    tma_load_3d(sK + CT * 128, &mapV, h * p.hd, n * CT, b, &bars[st]);
+    pending |= 1 << st;
   };
-  if (tid == 0 && n0 < n1) issue(n0);
-  for (int n = n0; n < n1 && ok; ++n) {
-    if (!mbar_wait(&bars[0], tph, 11)) { ok = false; break; }
-    tph ^= 1;
+  if (tid == 0) {
+    if (n0 < n1) issue(n0, 0);
+    if (n0 + 1 < n1) issue(n0 + 1, 1);
+  }
+  for (int n = n0; n < n1; ++n) {
+    const int st = (n - n0) & 1;
+    uint8_t* sK = base + st * 2 * CT * 128;
+    uint8_t* sV = sK + CT * 128;
+    if (!mbar_wait(&bars[st], st ? fph1 : fph0, 11)) { ok = false; break; }
+    if (st) fph1 ^= 1; else fph0 ^= 1;
+    if (tid == 0) pending &= ~(1 << st);
     if (PERSTEP) {
       if (warp == 0) chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
       __syncthreads();
     }
     // k~ = bf16(bf16(phi(k)) * kdec_j) in place; v padding
+#pragma unroll 2
     for (int idx = tid; idx < CT * 8; idx += NT) {
       const int row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
       const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
@@ -211,32 +226,36 @@ __global__ void __launch_bounds__(128, 3)
       for (int kk = 0; kk < CT / 16; ++kk)
         umma_bf16(tU, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024), sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024),
                   idU, kk > 0 ? 1u : 0u);
-      umma_commit(&bars[1]);
+      umma_commit(&bars[2]);
     }
-    if (!mbar_wait(&bars[1], mph, 12)) { ok = false; break; }
+    if (!mbar_wait(&bars[2], mph, 12)) { ok = false; break; }
     mph ^= 1;
     tc_fence_after();
-    if (tid == 0 && n + 1 < n1) issue(n + 1);
+    if (tid == 0 && n + 2 < n1) issue(n + 2, st);  // this stage's product is done
     const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
-    float u[32];
+    float u[16];
+    tmem_ld16(tU + lane_base + cgrp * 16, u);
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      tmem_ld32(tU + lane_base + hf * 32, u);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) R[hf * 32 + e] = R[hf * 32 + e] * gC + u[e];
-    }
+    for (int e = 0; e < 16; ++e) R[e] = R[e] * gC + u[e];
     D *= gC;
+    // every thread's TMEM read (and, per-step, table read) is done before the next
+    // chunk's product or table
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
   }
   if (ok && lane < 16) {
-    const int f = warp * 16 + lane;
-    float* dst = p.Rseg + ((size_t)bh * p.nseg + seg) * 4096 + f * 64;
+    const int f = quarter * 16 + lane;
+    float* dst = p.Rseg + ((size_t)bh * p.nseg + seg) * 4096 + f * 64 + cgrp * 16;
 #pragma unroll
-    for (int e = 0; e < 64; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
+    for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
   }
   if (ok && tid == 0) p.Dseg[(size_t)bh * p.nseg + seg] = D;
+  // after a timed-out wait: let this CTA's own loads in flight land (bounded) before exit
+  if (!ok && tid == 0) {
+    if (pending & 1) mbar_wait(&bars[0], fph0, 13);
+    if (pending & 2) mbar_wait(&bars[1], fph1, 13);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tU, 64);
@@ -269,14 +288,16 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   uint8_t* sK = base;
   uint8_t* sV = sK + CT * 128;
   uint8_t* sQ = sV + CT * 128;
-  uint8_t* sP = sQ + CT * 128;              // [CT/64 atoms][RB rows][128 B]
+  uint8_t* sKt = sQ + CT * 128;             // bf16(phi(K) * kdec) for the state update
+  uint8_t* sP = sKt + CT * 128;             // [CT/64 atoms][RB rows][128 B]
   uint8_t* sR = sP + CT * RB * 2;           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
   float* sGn = sTab + CT + 4;                              // [128] gn weight | bias of this head
   float* sRed = sGn + 128;                                 // [RB][8] GroupNorm partial sums
-  // mbarriers: [0] TMA loads, [1] S (+Yx) products, [2] P.V products, [3] state update.
-  // Each MMA stream has its own barrier and every commit follows a CTA barrier, so no
-  // thread can fall two phases behind on a barrier (which would alias the parity).
+  // mbarriers: [0] K + V loads, [1] S (+Yx, + the state update issued before them)
+  // products, [2] P.V products, [3] Q loads.  Each MMA stream has its own barrier and
+  // every commit follows a CTA barrier, so no thread can fall two phases behind on a
+  // barrier (which would alias the parity).
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + RB * 8);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
 
@@ -358,24 +379,74 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
   constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
 
-  uint32_t tph = 0, sph = 0, pph = 0, uph = 0;
+  uint32_t kph = 0, qph = 0, sph = 0, pph = 0;
+  int pending = 0;  // thread 0: bit 0 K/V loads, bit 1 Q load in flight
   bool ok = true;
-  auto issue = [&](int n) {
-    mbar_expect_tx(&bars[0], 3 * CT * 128);
+  // K and V of a chunk complete one phase of bars[0] (one expect_tx for both); K is issued
+  // once the last S product of the previous chunk is done, V once its last P.V is done.
+  auto issue_k = [&](int n) {
+    mbar_expect_tx(&bars[0], 2 * CT * 128);
     tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
-    tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
-    tma_load_3d(sQ, &mapQ, h * p.hd, n * CT, b, &bars[0]);
+    pending |= 1;
   };
-  if (tid == 0 && n0 < n1) issue(n0);
+  auto issue_v = [&](int n) { tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]); };
+  auto issue_q = [&](int n) {
+    mbar_expect_tx(&bars[3], CT * 128);
+    tma_load_3d(sQ, &mapQ, h * p.hd, n * CT, b, &bars[3]);
+    pending |= 2;
+  };
+  if (tid == 0 && n0 < n1) {
+    issue_k(n0);
+    issue_v(n0);
+    issue_q(n0);
+  }
 
   for (int n = n0; n < n1 && ok; ++n) {
-    if (!mbar_wait(&bars[0], tph, 21)) { ok = false; break; }
-    tph ^= 1;
-    if (PERSTEP && warp == 0)
-      chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
-    prep_tile_u<NT, CT, true>(sK, p.hd, 1.f);
+    if (!mbar_wait(&bars[0], kph, 21) || !mbar_wait(&bars[3], qph, 22)) { ok = false; break; }
+    kph ^= 1;
+    qph ^= 1;
+    if (tid == 0) pending = 0;
+    if (PERSTEP) {
+      if (warp == 0) chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
+      __syncthreads();
+    }
+    // phi(K) in place and k~ = bf16(bf16(phi(k)) * kdec_j) -> sKt in one pass (feature
+    // padding: ones), phi(Q) in place, V padding
+    for (int idx = tid; idx < CT * 8; idx += NT) {
+      const int row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
+      const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
+      float f[8];
+      unpack16<__nv_bfloat16>(reinterpret_cast<const uint4*>(sK)[idx], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = (c0 + e < p.hd) ? bf16_round(phi_fast(f[e])) : 1.f;
+      reinterpret_cast<uint4*>(sK)[idx] = pack16<__nv_bfloat16>(f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= kd;
+      reinterpret_cast<uint4*>(sKt)[idx] = pack16<__nv_bfloat16>(f);
+    }
     prep_tile_u<NT, CT, true>(sQ, p.hd, 1.f);
     if (p.hd < 64) prep_tile_u<NT, CT, false>(sV, p.hd, 0.f);
+    {  // R <- gC * R in TMEM before the update product is issued
+      const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
+#pragma unroll
+      for (int pc = 0; pc < EPW / 16; ++pc) {
+        float r[16];
+        tmem_ld16(tR + e0 + pc * 16, r);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) r[e] *= gC;
+        tmem_st16(tR + e0 + pc * 16, r);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {  // R += k~^T V: completes before the first S commit below arrives
+#pragma unroll
+      for (int kk = 0; kk < CT / 16; ++kk)
+        umma_bf16(tmem + CT + 128, sdesc_sw128(smem_u32(sKt) + kk * 2048, 0, 1024),
+                  sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, 1u);
+    }
 
 #pragma unroll
     for (int rb = 0; rb < NRB; ++rb) {
@@ -415,6 +486,10 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
       if (!mbar_wait(&bars[1], sph, 23)) { ok = false; break; }
       sph ^= 1;
       tc_fence_after();
+      if (rb == NRB - 1 && tid == 0 && n + 1 < n1) {  // Q and K are no longer read
+        issue_q(n + 1);
+        issue_k(n + 1);
+      }
       // P = bf16(mask(S) * decay): this warpgroup's cpw columns of every row -> sP
       {
         float sv[64];
@@ -455,6 +530,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
       if (!mbar_wait(&bars[2], pph, 24)) { ok = false; break; }
       pph ^= 1;
       tc_fence_after();
+      if (rb == NRB - 1 && tid == 0 && n + 1 < n1) issue_v(n + 1);  // V is no longer read
       // epilogue: y = bf16(Yi + qdec_i * Yx), plain or GroupNorm * sigmoid(gate)
       {
         float o[EPW];
@@ -472,7 +548,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 #pragma unroll
           for (int e = 0; e < EPW; ++e) sum += (e0 + e < p.hd) ? o[e] : 0.f;
           if (my_row >= 0) sRed[my_row * 8 + wg] = sum;
-          __syncthreads();
+          named_bar_sync(1 + quarter, NWG * 32);  // the warps holding these rows
           float mean = 0.f;
           if (my_row >= 0) {
 #pragma unroll
@@ -486,7 +562,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
             sq += (e0 + e < p.hd) ? d * d : 0.f;
           }
           if (my_row >= 0) sRed[my_row * 8 + 4 + wg] = sq;
-          __syncthreads();
+          named_bar_sync(1 + quarter, NWG * 32);
           if (my_row >= 0) {
             float ssq = 0.f;
 #pragma unroll
@@ -529,43 +605,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
       tc_fence_after();
     }
     if (!ok) break;
-    // state update: k~ = bf16(phi(k) * kdec_j) in place; R <- gC * R (TMEM); R += k~^T V
-    for (int idx = tid; idx < CT * 8; idx += NT) {
-      const int row = idx >> 3, pc = idx & 7;
-      const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
-      uint4* pk = reinterpret_cast<uint4*>(sK + row * 128 + pc * 16);
-      float f[8];
-      unpack16<__nv_bfloat16>(*pk, f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] *= kd;
-      *pk = pack16<__nv_bfloat16>(f);
-    }
-    {
-      const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
-#pragma unroll
-      for (int pc = 0; pc < EPW / 16; ++pc) {
-        float r[16];
-        tmem_ld16(tR + e0 + pc * 16, r);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) r[e] *= gC;
-        tmem_st16(tR + e0 + pc * 16, r);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0) {
-#pragma unroll
-      for (int kk = 0; kk < CT / 16; ++kk)
-        umma_bf16(tmem + CT + 128, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
-                  sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, 1u);
-      umma_commit(&bars[3]);
-    }
-    if (!mbar_wait(&bars[3], uph, 25)) { ok = false; break; }
-    uph ^= 1;
-    tc_fence_after();
-    if (tid == 0 && n + 1 < n1) issue(n + 1);
+    // R (updated by the product issued after prep, complete since the first S commit) -> sR
 #pragma unroll
     for (int pc = 0; pc < EPW / 16; ++pc) {
       float r[16];
@@ -581,6 +621,11 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+  }
+  // after a timed-out wait: let this CTA's own loads in flight land (bounded) before exit
+  if (!ok && tid == 0) {
+    if (pending & 1) mbar_wait(&bars[0], kph, 26);
+    if (pending & 2) mbar_wait(&bars[3], qph, 27);
   }
   if (ok && seg == p.nseg - 1 && p.state_out) {
 #pragma unroll
@@ -638,9 +683,9 @@ static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, 
 
 static size_t smem_out_bytes(int CT) {
   const int RB = CT < 128 ? CT : 128;
-  return 1024 + 3 * CT * 128 + CT * RB * 2 + 64 * 128 + (CT + 4 + 128 + RB * 8) * 4 + 64;
+  return 1024 + 4 * CT * 128 + CT * RB * 2 + 64 * 128 + (CT + 4 + 128 + RB * 8) * 4 + 64;
 }
-static size_t smem_state_bytes(int CT) { return 1024 + 2 * CT * 128 + (CT + 4) * 4 + 64; }
+static size_t smem_state_bytes(int CT) { return 1024 + 4 * CT * 128 + (CT + 4) * 4 + 64; }
 
 // One output CTA per SM for chunk 128 / 256 (512 TMEM columns), two for chunk 64.
 static void plan_segments(int64_t BH, int N, int C, int* nseg, int* seg_len) {
@@ -698,7 +743,7 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
     p.nseg_a = p.nseg - 1;
     const size_t sm = smem_state_bytes(CT);
     cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), 128, sm, s>>>(mk, mv, p);
+    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), kStateThreads, sm, s>>>(mk, mv, p);
     if (int e = launch_status("slot_tc_state_kernel")) return e;
   }
   const size_t sm = smem_out_bytes(CT);
@@ -746,7 +791,7 @@ static int run_tc_state(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t 
   if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
   const size_t sm = smem_state_bytes(CT);
   cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg), 128, sm, s>>>(mk, mv, p);
+  slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg), kStateThreads, sm, s>>>(mk, mv, p);
   if (int e = launch_status("slot_tc_state_kernel")) return e;
   slot_fold_kernel<<<(unsigned)BH, 256, 0, s>>>(p);
   return launch_status("slot_fold_kernel");

@@ -8,8 +8,9 @@
 //   output:          y_t = bf16( bf16(h_t) + bf16(G_n) * exp(cum_log_t) )
 // These are the reference's rounding points (its three kernels store bf16).
 //
-// Schedule: one CTA per (chunk, batch) with ds*S threads; thread (j, s) scans
-// C/S consecutive steps of channel j.  Segment results are combined through
+// Schedule: one CTA per (chunk, group of 16 channels, batch) with 16*S <= 256 threads;
+// thread (j, s) scans C/S consecutive steps of channel j (16 at C 256), loading them into
+// registers up front.  Segment results are combined through
 // shared memory: (h_s, sum_log_s) with h = h_prev * exp(sum_log_s) + h_s.
 //   pass 1 (hdc_ssm_chunk_stats): chunk statistics -> stats[b, n, 0:2ds]
 //   pass 2 (hdc_ssm_scan_out):    exclusive prefix over all earlier chunks (including
@@ -18,6 +19,7 @@
 #include <mutex>
 
 #include <climits>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -32,51 +34,95 @@ struct SsmParams {
   int blk; int64_t blk_stride;
   void* y; int64_t ysb, yst;
   int L, ds, C, S;
+  int CG;  // channels per CTA (grid.y = ds / CG channel groups)
 };
 
+// Steps of one segment held in registers at a time.  All loads of a tile are issued before
+// any arithmetic, so a segment costs one memory latency per tile instead of one per step.
+constexpr int kTile = 8;
+
+// exp / softplus: the hardware approximations (ex2 / lg2 based, as the reference's Triton
+// kernels use) for bf16 activations; the accurate library functions for fp32.
 template <typename T>
-__device__ __forceinline__ void ssm_step(const T* row, int j, int ds, float A, float& ld, float& u) {
-  const float dt = to_f(row[j]);
-  const float xv = to_f(row[ds + j]);
-  const float bv = to_f(row[2 * ds + j]);
-  const float dts = softplus20(dt);
-  ld = dts * A;
-  u = dts * bv * xv;
+__device__ __forceinline__ float sexp(float x) {
+  if constexpr (std::is_same<T, float>::value) return expf(x);
+  else return __expf(x);
+}
+template <typename T>
+__device__ __forceinline__ float ssoftplus(float x) {
+  if constexpr (std::is_same<T, float>::value) return softplus20(x);
+  else return x > 20.0f ? x : __logf(1.0f + __expf(x));
 }
 
-// per-thread scan of its segment from h = 0; returns (h, sum_log)
 template <typename T>
-__device__ __forceinline__ void ssm_segment(const SsmParams& p, int b, int n, int j, int s, float A,
+__device__ __forceinline__ float ldnc(const T* ptr) {
+  return to_f(__ldg(ptr));
+}
+
+// (log decay, input) of steps [t0, t0 + cnt) of channel j, cnt <= kTile
+template <typename T>
+__device__ __forceinline__ void ssm_tile(const SsmParams& p, const T* base, int j, float A, int cnt, float* ld,
+                                         float* u) {
+  float dt[kTile], xv[kTile], bv[kTile];
+#pragma unroll
+  for (int t = 0; t < kTile; ++t) {
+    if (t < cnt) {
+      const T* row = base + (size_t)t * p.pst;
+      dt[t] = ldnc(row + j);
+      xv[t] = ldnc(row + p.ds + j);
+      bv[t] = ldnc(row + 2 * p.ds + j);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kTile; ++t) {
+    if (t < cnt) {
+      const float dts = ssoftplus<T>(dt[t]);
+      ld[t] = dts * A;
+      u[t] = dts * bv[t] * xv[t];
+    }
+  }
+}
+
+// per-thread scan of its segment from h = 0: (h, sum_log).  With a segment of at most
+// kTile steps, ld / u keep the whole segment for the output pass.
+template <typename T>
+__device__ __forceinline__ void ssm_segment(const SsmParams& p, const T* base, int j, float A, float* ld, float* u,
                                             float& h, float& sl) {
   const int seglen = p.C / p.S;
-  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)(n * p.C + s * seglen) * p.pst;
   h = 0.f;
   sl = 0.f;
-  for (int t = 0; t < seglen; ++t) {
-    float ld, u;
-    ssm_step<T>(base + (size_t)t * p.pst, j, p.ds, A, ld, u);
-    sl += ld;
-    h = h * expf(ld) + u;
+  for (int t0 = 0; t0 < seglen; t0 += kTile) {
+    const int cnt = min(kTile, seglen - t0);
+    ssm_tile<T>(p, base + (size_t)t0 * p.pst, j, A, cnt, ld, u);
+#pragma unroll
+    for (int t = 0; t < kTile; ++t) {
+      if (t < cnt) {
+        sl += ld[t];
+        h = h * sexp<T>(ld[t]) + u[t];
+      }
+    }
   }
 }
 
 template <typename T>
-__global__ void ssm_chunk_stats_kernel(SsmParams p) {
-  extern __shared__ float sh[];  // [2][S][ds]
-  const int n = blockIdx.x, b = blockIdx.y;
-  const int j = threadIdx.x % p.ds, s = threadIdx.x / p.ds;
+__global__ void __launch_bounds__(256) ssm_chunk_stats_kernel(SsmParams p) {
+  extern __shared__ float sh[];  // [2][S][CG]
+  const int n = blockIdx.x, b = blockIdx.z;
+  const int jl = threadIdx.x % p.CG, s = threadIdx.x / p.CG, j = blockIdx.y * p.CG + jl;
   const int N = p.L / p.C;
   const float A = -expf(to_f(static_cast<const T*>(p.A_log)[j]));
-  float h, sl;
-  ssm_segment<T>(p, b, n, j, s, A, h, sl);
-  sh[s * p.ds + j] = h;
-  sh[(p.S + s) * p.ds + j] = sl;
+  const int seglen = p.C / p.S;
+  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)(n * p.C + s * seglen) * p.pst;
+  float ld[kTile], u[kTile], h, sl;
+  ssm_segment<T>(p, base, j, A, ld, u, h, sl);
+  sh[s * p.CG + jl] = h;
+  sh[(p.S + s) * p.CG + jl] = sl;
   __syncthreads();
   if (s == 0) {
     float hc = 0.f, lc = 0.f;
     for (int q = 0; q < p.S; ++q) {
-      hc = hc * expf(sh[(p.S + q) * p.ds + j]) + sh[q * p.ds + j];
-      lc += sh[(p.S + q) * p.ds + j];
+      hc = hc * sexp<T>(sh[(p.S + q) * p.CG + jl]) + sh[q * p.CG + jl];
+      lc += sh[(p.S + q) * p.CG + jl];
     }
     float* st = p.stats_w + ((size_t)b * N + n) * 2 * p.ds;
     st[j] = bf16_round(hc);
@@ -85,13 +131,21 @@ __global__ void ssm_chunk_stats_kernel(SsmParams p) {
 }
 
 template <typename T>
-__global__ void ssm_scan_out_kernel(SsmParams p) {
-  extern __shared__ float sh[];  // [2][S][ds] + [ds] prefix
-  const int n = blockIdx.x, b = blockIdx.y;
-  const int j = threadIdx.x % p.ds, s = threadIdx.x / p.ds;
+__global__ void __launch_bounds__(256) ssm_scan_out_kernel(SsmParams p) {
+  extern __shared__ float sh[];  // [2][S][CG] + [CG] prefix
+  const int n = blockIdx.x, b = blockIdx.z;
+  const int jl = threadIdx.x % p.CG, s = threadIdx.x / p.CG, j = blockIdx.y * p.CG + jl;
   const float A = -expf(to_f(static_cast<const T*>(p.A_log)[j]));
-  float* shG = sh + 2 * p.S * p.ds;
+  float* shG = sh + 2 * p.S * p.CG;
+  const int seglen = p.C / p.S;
+  const int t0 = n * p.C + s * seglen;
+  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)t0 * p.pst;
 
+  // this thread's segment first (its loads overlap the prefix below)
+  float ld[kTile], u[kTile], h, sl;
+  ssm_segment<T>(p, base, j, A, ld, u, h, sl);
+  sh[s * p.CG + jl] = h;
+  sh[(p.S + s) * p.CG + jl] = sl;
   // exclusive prefix over chunks [0, n_prev + n) -- fp32, sequential (the reference order)
   if (s == 0) {
     const int m_end = p.n_prev + n;
@@ -99,42 +153,47 @@ __global__ void ssm_scan_out_kernel(SsmParams p) {
     for (int m0 = 0, blkno = 0; m0 < m_end; ++blkno) {
       const float* st = p.stats_r + (size_t)blkno * p.blk_stride + (size_t)b * p.stats_sb;
       const int m1 = min(m_end - m0, p.blk);
+#pragma unroll 4
       for (int m = 0; m < m1; ++m)
-        G = G * expf(st[(size_t)m * 2 * p.ds + p.ds + j]) + st[(size_t)m * 2 * p.ds + j];
+        G = G * sexp<T>(st[(size_t)m * 2 * p.ds + p.ds + j]) + st[(size_t)m * 2 * p.ds + j];
       m0 += m1;
     }
-    shG[j] = bf16_round(G);
+    shG[jl] = bf16_round(G);
   }
-  float h, sl;
-  ssm_segment<T>(p, b, n, j, s, A, h, sl);
-  sh[s * p.ds + j] = h;
-  sh[(p.S + s) * p.ds + j] = sl;
   __syncthreads();
   // carry-in from earlier segments of this chunk
   float hin = 0.f, cum = 0.f;
   for (int q = 0; q < s; ++q) {
-    hin = hin * expf(sh[(p.S + q) * p.ds + j]) + sh[q * p.ds + j];
-    cum += sh[(p.S + q) * p.ds + j];
+    hin = hin * sexp<T>(sh[(p.S + q) * p.CG + jl]) + sh[q * p.CG + jl];
+    cum += sh[(p.S + q) * p.CG + jl];
   }
-  const float G = shG[j];
-  const int seglen = p.C / p.S;
-  const int t0 = n * p.C + s * seglen;
-  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)t0 * p.pst;
+  const float G = shG[jl];
   T* yb = static_cast<T*>(p.y) + (size_t)b * p.ysb + (size_t)t0 * p.yst;
   float hh = hin;
-  for (int t = 0; t < seglen; ++t) {
-    float ld, u;
-    ssm_step<T>(base + (size_t)t * p.pst, j, p.ds, A, ld, u);
-    cum += ld;
-    hh = hh * expf(ld) + u;
-    const float yv = bf16_round(bf16_round(hh) + G * expf(cum));
-    yb[(size_t)t * p.yst + j] = from_f<T>(yv);
+  for (int tb = 0; tb < seglen; tb += kTile) {
+    const int cnt = min(kTile, seglen - tb);
+    if (seglen > kTile) ssm_tile<T>(p, base + (size_t)tb * p.pst, j, A, cnt, ld, u);
+#pragma unroll
+    for (int t = 0; t < kTile; ++t) {
+      if (t < cnt) {
+        cum += ld[t];
+        hh = hh * sexp<T>(ld[t]) + u[t];
+        const float yv = bf16_round(bf16_round(hh) + G * sexp<T>(cum));
+        yb[(size_t)(tb + t) * p.yst + j] = from_f<T>(yv);
+      }
+    }
   }
 }
 
+// Channels per CTA: 16, so a chunk's channels spread over ds / 16 CTAs (one CTA per chunk
+// is instruction-bound on a single SM: softplus and exp for every step of every channel).
+static int ssm_group(int ds) { return ds < 16 ? ds : 16; }
+
+// Segments per chunk: steps of C / S per thread, at least 4, at most 256 threads per CTA.
 static int ssm_segments(int ds, int C) {
+  const int cg = ssm_group(ds);
   int S = 1;
-  while (S * 2 * ds <= 512 && C % (S * 2) == 0 && C / (S * 2) >= 4) S *= 2;
+  while (S * 2 * cg <= 256 && C % (S * 2) == 0 && C / (S * 2) >= 4) S *= 2;
   return S;
 }
 
@@ -158,12 +217,12 @@ extern "C" int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb
   if (!stats) return fail(HDC_E_NULL, "ssm: null stats");
   SsmParams p{};
   p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_w = stats;
-  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C);
-  dim3 grid((unsigned)(L / C), (unsigned)B);
-  const size_t smem = 2 * p.S * ds * sizeof(float);
+  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C); p.CG = ssm_group((int)ds);
+  dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
+  const size_t smem = 2 * p.S * p.CG * sizeof(float);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) ssm_chunk_stats_kernel<float><<<grid, p.S * ds, smem, s>>>(p);
-  else ssm_chunk_stats_kernel<__nv_bfloat16><<<grid, p.S * ds, smem, s>>>(p);
+  if (dtype == HDC_F32) ssm_chunk_stats_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
+  else ssm_chunk_stats_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
   return launch_status("ssm_chunk_stats_kernel");
 }
 
@@ -177,12 +236,12 @@ static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, in
   p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_r = stats;
   p.stats_sb = stats_sb; p.n_prev = (int)n_prev; p.y = y; p.ysb = y_sb; p.yst = y_st;
   p.blk = (int)blk; p.blk_stride = blk_stride;
-  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C);
-  dim3 grid((unsigned)(L / C), (unsigned)B);
-  const size_t smem = (2 * p.S + 1) * ds * sizeof(float);
+  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C); p.CG = ssm_group((int)ds);
+  dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
+  const size_t smem = (2 * p.S + 1) * p.CG * sizeof(float);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) ssm_scan_out_kernel<float><<<grid, p.S * ds, smem, s>>>(p);
-  else ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * ds, smem, s>>>(p);
+  if (dtype == HDC_F32) ssm_scan_out_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
+  else ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
   return launch_status("ssm_scan_out_kernel");
 }
 

@@ -78,6 +78,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int cod
 }
 
 // ---------------------------------------------------------------- fences
+// Named barrier `id` (1..15; 0 is __syncthreads) over `nthreads` threads (a multiple of 32),
+// all of which execute it.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -188,9 +188,14 @@ def test_gate_shipped_golden(tag):
 
 
 @pytest.mark.parametrize("rows,width,dtype", [(1000, 832, torch.bfloat16), (77, 320, torch.float32),
-                                              (4096, 1152, torch.bfloat16)])
+                                              (4096, 1152, torch.bfloat16), (300, 100, torch.bfloat16),
+                                              (33, 2048, torch.bfloat16)])
 def test_row_layernorm(rows, width, dtype):
+    """Vectorized path (bf16, width % 8 == 0, <= 2048) and the scalar one (the others)."""
     x = (3 * torch.randn(rows, width, generator=gen(40)) + 1).to(dtype)
     y = ops.row_layernorm(x.to(DEV))
     ref = torch.nn.functional.layer_norm(x.float(), (width,)).to(dtype)
     assert rel(y, ref) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
+    xi = x.to(DEV)
+    ops.row_layernorm(xi, out=xi)  # in place, as the Block runs it
+    assert torch.equal(xi, y)
