@@ -76,6 +76,19 @@ __device__ __forceinline__ uint4 ldg16(const void* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
+// ldg16 when `pred`, zeros otherwise, as one predicated load: the caller does not wait
+// for the data until it first uses it (a select on the loaded value would).
+__device__ __forceinline__ uint4 ldg16_pred(const void* p, bool pred) {
+  uint4 r;
+  asm volatile(
+      "{\n\t.reg .pred q;\n\t"
+      "setp.ne.b32 q, %5, 0;\n\t"
+      "mov.b32 %0, 0;\n\tmov.b32 %1, 0;\n\tmov.b32 %2, 0;\n\tmov.b32 %3, 0;\n\t"
+      "@q ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n\t}"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p), "r"((int)pred));
+  return r;
+}
 __device__ __forceinline__ void stg16(void* p, const uint4& v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};"
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");

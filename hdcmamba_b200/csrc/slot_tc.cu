@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kStateThreads, 1)
     const int st = (n - n0) & 1;
     uint8_t* sK = base + st * 2 * CT * 128;
     uint8_t* sV = sK + CT * 128;
-    if (!mbar_wait(&bars[st], st ? fph1 : fph0, 11)) { ok = false; break; }
+    if (!mbar_wait_warp(&bars[st], st ? fph1 : fph0, 11)) { ok = false; break; }
     if (st) fph1 ^= 1; else fph0 ^= 1;
     if (tid == 0) pending &= ~(1 << st);
     if (PERSTEP) {
@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(kStateThreads, 1)
                   idU, kk > 0 ? 1u : 0u);
       umma_commit(&bars[2]);
     }
-    if (!mbar_wait(&bars[2], mph, 12)) { ok = false; break; }
+    if (!mbar_wait_warp(&bars[2], mph, 12)) { ok = false; break; }
     mph ^= 1;
     tc_fence_after();
     if (tid == 0 && n + 2 < n1) issue(n + 2, st);  // this stage's product is done
@@ -263,18 +263,35 @@ __global__ void __launch_bounds__(kStateThreads, 1)
 
 // ---------------------------------------------------------------------------------
 // Pass B: outputs.  NWG warpgroups (NWG*128 threads); all of them cover every TMEM lane
-// (row) and split the columns: S columns of the current row block, the 64 columns of
-// the Yi / Yx / R accumulators.  Each row block needs one S MMA group (N up to 256) and
-// one P.V MMA group, so a chunk takes 2 * (C / 128) + 1 tensor-core round trips.
+// (row) and split the columns.  Both row blocks of a chunk go through the tensor cores
+// together, so a chunk takes two round trips:
+//   1. S_rb = phi(Q_rb) phi(K[0:ncol_rb])^T for every row block rb (causal columns only);
+//   2. Yi_rb = P_rb V, Yx_rb = phi(Q_rb) bf16(R) and the state update R += k~^T V.
+// With 128-row blocks Yi / Yx reuse the S columns of their block once P is read out.
+// The fp32 state R stays in registers (R <- gC R + U after round 2); while round 1 runs
+// the threads fetch the gate; the next chunk's loads start as soon as round 2 completes.
 // ---------------------------------------------------------------------------------
 template <int CT>
 struct OutCfg {
-  static constexpr int RB = CT < 128 ? CT : 128;                 // rows per block (MMA M)
-  static constexpr int NWG = CT == 64 ? 2 : 4;                   // warpgroups
+  static constexpr int RB = CT < 128 ? CT : 128;        // rows per block (MMA M)
+  static constexpr int NRB = CT / RB;                    // row blocks per chunk
+  static constexpr int NWG = CT == 64 ? 2 : 4;           // warpgroups
   static constexpr int NT = NWG * 128;
-  static constexpr int TMEM_COLS = CT == 64 ? 256 : 512;         // S (CT) + Yi + Yx + R (64 each)
-  static constexpr int EPW = 64 / NWG;                           // accumulator columns per warpgroup
-  static constexpr int MINB = CT == 64 ? 2 : 1;                  // resident CTAs per SM
+  static constexpr int EPW = 64 / NWG;                   // accumulator columns per warpgroup
+  static constexpr int MINB = CT == 64 ? 2 : 1;          // resident CTAs per SM
+  static constexpr bool INPLACE = RB == 128;             // Yi / Yx inside the S columns
+  static constexpr int ncol(int rb) { return (rb + 1) * RB; }      // S columns of block rb
+  static constexpr int scol(int rb) { return rb == 0 ? 0 : ncol(0); }
+  static constexpr int SCOLS = NRB == 1 ? ncol(0) : ncol(0) + ncol(1);
+  static constexpr int yi(int rb) { return INPLACE ? scol(rb) : SCOLS; }
+  static constexpr int yx(int rb) { return INPLACE ? scol(rb) + 64 : SCOLS + 64; }
+  static constexpr int RCOL = INPLACE ? SCOLS : SCOLS + 128;      // U = k~^T V (64 columns)
+  static constexpr int TMEM_COLS = RCOL + 64 <= 256 ? 256 : 512;
+  static constexpr int pbase(int rb) { return rb == 0 ? 0 : RB * ncol(0) * 2; }  // bytes into sP
+  static constexpr int PBYTES = NRB == 1 ? RB * ncol(0) * 2 : RB * (ncol(0) + ncol(1)) * 2;
+  static constexpr int NCHUNK = SCOLS / 32;              // 32-column pieces of S / P
+  static constexpr int CPW = NCHUNK / NWG;               // pieces per warpgroup
+  static_assert(CPW * NWG == NCHUNK, "S pieces must split evenly over the warpgroups");
 };
 
 template <int CT, bool PERSTEP, bool GATE>
@@ -282,23 +299,21 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     slot_tc_out_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                        const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
   using Cfg = OutCfg<CT>;
-  constexpr int NT = Cfg::NT, RB = Cfg::RB, NRB = CT / RB, NWG = Cfg::NWG, EPW = Cfg::EPW;
+  constexpr int NT = Cfg::NT, RB = Cfg::RB, NRB = Cfg::NRB, NWG = Cfg::NWG, EPW = Cfg::EPW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
-  uint8_t* sK = base;
+  uint8_t* sK = base;                       // phi(K), then k~ = bf16(phi(K) * kdec) in place
   uint8_t* sV = sK + CT * 128;
   uint8_t* sQ = sV + CT * 128;
-  uint8_t* sKt = sQ + CT * 128;             // bf16(phi(K) * kdec) for the state update
-  uint8_t* sP = sKt + CT * 128;             // [CT/64 atoms][RB rows][128 B]
-  uint8_t* sR = sP + CT * RB * 2;           // [64 rows][128 B], MN-major bf16 R
+  uint8_t* sP = sQ + CT * 128;              // per row block: [ncol/64 atoms][RB rows][128 B]
+  uint8_t* sR = sP + Cfg::PBYTES;           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
   float* sGn = sTab + CT + 4;                              // [128] gn weight | bias of this head
-  float* sRed = sGn + 128;                                 // [RB][8] GroupNorm partial sums
-  // mbarriers: [0] K + V loads, [1] S (+Yx, + the state update issued before them)
-  // products, [2] P.V products, [3] Q loads.  Each MMA stream has its own barrier and
-  // every commit follows a CTA barrier, so no thread can fall two phases behind on a
+  float* sRed = sGn + 128;                                 // [CT][8] GroupNorm partial sums
+  // mbarriers: [0] K + V loads, [1] S products, [2] P.V / Yx / state products, [3] Q loads.
+  // Each commit follows a CTA barrier, so no thread can fall two phases behind on a
   // barrier (which would alias the parity).
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + RB * 8);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * 8);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -306,8 +321,10 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   const int bh = blockIdx.x / p.nseg, seg = blockIdx.x - bh * p.nseg;
   const int b = bh / p.H, h = bh - b * p.H;
   const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
-  // accumulator row held by this thread (M=64 accumulators: lanes 0-15 of each quarter)
+  // accumulator row (within a row block) held by this thread (M=64: lanes 0-15 of a quarter)
   const int my_row = (RB == 128) ? quarter * 32 + lane : (lane < 16 ? quarter * 16 + lane : -1);
+  const int row_lo = (RB == 128) ? quarter * 32 : quarter * 16;   // rows of this warp
+  const int row_hi = row_lo + (RB == 128 ? 31 : 15);
   const bool f_valid = lane < 16;  // holds row f_row of the M=64 state R
   const int f_row = quarter * 16 + lane;
   const int e0 = wg * EPW;         // this thread's accumulator columns [e0, e0 + EPW)
@@ -339,12 +356,16 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   tc_fence_after();
   const uint32_t tmem = *sTmem;
   const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-  const uint32_t tS = tmem + lane_base, tYi = tS + CT, tYx = tS + CT + 64, tR = tS + CT + 128;
+  const uint32_t tL = tmem + lane_base;    // this warp's TMEM lanes, column 0
+  const uint32_t tR = tL + Cfg::RCOL;
 
-  // entering state: state_in folded with the earlier segments' local states -> TMEM + sR
+  // entering state: state_in, then earlier sequence parts, then the earlier segments'
+  // local states, folded -> registers (fp32 R: lanes < 16 hold row f_row, columns
+  // [e0, e0 + EPW)) + sR (bf16)
+  float Rr[EPW];
 #pragma unroll
   for (int pc = 0; pc < EPW / 16; ++pc) {
-    float Rp[16];
+    float* Rp = Rr + pc * 16;
 #pragma unroll
     for (int e = 0; e < 16; ++e) Rp[e] = 0.f;
     const int c0 = e0 + pc * 16;
@@ -370,7 +391,6 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
       for (int c = 0; c < 2; ++c)
         *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (c0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rp[c * 8]);
     }
-    tmem_st16(tR + c0, Rp);
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -382,27 +402,18 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   uint32_t kph = 0, qph = 0, sph = 0, pph = 0;
   int pending = 0;  // thread 0: bit 0 K/V loads, bit 1 Q load in flight
   bool ok = true;
-  // K and V of a chunk complete one phase of bars[0] (one expect_tx for both); K is issued
-  // once the last S product of the previous chunk is done, V once its last P.V is done.
-  auto issue_k = [&](int n) {
+  auto issue = [&](int n) {
     mbar_expect_tx(&bars[0], 2 * CT * 128);
     tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
-    pending |= 1;
-  };
-  auto issue_v = [&](int n) { tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]); };
-  auto issue_q = [&](int n) {
+    tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
     mbar_expect_tx(&bars[3], CT * 128);
     tma_load_3d(sQ, &mapQ, h * p.hd, n * CT, b, &bars[3]);
-    pending |= 2;
+    pending = 3;
   };
-  if (tid == 0 && n0 < n1) {
-    issue_k(n0);
-    issue_v(n0);
-    issue_q(n0);
-  }
+  if (tid == 0 && n0 < n1) issue(n0);
 
   for (int n = n0; n < n1 && ok; ++n) {
-    if (!mbar_wait(&bars[0], kph, 21) || !mbar_wait(&bars[3], qph, 22)) { ok = false; break; }
+    if (!mbar_wait_warp(&bars[0], kph, 21) || !mbar_wait_warp(&bars[3], qph, 22)) { ok = false; break; }
     kph ^= 1;
     qph ^= 1;
     if (tid == 0) pending = 0;
@@ -410,211 +421,227 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
       if (warp == 0) chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
       __syncthreads();
     }
-    // phi(K) in place and k~ = bf16(bf16(phi(k)) * kdec_j) -> sKt in one pass (feature
-    // padding: ones), phi(Q) in place, V padding
+    // phi in place (feature padding: ones for q / k, zeros for v)
+    prep_tile_u<NT, CT, true>(sK, p.hd, 1.f);
+    prep_tile_u<NT, CT, true>(sQ, p.hd, 1.f);
+    if (p.hd < 64) prep_tile_u<NT, CT, false>(sV, p.hd, 0.f);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // ---- round 1: S of every row block
+    if (tid == 0) {
+#pragma unroll
+      for (int rb = 0; rb < NRB; ++rb) {
+        const uint32_t aq = smem_u32(sQ) + rb * RB * 128;
+        const uint32_t idS = idesc_bf16_f32(RB, Cfg::ncol(rb), false, false);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_bf16(tmem + Cfg::scol(rb), sdesc_sw128(aq + k * 32, 16, 1024),
+                    sdesc_sw128(smem_u32(sK) + k * 32, 16, 1024), idS, k > 0 ? 1u : 0u);
+      }
+      umma_commit(&bars[1]);
+    }
+    // meanwhile: this thread's gate values
+    uint4 graw[NRB][EPW / 8];
+    if (GATE) {
+#pragma unroll
+      for (int rb = 0; rb < NRB; ++rb) {
+        const int t_row = n * CT + rb * RB + (my_row >= 0 ? my_row : 0);
+        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) + (size_t)b * p.g_sb +
+                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + e0;
+#pragma unroll
+        for (int c = 0; c < EPW / 8; ++c)
+          graw[rb][c] = ldg16_pred(gp + c * 8, my_row >= 0 && e0 + c * 8 < p.hd);
+      }
+    }
+    if (!mbar_wait_warp(&bars[1], sph, 23)) { ok = false; break; }
+    sph ^= 1;
+    tc_fence_after();
+    // k~ = bf16(phi(k) * kdec_j) in place (the S products no longer read sK)
     for (int idx = tid; idx < CT * 8; idx += NT) {
-      const int row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
+      const int row = idx >> 3;
       const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
       float f[8];
       unpack16<__nv_bfloat16>(reinterpret_cast<const uint4*>(sK)[idx], f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = (c0 + e < p.hd) ? bf16_round(phi_fast(f[e])) : 1.f;
-      reinterpret_cast<uint4*>(sK)[idx] = pack16<__nv_bfloat16>(f);
-#pragma unroll
       for (int e = 0; e < 8; ++e) f[e] *= kd;
-      reinterpret_cast<uint4*>(sKt)[idx] = pack16<__nv_bfloat16>(f);
+      reinterpret_cast<uint4*>(sK)[idx] = pack16<__nv_bfloat16>(f);
     }
-    prep_tile_u<NT, CT, true>(sQ, p.hd, 1.f);
-    if (p.hd < 64) prep_tile_u<NT, CT, false>(sV, p.hd, 0.f);
-    {  // R <- gC * R in TMEM before the update product is issued
-      const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
+    // P = bf16(mask(S) * decay): this warpgroup's 32-column pieces of S -> sP
 #pragma unroll
-      for (int pc = 0; pc < EPW / 16; ++pc) {
-        float r[16];
-        tmem_ld16(tR + e0 + pc * 16, r);
+    for (int cc = 0; cc < Cfg::CPW; ++cc) {
+      const int c = wg * Cfg::CPW + cc;
+      const int rb = (NRB == 2 && c * 32 >= Cfg::ncol(0)) ? 1 : 0;
+      const int j0 = c * 32 - (rb ? Cfg::ncol(0) : 0);           // first column of the piece
+      const int ib = rb * RB;                                     // first row of the block
+      uint8_t* pb = sP + Cfg::pbase(rb);
+      if (j0 > ib + row_hi) {  // above the diagonal for every row of this warp: zeros
+        if (my_row >= 0) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) r[e] *= gC;
-        tmem_st16(tR + e0 + pc * 16, r);
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(pb + ((j0 + q * 8) >> 6) * (RB * 128) +
+                                      sw128_chunk(my_row, ((j0 + q * 8) & 63) >> 3)) = make_uint4(0, 0, 0, 0);
+        }
+        continue;
+      }
+      float sv[32];
+      tmem_ld32(tL + Cfg::scol(rb) + j0, sv);
+      if (my_row < 0) continue;
+      const int i = ib + my_row;
+      const bool full = j0 + 31 <= ib + row_lo;  // no masking for any row of this warp
+      const float ci = PERSTEP ? sTab[i] : 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[8];
+        if (!PERSTEP && full) {
+          // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e
+          const float rf = sTab[i - j0 - q * 8 - 7];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = sv[q * 8 + e] * (rf * sTab[7 - e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int j = j0 + q * 8 + e;
+            float dm = 0.f;
+            if (j <= i) dm = PERSTEP ? fast_exp(ci - sTab[j]) : sTab[i - j];
+            v[e] = (j <= i) ? sv[q * 8 + e] * dm : 0.f;
+          }
+        }
+        const int jq = j0 + q * 8;
+        *reinterpret_cast<uint4*>(pb + (jq >> 6) * (RB * 128) + sw128_chunk(my_row, (jq & 63) >> 3)) =
+            pack16<__nv_bfloat16>(v);
       }
     }
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (tid == 0) {  // R += k~^T V: completes before the first S commit below arrives
+    // ---- round 2: Yi = P V, Yx = phi(Q) bf16(R) per row block; U = k~^T V
+    if (tid == 0) {
 #pragma unroll
-      for (int kk = 0; kk < CT / 16; ++kk)
-        umma_bf16(tmem + CT + 128, sdesc_sw128(smem_u32(sKt) + kk * 2048, 0, 1024),
-                  sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, 1u);
+      for (int rb = 0; rb < NRB; ++rb) {
+        const uint32_t ap = smem_u32(sP + Cfg::pbase(rb));
+        for (int kk = 0; kk < Cfg::ncol(rb) / 16; ++kk)
+          umma_bf16(tmem + Cfg::yi(rb), sdesc_sw128(ap + ((kk * 16) >> 6) * (RB * 128) + ((kk * 16) & 63) * 2, 16, 1024),
+                    sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, kk > 0 ? 1u : 0u);
+        const uint32_t aq = smem_u32(sQ) + rb * RB * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_bf16(tmem + Cfg::yx(rb), sdesc_sw128(aq + k * 32, 16, 1024),
+                    sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV, k > 0 ? 1u : 0u);
+      }
+#pragma unroll
+      for (int kk = 0; kk < CT / 16; ++kk)  // U = k~^T V
+        umma_bf16(tmem + Cfg::RCOL, sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
+                  sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, kk > 0 ? 1u : 0u);
+      umma_commit(&bars[2]);
     }
-
+    if (!mbar_wait_warp(&bars[2], pph, 24)) { ok = false; break; }
+    pph ^= 1;
+    tc_fence_after();
+    if (tid == 0 && n + 1 < n1) issue(n + 1);  // every buffer of this chunk is free
+    // ---- epilogue: y = bf16(Yi + qdec_i * Yx), plain or GroupNorm * sigmoid(gate)
+    float o[NRB][EPW];
 #pragma unroll
     for (int rb = 0; rb < NRB; ++rb) {
-      if (!ok) break;
-      const int r0 = rb * RB;
-      const int nrb = (RB == 128) ? min(CT, r0 + RB) : CT;  // S columns needed by this row block
-      const int cpw = nrb / NWG;                             // S columns per warpgroup (32 or 64)
-      const int i_row = r0 + (my_row >= 0 ? my_row : 0);
-      const int t_row = n * CT + i_row;
-      uint4 graw[EPW / 8];
-      if (GATE) {  // gate values of this thread's row and columns, loaded early
-        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) + (size_t)b * p.g_sb +
-                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + e0;
+      const int i_row = rb * RB + (my_row >= 0 ? my_row : 0);
+      const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
 #pragma unroll
-        for (int c = 0; c < EPW / 8; ++c)
-          graw[c] = (my_row >= 0 && e0 + c * 8 < p.hd) ? ldg16(gp + c * 8) : make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      if (tid == 0) {
-        const uint32_t aq = smem_u32(sQ) + r0 * 128;
-        // Yx = phi(Q) bf16(R) (B = R rows f, e contiguous: MN-major)
+      for (int pc = 0; pc < EPW / 16; ++pc) {
+        float yi[16], yx[16];
+        tmem_ld16x2(tL + Cfg::yi(rb) + e0 + pc * 16, tL + Cfg::yx(rb) + e0 + pc * 16, yi, yx);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_bf16(tmem + CT + 64, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024),
-                    idPV, k > 0 ? 1u : 0u);
-        // S = phi(Q_blk) phi(K[0:nrb])^T
-        const uint32_t idS = idesc_bf16_f32(RB, nrb, false, false);
+        for (int e = 0; e < 16; ++e) o[rb][pc * 16 + e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is bf16
+      }
+    }
+    if (GATE) {
+      float mean[NRB];
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_bf16(tmem, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sK) + k * 32, 16, 1024), idS,
-                    k > 0 ? 1u : 0u);
-        umma_commit(&bars[1]);
+      for (int rb = 0; rb < NRB; ++rb) {
+        float sum = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPW; ++e) sum += (e0 + e < p.hd) ? o[rb][e] : 0.f;
+        if (my_row >= 0) sRed[(rb * RB + my_row) * 8 + wg] = sum;
       }
-      if (!mbar_wait(&bars[1], sph, 23)) { ok = false; break; }
-      sph ^= 1;
-      tc_fence_after();
-      if (rb == NRB - 1 && tid == 0 && n + 1 < n1) {  // Q and K are no longer read
-        issue_q(n + 1);
-        issue_k(n + 1);
-      }
-      // P = bf16(mask(S) * decay): this warpgroup's cpw columns of every row -> sP
-      {
-        float sv[64];
-        const int jb = wg * cpw;
-        if (cpw == 64) tmem_ld32x2(tS + jb, tS + jb + 32, sv, sv + 32);
-        else tmem_ld32(tS + jb, sv);
+      named_bar_sync(1 + quarter, NWG * 32);  // the warps holding these rows
+#pragma unroll
+      for (int rb = 0; rb < NRB; ++rb) {
+        mean[rb] = 0.f;
         if (my_row >= 0) {
-          const int i = r0 + my_row;
-          const float ci = PERSTEP ? sTab[i] : 0.f;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (q * 8 >= cpw) break;
-            float v[8];
+          for (int w = 0; w < NWG; ++w) mean[rb] += sRed[(rb * RB + my_row) * 8 + w];
+          mean[rb] *= fast_rcp((float)p.hd);
+        }
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPW; ++e) {
+          const float d = o[rb][e] - mean[rb];
+          sq += (e0 + e < p.hd) ? d * d : 0.f;
+        }
+        if (my_row >= 0) sRed[(rb * RB + my_row) * 8 + 4 + wg] = sq;
+      }
+      named_bar_sync(1 + quarter, NWG * 32);
+      if (my_row >= 0) {
+#pragma unroll
+        for (int rb = 0; rb < NRB; ++rb) {
+          float ssq = 0.f;
+#pragma unroll
+          for (int w = 0; w < NWG; ++w) ssq += sRed[(rb * RB + my_row) * 8 + 4 + w];
+          // the reference's padded lanes (block width 64) add (64 - hd) * mean^2
+          const float var = (ssq + (float)(64 - p.hd) * mean[rb] * mean[rb]) / (float)p.hd;
+          const float inv = rsqrtf(var + 1e-5f);
+          const int t_row = n * CT + rb * RB + my_row;
+          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                              (size_t)t_row * p.y_st + e0;
+#pragma unroll
+          for (int c = 0; c < EPW / 8; ++c) {
+            if (e0 + c * 8 >= p.hd) continue;
+            float g[8], r[8];
+            unpack16<__nv_bfloat16>(graw[rb][c], g);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const int j = jb + q * 8 + e;
-              float dm = 0.f;
-              if (j <= i) dm = PERSTEP ? fast_exp(ci - sTab[j]) : sTab[i - j];
-              v[e] = (j <= i) ? sv[q * 8 + e] * dm : 0.f;
+              const int d = e0 + c * 8 + e;
+              const float ygn = ((o[rb][c * 8 + e] - mean[rb]) * inv) * sGn[d] + sGn[64 + d];
+              r[e] = ygn * fast_sigmoid(g[e]);
             }
-            const int j0 = jb + q * 8;
-            *reinterpret_cast<uint4*>(sP + (j0 >> 6) * (RB * 128) + sw128_chunk(my_row, (j0 & 63) >> 3)) =
-                pack16<__nv_bfloat16>(v);
+            stg16(op + c * 8, pack16<__nv_bfloat16>(r));
           }
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
-      if (tid == 0) {
-        for (int kk = 0; kk < nrb / 16; ++kk)
-          umma_bf16(tmem + CT,
-                    sdesc_sw128(smem_u32(sP) + ((kk * 16) >> 6) * (RB * 128) + ((kk * 16) & 63) * 2, 16, 1024),
-                    sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, kk > 0 ? 1u : 0u);
-        umma_commit(&bars[2]);
-      }
-      if (!mbar_wait(&bars[2], pph, 24)) { ok = false; break; }
-      pph ^= 1;
-      tc_fence_after();
-      if (rb == NRB - 1 && tid == 0 && n + 1 < n1) issue_v(n + 1);  // V is no longer read
-      // epilogue: y = bf16(Yi + qdec_i * Yx), plain or GroupNorm * sigmoid(gate)
-      {
-        float o[EPW];
+    } else if (my_row >= 0) {
 #pragma unroll
-        for (int pc = 0; pc < EPW / 16; ++pc) {
-          float yi[16], yx[16];
-          tmem_ld16(tYi + e0 + pc * 16, yi);
-          tmem_ld16(tYx + e0 + pc * 16, yx);
-          const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
+      for (int rb = 0; rb < NRB; ++rb) {
+        const int t_row = n * CT + rb * RB + my_row;
+        __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                              (size_t)t_row * p.y_st + e0;
+        if (p.y_vec) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[pc * 16 + e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is bf16
-        }
-        if (GATE) {
-          float sum = 0.f;
+          for (int c = 0; c < EPW / 8; ++c)
+            if (e0 + c * 8 < p.hd) stg16(yrow + c * 8, pack16<__nv_bfloat16>(&o[rb][c * 8]));
+        } else {
 #pragma unroll
-          for (int e = 0; e < EPW; ++e) sum += (e0 + e < p.hd) ? o[e] : 0.f;
-          if (my_row >= 0) sRed[my_row * 8 + wg] = sum;
-          named_bar_sync(1 + quarter, NWG * 32);  // the warps holding these rows
-          float mean = 0.f;
-          if (my_row >= 0) {
-#pragma unroll
-            for (int w = 0; w < NWG; ++w) mean += sRed[my_row * 8 + w];
-            mean *= fast_rcp((float)p.hd);
-          }
-          float sq = 0.f;
-#pragma unroll
-          for (int e = 0; e < EPW; ++e) {
-            const float d = o[e] - mean;
-            sq += (e0 + e < p.hd) ? d * d : 0.f;
-          }
-          if (my_row >= 0) sRed[my_row * 8 + 4 + wg] = sq;
-          named_bar_sync(1 + quarter, NWG * 32);
-          if (my_row >= 0) {
-            float ssq = 0.f;
-#pragma unroll
-            for (int w = 0; w < NWG; ++w) ssq += sRed[my_row * 8 + 4 + w];
-            // the reference's padded lanes (block width 64) add (64 - hd) * mean^2
-            const float var = (ssq + (float)(64 - p.hd) * mean * mean) / (float)p.hd;
-            const float inv = rsqrtf(var + 1e-5f);
-            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
-                                (size_t)t_row * p.y_st + e0;
-#pragma unroll
-            for (int c = 0; c < EPW / 8; ++c) {
-              if (e0 + c * 8 >= p.hd) continue;
-              float g[8], r[8];
-              unpack16<__nv_bfloat16>(graw[c], g);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                const int d = e0 + c * 8 + e;
-                const float ygn = ((o[c * 8 + e] - mean) * inv) * sGn[d] + sGn[64 + d];
-                r[e] = ygn * fast_sigmoid(g[e]);
-              }
-              stg16(op + c * 8, pack16<__nv_bfloat16>(r));
-            }
-          }
-        } else if (my_row >= 0) {
-          __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
-                                (size_t)t_row * p.y_st + e0;
-          if (p.y_vec) {
-#pragma unroll
-            for (int c = 0; c < EPW / 8; ++c)
-              if (e0 + c * 8 < p.hd) stg16(yrow + c * 8, pack16<__nv_bfloat16>(&o[c * 8]));
-          } else {
-#pragma unroll
-            for (int e = 0; e < EPW; ++e)
-              if (e0 + e < p.hd) yrow[e] = __float2bfloat16_rn(o[e]);
-          }
+          for (int e = 0; e < EPW; ++e)
+            if (e0 + e < p.hd) yrow[e] = __float2bfloat16_rn(o[rb][e]);
         }
       }
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
     }
-    if (!ok) break;
-    // R (updated by the product issued after prep, complete since the first S commit) -> sR
+    // R <- gC * R + U (fp32) -> sR (bf16) for the next chunk's Yx
+    {
+      const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
 #pragma unroll
-    for (int pc = 0; pc < EPW / 16; ++pc) {
-      float r[16];
-      tmem_ld16(tR + e0 + pc * 16, r);
-      if (f_valid) {
+      for (int pc = 0; pc < EPW / 16; ++pc) {
+        float u[16];
+        tmem_ld16(tR + e0 + pc * 16, u);
+        float* Rp = Rr + pc * 16;
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-          *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, ((e0 + pc * 16) >> 3) + c)) =
-              pack16<__nv_bfloat16>(&r[c * 8]);
+        for (int e = 0; e < 16; ++e) Rp[e] = fmaf(Rp[e], gC, u[e]);
+        if (f_valid) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, ((e0 + pc * 16) >> 3) + c)) =
+                pack16<__nv_bfloat16>(&Rp[c * 8]);
+        }
       }
     }
     fence_proxy_async_smem();
@@ -630,8 +657,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   if (ok && seg == p.nseg - 1 && p.state_out) {
 #pragma unroll
     for (int pc = 0; pc < EPW / 16; ++pc) {
-      float r[16];
-      tmem_ld16(tR + e0 + pc * 16, r);
+      const float* r = Rr + pc * 16;
       if (f_valid) {
         float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0 + pc * 16;
 #pragma unroll
@@ -681,9 +707,9 @@ static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, 
   return 0;
 }
 
-static size_t smem_out_bytes(int CT) {
-  const int RB = CT < 128 ? CT : 128;
-  return 1024 + 4 * CT * 128 + CT * RB * 2 + 64 * 128 + (CT + 4 + 128 + RB * 8) * 4 + 64;
+template <int CT>
+static size_t smem_out_bytes() {
+  return 1024 + 3 * CT * 128 + OutCfg<CT>::PBYTES + 64 * 128 + (CT + 4 + 128 + CT * 8) * 4 + 64;
 }
 static size_t smem_state_bytes(int CT) { return 1024 + 4 * CT * 128 + (CT + 4) * 4 + 64; }
 
@@ -746,7 +772,7 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
     slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), kStateThreads, sm, s>>>(mk, mv, p);
     if (int e = launch_status("slot_tc_state_kernel")) return e;
   }
-  const size_t sm = smem_out_bytes(CT);
+  const size_t sm = smem_out_bytes<CT>();
   cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   slot_tc_out_kernel<CT, PS, GATE><<<(unsigned)(BH * p.nseg), OutCfg<CT>::NT, sm, s>>>(mq, mk, mv, p);
   return launch_status("slot_tc_out_kernel");

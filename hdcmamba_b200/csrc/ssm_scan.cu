@@ -8,13 +8,15 @@
 //   output:          y_t = bf16( bf16(h_t) + bf16(G_n) * exp(cum_log_t) )
 // These are the reference's rounding points (its three kernels store bf16).
 //
-// Schedule: one CTA per (chunk, group of 16 channels, batch) with 16*S <= 256 threads;
-// thread (j, s) scans C/S consecutive steps of channel j (16 at C 256), loading them into
-// registers up front.  Segment results are combined through
+// Schedule: one CTA per (chunk, group of 16 channels, batch) with 16*S <= 256 threads.
+// The CTA stages the chunk's dt / x / b columns of its channels in shared memory with
+// 16-byte loads, all in flight at once; thread (j, s) then scans C/S consecutive steps of
+// channel j (16 at C 256).  Segment results are combined through
 // shared memory: (h_s, sum_log_s) with h = h_prev * exp(sum_log_s) + h_s.
 //   pass 1 (hdc_ssm_chunk_stats): chunk statistics -> stats[b, n, 0:2ds]
 //   pass 2 (hdc_ssm_scan_out):    exclusive prefix over all earlier chunks (including
-//                                 n_prev chunks of earlier sequence segments),
+//                                 n_prev chunks of earlier sequence segments; folded
+//                                 in S contiguous blocks, then across blocks),
 //                                 then the outputs, written with caller strides.
 #include <mutex>
 
@@ -34,12 +36,9 @@ struct SsmParams {
   int blk; int64_t blk_stride;
   void* y; int64_t ysb, yst;
   int L, ds, C, S;
-  int CG;  // channels per CTA (grid.y = ds / CG channel groups)
+  int CG;   // channels per CTA (kCG; grid.y = ds / kCG channel groups)
+  int vec;  // 16-byte loads of the staged columns are aligned
 };
-
-// Steps of one segment held in registers at a time.  All loads of a tile are issued before
-// any arithmetic, so a segment costs one memory latency per tile instead of one per step.
-constexpr int kTile = 8;
 
 // exp / softplus: the hardware approximations (ex2 / lg2 based, as the reference's Triton
 // kernels use) for bf16 activations; the accurate library functions for fp32.
@@ -54,75 +53,79 @@ __device__ __forceinline__ float ssoftplus(float x) {
   else return x > 20.0f ? x : __logf(1.0f + __expf(x));
 }
 
-template <typename T>
-__device__ __forceinline__ float ldnc(const T* ptr) {
-  return to_f(__ldg(ptr));
-}
+constexpr int kCG = 16;  // channels per CTA
 
-// (log decay, input) of steps [t0, t0 + cnt) of channel j, cnt <= kTile
+// Stage the chunk's dt / x / b columns of channel group g into shared memory,
+// tile[(a * C + row) * kCG + c] for a = 0 (dt), 1 (x), 2 (b): every 16-byte load of the CTA
+// is in flight at once (eight per thread per round), so staging costs one memory latency.
 template <typename T>
-__device__ __forceinline__ void ssm_tile(const SsmParams& p, const T* base, int j, float A, int cnt, float* ld,
-                                         float* u) {
-  float dt[kTile], xv[kTile], bv[kTile];
+__device__ __forceinline__ void ssm_stage(const SsmParams& p, int b, int n, int g, T* tile) {
+  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)n * p.C * p.pst + g * kCG;
+  if (p.vec) {
+    constexpr int VE = 16 / sizeof(T);   // elements per 16-byte vector
+    constexpr int VPR = kCG / VE;        // vectors per row of one array
+    const int nvec = p.C * 3 * VPR;
+    for (int i0 = 0; i0 < nvec; i0 += 8 * (int)blockDim.x) {
+      uint4 r[8];
 #pragma unroll
-  for (int t = 0; t < kTile; ++t) {
-    if (t < cnt) {
-      const T* row = base + (size_t)t * p.pst;
-      dt[t] = ldnc(row + j);
-      xv[t] = ldnc(row + p.ds + j);
-      bv[t] = ldnc(row + 2 * p.ds + j);
-    }
-  }
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k * blockDim.x + threadIdx.x;
+        if (i < nvec) {
+          const int v = i % VPR, a = (i / VPR) % 3, row = i / (3 * VPR);
+          r[k] = ldg16(base + (size_t)row * p.pst + a * p.ds + v * VE);
+        }
+      }
 #pragma unroll
-  for (int t = 0; t < kTile; ++t) {
-    if (t < cnt) {
-      const float dts = ssoftplus<T>(dt[t]);
-      ld[t] = dts * A;
-      u[t] = dts * bv[t] * xv[t];
-    }
-  }
-}
-
-// per-thread scan of its segment from h = 0: (h, sum_log).  With a segment of at most
-// kTile steps, ld / u keep the whole segment for the output pass.
-template <typename T>
-__device__ __forceinline__ void ssm_segment(const SsmParams& p, const T* base, int j, float A, float* ld, float* u,
-                                            float& h, float& sl) {
-  const int seglen = p.C / p.S;
-  h = 0.f;
-  sl = 0.f;
-  for (int t0 = 0; t0 < seglen; t0 += kTile) {
-    const int cnt = min(kTile, seglen - t0);
-    ssm_tile<T>(p, base + (size_t)t0 * p.pst, j, A, cnt, ld, u);
-#pragma unroll
-    for (int t = 0; t < kTile; ++t) {
-      if (t < cnt) {
-        sl += ld[t];
-        h = h * sexp<T>(ld[t]) + u[t];
+      for (int k = 0; k < 8; ++k) {
+        const int i = i0 + k * blockDim.x + threadIdx.x;
+        if (i < nvec) {
+          const int v = i % VPR, a = (i / VPR) % 3, row = i / (3 * VPR);
+          *reinterpret_cast<uint4*>(tile + (a * p.C + row) * kCG + v * VE) = r[k];
+        }
       }
     }
+  } else {
+    for (int i = threadIdx.x; i < p.C * 3 * kCG; i += blockDim.x) {
+      const int c = i % kCG, a = (i / kCG) % 3, row = i / (3 * kCG);
+      tile[(a * p.C + row) * kCG + c] = base[(size_t)row * p.pst + a * p.ds + c];
+    }
   }
+}
+
+// (log decay, input) of step `row` of channel jl from the staged tile
+template <typename T>
+__device__ __forceinline__ void ssm_step(const T* tile, int C, int row, int jl, float A, float& ld, float& u) {
+  const float dts = ssoftplus<T>(to_f(tile[row * kCG + jl]));
+  ld = dts * A;
+  u = dts * to_f(tile[(2 * C + row) * kCG + jl]) * to_f(tile[(C + row) * kCG + jl]);
 }
 
 template <typename T>
 __global__ void __launch_bounds__(256) ssm_chunk_stats_kernel(SsmParams p) {
-  extern __shared__ float sh[];  // [2][S][CG]
-  const int n = blockIdx.x, b = blockIdx.z;
-  const int jl = threadIdx.x % p.CG, s = threadIdx.x / p.CG, j = blockIdx.y * p.CG + jl;
+  extern __shared__ float sh[];  // [2][S][kCG] partials, then the staged tile
+  T* tile = reinterpret_cast<T*>(sh + 2 * p.S * kCG);
+  const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int jl = threadIdx.x % kCG, s = threadIdx.x / kCG, j = g * kCG + jl;
   const int N = p.L / p.C;
-  const float A = -expf(to_f(static_cast<const T*>(p.A_log)[j]));
+  const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[j]));
+  ssm_stage<T>(p, b, n, g, tile);
+  __syncthreads();
   const int seglen = p.C / p.S;
-  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)(n * p.C + s * seglen) * p.pst;
-  float ld[kTile], u[kTile], h, sl;
-  ssm_segment<T>(p, base, j, A, ld, u, h, sl);
-  sh[s * p.CG + jl] = h;
-  sh[(p.S + s) * p.CG + jl] = sl;
+  float h = 0.f, sl = 0.f;
+  for (int t = 0; t < seglen; ++t) {
+    float ld, u;
+    ssm_step<T>(tile, p.C, s * seglen + t, jl, A, ld, u);
+    sl += ld;
+    h = h * sexp<T>(ld) + u;
+  }
+  sh[s * kCG + jl] = h;
+  sh[(p.S + s) * kCG + jl] = sl;
   __syncthreads();
   if (s == 0) {
     float hc = 0.f, lc = 0.f;
     for (int q = 0; q < p.S; ++q) {
-      hc = hc * sexp<T>(sh[(p.S + q) * p.CG + jl]) + sh[q * p.CG + jl];
-      lc += sh[(p.S + q) * p.CG + jl];
+      hc = hc * sexp<T>(sh[(p.S + q) * kCG + jl]) + sh[q * kCG + jl];
+      lc += sh[(p.S + q) * kCG + jl];
     }
     float* st = p.stats_w + ((size_t)b * N + n) * 2 * p.ds;
     st[j] = bf16_round(hc);
@@ -130,64 +133,76 @@ __global__ void __launch_bounds__(256) ssm_chunk_stats_kernel(SsmParams p) {
   }
 }
 
+// statistics (last, dec) of chunk m of batch b in the (possibly blocked) layout
+__device__ __forceinline__ const float* ssm_stats_at(const SsmParams& p, int b, int m) {
+  const int blk = m / p.blk;
+  return p.stats_r + (size_t)blk * p.blk_stride + (size_t)b * p.stats_sb + (size_t)(m - blk * p.blk) * 2 * p.ds;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) ssm_scan_out_kernel(SsmParams p) {
-  extern __shared__ float sh[];  // [2][S][CG] + [CG] prefix
-  const int n = blockIdx.x, b = blockIdx.z;
-  const int jl = threadIdx.x % p.CG, s = threadIdx.x / p.CG, j = blockIdx.y * p.CG + jl;
-  const float A = -expf(to_f(static_cast<const T*>(p.A_log)[j]));
-  float* shG = sh + 2 * p.S * p.CG;
-  const int seglen = p.C / p.S;
-  const int t0 = n * p.C + s * seglen;
-  const T* base = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)t0 * p.pst;
-
-  // this thread's segment first (its loads overlap the prefix below)
-  float ld[kTile], u[kTile], h, sl;
-  ssm_segment<T>(p, base, j, A, ld, u, h, sl);
-  sh[s * p.CG + jl] = h;
-  sh[(p.S + s) * p.CG + jl] = sl;
-  // exclusive prefix over chunks [0, n_prev + n) -- fp32, sequential (the reference order)
-  if (s == 0) {
+  extern __shared__ float sh[];  // [4][S][kCG] partials, then the staged tile
+  T* tile = reinterpret_cast<T*>(sh + 4 * p.S * kCG);
+  float* pg = sh + 2 * p.S * kCG;  // prefix partials: fold of a block of earlier chunks
+  float* pd = pg + p.S * kCG;      // and its summed log decay
+  const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int jl = threadIdx.x % kCG, s = threadIdx.x / kCG, j = g * kCG + jl;
+  const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[j]));
+  ssm_stage<T>(p, b, n, g, tile);
+  // exclusive prefix over chunks [0, m_end): segment thread s folds the contiguous block
+  // [m_end * s / S, m_end * (s + 1) / S) (fp32, in chunk order); the blocks are then folded
+  // in order.  The split depends only on the absolute chunk index m_end, so every rank of a
+  // sequence-parallel run gets the same bits as one GPU over the whole sequence.
+  {
     const int m_end = p.n_prev + n;
-    float G = 0.f;
-    for (int m0 = 0, blkno = 0; m0 < m_end; ++blkno) {
-      const float* st = p.stats_r + (size_t)blkno * p.blk_stride + (size_t)b * p.stats_sb;
-      const int m1 = min(m_end - m0, p.blk);
+    const int m0 = (int)((int64_t)m_end * s / p.S), m1 = (int)((int64_t)m_end * (s + 1) / p.S);
+    float G = 0.f, D = 0.f;
 #pragma unroll 4
-      for (int m = 0; m < m1; ++m)
-        G = G * sexp<T>(st[(size_t)m * 2 * p.ds + p.ds + j]) + st[(size_t)m * 2 * p.ds + j];
-      m0 += m1;
+    for (int m = m0; m < m1; ++m) {
+      const float* st = ssm_stats_at(p, b, m);
+      const float dec = st[p.ds + j];
+      G = G * sexp<T>(dec) + st[j];
+      D += dec;
     }
-    shG[jl] = bf16_round(G);
+    pg[s * kCG + jl] = G;
+    pd[s * kCG + jl] = D;
   }
   __syncthreads();
+  const int seglen = p.C / p.S;
+  float h = 0.f, sl = 0.f;
+  for (int t = 0; t < seglen; ++t) {
+    float ld, u;
+    ssm_step<T>(tile, p.C, s * seglen + t, jl, A, ld, u);
+    sl += ld;
+    h = h * sexp<T>(ld) + u;
+  }
+  sh[s * kCG + jl] = h;
+  sh[(p.S + s) * kCG + jl] = sl;
+  __syncthreads();
+  float G = 0.f;
+  for (int q = 0; q < p.S; ++q) G = G * sexp<T>(pd[q * kCG + jl]) + pg[q * kCG + jl];
+  G = bf16_round(G);
   // carry-in from earlier segments of this chunk
   float hin = 0.f, cum = 0.f;
   for (int q = 0; q < s; ++q) {
-    hin = hin * sexp<T>(sh[(p.S + q) * p.CG + jl]) + sh[q * p.CG + jl];
-    cum += sh[(p.S + q) * p.CG + jl];
+    hin = hin * sexp<T>(sh[(p.S + q) * kCG + jl]) + sh[q * kCG + jl];
+    cum += sh[(p.S + q) * kCG + jl];
   }
-  const float G = shG[jl];
+  const int t0 = n * p.C + s * seglen;
   T* yb = static_cast<T*>(p.y) + (size_t)b * p.ysb + (size_t)t0 * p.yst;
   float hh = hin;
-  for (int tb = 0; tb < seglen; tb += kTile) {
-    const int cnt = min(kTile, seglen - tb);
-    if (seglen > kTile) ssm_tile<T>(p, base + (size_t)tb * p.pst, j, A, cnt, ld, u);
-#pragma unroll
-    for (int t = 0; t < kTile; ++t) {
-      if (t < cnt) {
-        cum += ld[t];
-        hh = hh * sexp<T>(ld[t]) + u[t];
-        const float yv = bf16_round(bf16_round(hh) + G * sexp<T>(cum));
-        yb[(size_t)(tb + t) * p.yst + j] = from_f<T>(yv);
-      }
-    }
+  for (int t = 0; t < seglen; ++t) {
+    float ld, u;
+    ssm_step<T>(tile, p.C, s * seglen + t, jl, A, ld, u);
+    cum += ld;
+    hh = hh * sexp<T>(ld) + u;
+    const float yv = bf16_round(bf16_round(hh) + G * sexp<T>(cum));
+    yb[(size_t)t * p.yst + j] = from_f<T>(yv);
   }
 }
 
-// Channels per CTA: 16, so a chunk's channels spread over ds / 16 CTAs (one CTA per chunk
-// is instruction-bound on a single SM: softplus and exp for every step of every channel).
-static int ssm_group(int ds) { return ds < 16 ? ds : 16; }
+// Channels per CTA: 16, so a chunk's channels spread over ds / 16 CTAs.
+static int ssm_group(int ds) { return ds < kCG ? ds : kCG; }
 
 // Segments per chunk: steps of C / S per thread, at least 4, at most 256 threads per CTA.
 static int ssm_segments(int ds, int C) {
@@ -195,6 +210,19 @@ static int ssm_segments(int ds, int C) {
   int S = 1;
   while (S * 2 * cg <= 256 && C % (S * 2) == 0 && C / (S * 2) >= 4) S *= 2;
   return S;
+}
+
+template <typename T>
+static size_t ssm_smem(const SsmParams& p, int parts) {
+  return (size_t)parts * p.S * kCG * sizeof(float) + (size_t)3 * p.C * kCG * sizeof(T);
+}
+
+static void ssm_setup(SsmParams& p, int dtype) {
+  p.S = ssm_segments(p.ds, p.C);
+  p.CG = kCG;
+  const size_t es = dtype == HDC_F32 ? 4 : 2;
+  p.vec = ((reinterpret_cast<uintptr_t>(p.projs) & 15u) == 0 && (p.pst * es) % 16 == 0 && (p.psb * es) % 16 == 0)
+              ? 1 : 0;
 }
 
 static int ssm_check(int dtype, const void* projs, const void* A_log, int64_t B, int64_t L, int64_t ds, int64_t C) {
@@ -217,12 +245,19 @@ extern "C" int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb
   if (!stats) return fail(HDC_E_NULL, "ssm: null stats");
   SsmParams p{};
   p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_w = stats;
-  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C); p.CG = ssm_group((int)ds);
+  p.L = (int)L; p.ds = (int)ds; p.C = (int)C;
+  ssm_setup(p, dtype);
   dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
-  const size_t smem = 2 * p.S * p.CG * sizeof(float);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) ssm_chunk_stats_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
-  else ssm_chunk_stats_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
+  if (dtype == HDC_F32) {
+    const size_t smem = ssm_smem<float>(p, 2);
+    cudaFuncSetAttribute(ssm_chunk_stats_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ssm_chunk_stats_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
+  } else {
+    const size_t smem = ssm_smem<__nv_bfloat16>(p, 2);
+    cudaFuncSetAttribute(ssm_chunk_stats_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ssm_chunk_stats_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
+  }
   return launch_status("ssm_chunk_stats_kernel");
 }
 
@@ -236,12 +271,19 @@ static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, in
   p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_r = stats;
   p.stats_sb = stats_sb; p.n_prev = (int)n_prev; p.y = y; p.ysb = y_sb; p.yst = y_st;
   p.blk = (int)blk; p.blk_stride = blk_stride;
-  p.L = (int)L; p.ds = (int)ds; p.C = (int)C; p.S = ssm_segments((int)ds, (int)C); p.CG = ssm_group((int)ds);
+  p.L = (int)L; p.ds = (int)ds; p.C = (int)C;
+  ssm_setup(p, dtype);
   dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
-  const size_t smem = (2 * p.S + 1) * p.CG * sizeof(float);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) ssm_scan_out_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
-  else ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
+  if (dtype == HDC_F32) {
+    const size_t smem = ssm_smem<float>(p, 4);
+    cudaFuncSetAttribute(ssm_scan_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ssm_scan_out_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
+  } else {
+    const size_t smem = ssm_smem<__nv_bfloat16>(p, 4);
+    cudaFuncSetAttribute(ssm_scan_out_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
+  }
   return launch_status("ssm_scan_out_kernel");
 }
 

@@ -77,6 +77,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int cod
   }
 }
 
+// mbar_wait for a whole warp with one poller: lane 0 spins (bounded), the other lanes wait
+// at __syncwarp instead of polling the barrier (31 fewer threads competing for the
+// shared-memory pipe), then every lane takes the completed phase with one try_wait (its
+// own acquire of the data).  All 32 lanes must call it.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t phase, int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, phase, code) ? 1 : 0;
+  __syncwarp();
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) mbar_try_wait(bar, phase);
+  return ok != 0;
+}
+
 // ---------------------------------------------------------------- fences
 // Named barrier `id` (1..15; 0 is __syncthreads) over `nthreads` threads (a multiple of 32),
 // all of which execute it.
@@ -204,6 +217,28 @@ __device__ __forceinline__ float fast_sigmoid(float x) {
   float t;
   asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
   return fmaf(0.5f, t, 0.5f);
+}
+
+// Two 16-column TMEM loads (columns [a, a+16) and [b, b+16)) and one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[16 + i]);
+  }
 }
 
 // Two 32-column TMEM loads (columns [a, a+32) and [b, b+32)) and one wait.
