@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   }
 
   // per-row statistics of `nrows` rows at `rows`, one warp per row -> st[2*r], st[2*r+1]
+  // (two passes over the row in shared memory: mean, then the centred sum of squares)
   auto row_stats = [&](const uint8_t* rows, int nrows, float* st) {
     for (int r = warp; r < nrows; r += nwarps) {
       const uint4* rp = reinterpret_cast<const uint4*>(rows + (size_t)r * row_bytes);
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
           const float d = f[e] - mean;
-          q += d * d;
+          q = fmaf(d, d, q);
         }
       }
       const float rstd = rsqrtf(warp_sum(q) * invD + p.eps);
@@ -143,8 +144,10 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
     }
   }
 
-  // conv window from the three preceding rows
-  float w3[VPT][VEC], w2[VPT][VEC], w1[VPT][VEC];
+  // conv window: W[k][rho & 3] holds the normalised row rho (relative to the segment start,
+  // rows -3..-1 from the preceding rows), so with tiles of a multiple of 4 rows and the row
+  // loop unrolled by 4 every index is a compile-time constant (no register moves)
+  float W[VPT][4][VEC];
   row_stats(pre, 3, stats);  // first six stats slots; tile 0 rewrites them after the barrier below
   __syncthreads();
 #pragma unroll
@@ -157,8 +160,7 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
       const float m = stats[2 * r], rs = stats[2 * r + 1];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
-        const float n = (f[e] - m) * rs * nw[k][e] + nb[k][e];
-        if (r == 0) w3[k][e] = n; else if (r == 1) w2[k][e] = n; else w1[k][e] = n;
+        W[k][r + 1][e] = (f[e] - m) * rs * nw[k][e] + nb[k][e];
       }
     }
   }
@@ -181,21 +183,27 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
     for (int kk = 0; kk < VPT; ++kk) {
       if (!active[kk]) continue;
       const int c = tid + kk * blockDim.x;
-      for (int r = 0; r < nv; ++r) {
-        float f[VEC], o[VEC];
-        unpack16<T>(reinterpret_cast<const uint4*>(tile + (size_t)r * row_bytes)[c], f);
-        const float m = tstat[2 * r], rs = tstat[2 * r + 1];
+      for (int r4 = 0; r4 < nv; r4 += 4) {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float n0 = (f[e] - m) * rs * nw[kk][e] + nb[kk][e];
-          float v = w3[kk][e] * c0[kk][e] + w2[kk][e] * c1[kk][e] + w1[kk][e] * c2[kk][e] + n0 * c3[kk][e] + cb[kk][e];
-          if (p.act == HDC_ACT_SILU) v = v / (1.0f + fast_exp(-v));
-          o[e] = v;
-          w3[kk][e] = w2[kk][e];
-          w2[kk][e] = w1[kk][e];
-          w1[kk][e] = n0;
+        for (int u = 0; u < 4; ++u) {
+          const int r = r4 + u;
+          if (r < nv) {
+            float f[VEC], o[VEC];
+            unpack16<T>(reinterpret_cast<const uint4*>(tile + (size_t)r * row_bytes)[c], f);
+            const float rs = tstat[2 * r + 1], mrs = -tstat[2 * r] * rs;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+              const float n0 = fmaf(fmaf(f[e], rs, mrs), nw[kk][e], nb[kk][e]);  // (x - mean) rstd w + b
+              float v = fmaf(W[kk][(u + 1) & 3][e], c0[kk][e],
+                             fmaf(W[kk][(u + 2) & 3][e], c1[kk][e],
+                                  fmaf(W[kk][(u + 3) & 3][e], c2[kk][e], fmaf(n0, c3[kk][e], cb[kk][e]))));
+              if (p.act == HDC_ACT_SILU) v *= fast_sigmoid(v);
+              o[e] = v;
+              W[kk][u][e] = n0;
+            }
+            stg16(out + (size_t)(t0 + r) * p.D + c * VEC, pack16<T>(o));
+          }
         }
-        stg16(out + (size_t)(t0 + r) * p.D + c * VEC, pack16<T>(o));
       }
     }
     __syncthreads();
@@ -212,14 +220,14 @@ static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   int threads = ((G + VPT - 1) / VPT + 31) / 32 * 32;
   if (threads < 128) threads = 128;
   const int row_bytes = p.D * (int)sizeof(T);
-  int tile = 16384 / row_bytes;
+  int tile = (16384 / row_bytes) & ~3;  // a multiple of 4 rows (the conv window unroll)
   tile = tile < 4 ? 4 : (tile > 16 ? 16 : tile);
   int nst = 3;
   auto smem_of = [&](int t, int s) {
     return (size_t)128 + (size_t)s * t * row_bytes + 3 * (size_t)row_bytes + (2 * s * t + 2) * 4 + (s + 1) * 8 + 16;
   };
   while (smem_of(tile, nst) > 110 * 1024 && nst > 2) --nst;
-  while (smem_of(tile, nst) > 200 * 1024 && tile > 2) tile /= 2;
+  while (smem_of(tile, nst) > 200 * 1024 && tile > 4) tile -= 4;
   const size_t smem = smem_of(tile, nst);
   cudaFuncSetAttribute(ln_conv_kernel<T, VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int occ = 0;
