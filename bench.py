@@ -230,7 +230,8 @@ def run_reference(args, cfg, rank):
     v = tokens / dt
     sample = f"first {tokens} of {cfg.seq_len} tokens per step, all {cfg.n_layers} layers + vocab-{cfg.vocab} head"
     print(json.dumps({
-        "metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+        "metric": METRIC if cfg.seq_len == 32768 else f"prefill tokens/sec at L={cfg.seq_len}",
+        "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"{cfg.name}: {cfg.n_layers}x d{cfg.d_model} H{cfg.num_heads} ds{cfg.d_state} "
@@ -251,6 +252,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c5")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "sp", "batch"],
+                    help="N > 1: batch = split the global batch over the ranks (no collective, config 4); "
+                         "sp = split the sequence (config 5); auto = batch when the batch divides evenly")
     ap.add_argument("--ref-tokens", type=int, default=512)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -287,7 +291,23 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     lm = build_lm(cfg).to(dev).bfloat16()
+    mode = "single"
     if world > 1:
+        mode = args.parallel
+        if mode == "auto":
+            mode = "batch" if cfg.batch % world == 0 else "sp"
+        if mode == "batch" and cfg.batch % world != 0:
+            raise SystemExit(f"batch {cfg.batch} does not split over {world} ranks")
+    if mode == "batch":
+        # batch sharding: rank r runs samples [r*B/W, (r+1)*B/W) through the whole model, no
+        # collective in the forward
+        Bs = cfg.batch // world
+        ids_host = synthetic_ids(cfg)[rank * Bs:(rank + 1) * Bs].contiguous().pin_memory()
+
+        def forward(x):
+            with torch.no_grad():
+                return lm(x)
+    elif mode == "sp":
         # sequence parallel: rank r runs positions [r*L/W, (r+1)*L/W) of the same sequence
         from hdcmamba_b200.sp import SequenceParallel
         if cfg.seq_len % (world * cfg.chunk_size) != 0:
@@ -371,7 +391,7 @@ def main():
         forward(ids)
     for name in slot_names:
         setattr(ops, name, originals[name])
-    per_layer = 2 if world > 1 else 1
+    per_layer = 2 if mode == "sp" else 1
     layer_calls = slot_calls[:per_layer]
     slot_per_step = len(slot_calls) / per_layer
 
@@ -396,7 +416,7 @@ def main():
     del flush, slot_calls, layer_calls, slot_graph
 
     # end to end through the public call: pinned host ids -> device, logits[:, -1] -> host
-    out_host = torch.empty(cfg.batch, cfg.vocab, dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty(ids_host.shape[0], cfg.vocab, dtype=torch.bfloat16).pin_memory()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -418,18 +438,21 @@ def main():
         slot_bytes = 5 * tokens_per_rank * cfg.d_model * 2
         achieved = slot_bytes / (slot_ms * 1e-3) / 1e9
         line = {
-            "metric": METRIC, "value": world * tokens_per_rank / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC if cfg.seq_len == 32768 else f"prefill tokens/sec at L={cfg.seq_len}",
+            "value": world * tokens_per_rank / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random weights N(0,0.02), uniform token ids)",
             "config": {"workload": f"{cfg.name}: {cfg.n_layers}x d{cfg.d_model} H{cfg.num_heads} ds{cfg.d_state} "
                                    f"C{cfg.chunk_size}, vocab {cfg.vocab}, B{cfg.batch} L{cfg.seq_len}, full logits",
                        "global_batch": cfg.batch, "seq_len": cfg.seq_len,
-                       "parallelism": f"sp{world} (sequence-parallel segments, NCCL carries)" if world > 1 else "single",
+                       "parallelism": {"single": "single",
+                                       "sp": f"sp{world} (sequence-parallel segments, NCCL carries)",
+                                       "batch": f"dp{world} (batch-sharded, no collective)"}[mode],
                        "launch": "eager" if args.eager else "cuda_graph",
                        "l2": "working set > L2 (projs 214 MB/layer, weights 153 MB): no explicit flush"},
             "roofline": {"kernel": ("slot_state + slot_scan_gate_carry (slot_tc_state + slot_fold + slot_tc_out)"
-                                    if world > 1 else "slot_scan_gate (slot_tc_state + slot_tc_out)"), "bound": "hbm", "achieved": achieved, "peak": hbm,
+                                    if mode == "sp" else "slot_scan_gate (slot_tc_state + slot_tc_out)"), "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
                          "traffic": SLOT_TRAFFIC_BYTES * tokens_per_rank / (cfg.batch * cfg.seq_len),
                          "traffic_source": "ncu capture of the 1-GPU op" + (
