@@ -36,7 +36,7 @@ FALLBACK_HBM_GBS = 6650.0
 METRIC = "prefill tokens/sec at L=32768"
 # DRAM bytes (read + write) of one config-5 slot op (slot_tc_state + slot_tc_out) from an ncu
 # --set full capture of `bench.py --workload c5slot` (profiles/slot_scan_c5.md)
-SLOT_TRAFFIC_BYTES = 97.16e6 + 3.24e6 + 203.58e6 + 36.44e6
+SLOT_TRAFFIC_BYTES = 97.17e6 + 3.53e6 + 203.58e6 + 33.12e6
 
 
 def peaks():
