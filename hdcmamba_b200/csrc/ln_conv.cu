@@ -14,7 +14,8 @@
 //     rows, which are contiguous in memory.  The copy of tile k+NST is issued as soon
 //     as tile k has been consumed.
 //   * per-row mean / rstd: one warp per row reads the row from shared memory (the whole
-//     row is in the stage), two-pass variance with warp shuffles only.
+//     row is in the stage), two-pass variance with warp shuffles only.  The statistics of
+//     tile k+1 are computed in the same phase as the conv of tile k (one barrier per tile).
 //   * the conv walks the tile's rows with the three previous normalised rows held in
 //     registers, so each thread's window carries from tile to tile.
 #include "tc.cuh"
@@ -41,11 +42,13 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   extern __shared__ uint8_t smem_raw[];
   const int row_bytes = p.D * (int)sizeof(T);
   const int G = p.D / VEC;
-  // smem: [nst][tile] rows | 3 pre rows | stats [nst][tile][2] | mbarriers [nst + 1]
+  // smem: [nst][tile] rows | 3 pre rows | stats [nst][tile][2] + pre-row stats [3][2] |
+  // mbarriers [nst + 1]
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   uint8_t* pre = ring + (size_t)p.nst * p.tile * row_bytes;
   float* stats = reinterpret_cast<float*>(pre + 3 * row_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stats + 2 * p.nst * p.tile + 2);
+  float* pstats = stats + 2 * p.nst * p.tile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pstats + 6);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int seg = blockIdx.x;
@@ -148,7 +151,12 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   // rows -3..-1 from the preceding rows), so with tiles of a multiple of 4 rows and the row
   // loop unrolled by 4 every index is a compile-time constant (no register moves)
   float W[VPT][4][VEC];
-  row_stats(pre, 3, stats);  // first six stats slots; tile 0 rewrites them after the barrier below
+  row_stats(pre, 3, pstats);
+  bool ok = true;
+  if (ntiles > 0) {  // statistics of tile 0 (those of tile k+1 are computed next to tile k's conv)
+    ok = mbar_wait(&bars[0], 0, 32);
+    if (ok) row_stats(ring, min(p.tile, l1 - l0), stats);
+  }
   __syncthreads();
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -157,24 +165,24 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
     for (int r = 0; r < 3; ++r) {
       float f[VEC];
       unpack16<T>(reinterpret_cast<const uint4*>(pre + (size_t)r * row_bytes)[c], f);
-      const float m = stats[2 * r], rs = stats[2 * r + 1];
+      // the same expression as the row loop, so a halo row normalises to the same bits
+      const float rs = pstats[2 * r + 1], mrs = -pstats[2 * r] * rs;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        W[k][r + 1][e] = (f[e] - m) * rs * nw[k][e] + nb[k][e];
-      }
+      for (int e = 0; e < VEC; ++e) W[k][r + 1][e] = fmaf(fmaf(f[e], rs, mrs), nw[k][e], nb[k][e]);
     }
   }
-  __syncthreads();
 
-  for (int k = 0; k < ntiles; ++k) {
+  for (int k = 0; k < ntiles && ok; ++k) {
     const int st = k % p.nst;
     const int t0 = l0 + k * p.tile;
     const int nv = min(p.tile, l1 - t0);
     const uint8_t* tile = ring + (size_t)st * p.tile * row_bytes;
-    float* tstat = stats + 2 * st * p.tile;
-    if (!mbar_wait(&bars[st], (uint32_t)((k / p.nst) & 1), 32)) break;
-    row_stats(tile, nv, tstat);
-    __syncthreads();
+    const float* tstat = stats + 2 * st * p.tile;
+    if (k + 1 < ntiles) {  // the next tile's row statistics, in the same phase as this conv
+      const int st1 = (k + 1) % p.nst;
+      if (!mbar_wait(&bars[st1], (uint32_t)(((k + 1) / p.nst) & 1), 32)) { ok = false; break; }
+      row_stats(ring + (size_t)st1 * p.tile * row_bytes, min(p.tile, l1 - (t0 + p.tile)), stats + 2 * st1 * p.tile);
+    }
     if (p.mean && tid < nv) {
       p.mean[(size_t)b * p.L + t0 + tid] = __float2bfloat16_rn(tstat[2 * tid]);
       p.rstd[(size_t)b * p.L + t0 + tid] = __float2bfloat16_rn(tstat[2 * tid + 1]);
@@ -212,6 +220,10 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
       issue(k + p.nst);
     }
   }
+  // after a timed-out wait: let this CTA's own copies in flight land (bounded) before exit
+  if (!ok && tid == 0) {
+    for (int k = 0; k < ntiles && k < p.nst; ++k) mbar_wait(&bars[k], 0, 33);
+  }
 }
 
 template <typename T, int VPT>
@@ -220,11 +232,14 @@ static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   int threads = ((G + VPT - 1) / VPT + 31) / 32 * 32;
   if (threads < 128) threads = 128;
   const int row_bytes = p.D * (int)sizeof(T);
-  int tile = (16384 / row_bytes) & ~3;  // a multiple of 4 rows (the conv window unroll)
+  // stages of 32 KB for rows of 4 KB and more (8 rows: one per warp for the statistics),
+  // 16 KB otherwise (shorter segments keep more CTAs busy at narrow rows); a multiple of 4
+  // rows (the conv window unroll)
+  int tile = ((row_bytes >= 4096 ? 32768 : 16384) / row_bytes) & ~3;
   tile = tile < 4 ? 4 : (tile > 16 ? 16 : tile);
   int nst = 3;
   auto smem_of = [&](int t, int s) {
-    return (size_t)128 + (size_t)s * t * row_bytes + 3 * (size_t)row_bytes + (2 * s * t + 2) * 4 + (s + 1) * 8 + 16;
+    return (size_t)128 + (size_t)s * t * row_bytes + 3 * (size_t)row_bytes + (2 * s * t + 6) * 4 + (s + 1) * 8 + 16;
   };
   while (smem_of(tile, nst) > 110 * 1024 && nst > 2) --nst;
   while (smem_of(tile, nst) > 200 * 1024 && tile > 4) tile -= 4;

@@ -101,6 +101,8 @@ extern "C" int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, 
     return fail(HDC_E_NULL, "slot_gate_carry: n_prev=%lld needs prev_state / prev_decay", (long long)n_prev);
   if (n_prev > 1 && prev_stride < B * H * 4096)
     return fail(HDC_E_SHAPE, "slot_gate_carry: prev_stride %lld < B*H*4096", (long long)prev_stride);
+  if (n_prev > 0 && (!aligned16(prev_state) || prev_stride % 4 != 0))
+    return fail(HDC_E_ALIGN, "slot_gate_carry: prev_state must be 16-byte aligned, prev_stride a multiple of 4");
   const SlotCarry cy{prev_state, prev_decay, prev_stride, (int)n_prev};
   return slot_gate_common("slot_gate_carry", q, k, v, in_sb, in_st, gamma, log_a, gate, gate_sb, gate_st, gn_w,
                           gn_b, out, out_sb, out_sh, out_st, nullptr, state_out, workspace, workspace_bytes, B, L,

@@ -375,17 +375,33 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 #pragma unroll
         for (int e = 0; e < 16; ++e) Rp[e] = src[e];
       }
+      // (unrolled so that the loads of several parts are in flight together)
+#pragma unroll 4
       for (int s = 0; s < p.nprev; ++s) {
         const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
-        const float* src = p.prev_R + (size_t)s * p.prev_stride + (size_t)bh * 4096 + f_row * 64 + c0;
+        const float4* src = reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride +
+                                                            (size_t)bh * 4096 + f_row * 64 + c0);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) Rp[e] = Ds * Rp[e] + src[e];
+        for (int e = 0; e < 4; ++e) {
+          const float4 v = src[e];
+          Rp[4 * e] = Ds * Rp[4 * e] + v.x;
+          Rp[4 * e + 1] = Ds * Rp[4 * e + 1] + v.y;
+          Rp[4 * e + 2] = Ds * Rp[4 * e + 2] + v.z;
+          Rp[4 * e + 3] = Ds * Rp[4 * e + 3] + v.w;
+        }
       }
+#pragma unroll 4
       for (int s = 0; s < seg; ++s) {
         const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
-        const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + c0;
+        const float4* src = reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + c0);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) Rp[e] = Ds * Rp[e] + src[e];
+        for (int e = 0; e < 4; ++e) {
+          const float4 v = src[e];
+          Rp[4 * e] = Ds * Rp[4 * e] + v.x;
+          Rp[4 * e + 1] = Ds * Rp[4 * e + 1] + v.y;
+          Rp[4 * e + 2] = Ds * Rp[4 * e + 2] + v.z;
+          Rp[4 * e + 3] = Ds * Rp[4 * e + 3] + v.w;
+        }
       }
 #pragma unroll
       for (int c = 0; c < 2; ++c)

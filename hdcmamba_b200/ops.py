@@ -303,6 +303,8 @@ def slot_scan_gate_carry(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_s
     if (gamma is None) == (log_a is None):
         raise ValueError("give exactly one of gamma or log_a")
     if n_prev > 0:
+        if prev_state.data_ptr() % 16 != 0 or prev_stride % 4 != 0:
+            raise ValueError("prev_state must be 16-byte aligned and prev_stride a multiple of 4")
         for t, per in ((prev_state, B * H * 4096), (prev_decay, B * H)):
             if t.dtype != torch.float32 or t.dim() != 1 or t.stride(0) != 1:
                 raise ValueError("prev_state / prev_decay must be 1-D contiguous fp32 tensors")

@@ -194,7 +194,8 @@ int hdc_slot_state_fwd(int dtype, const void* k, const void* v, int64_t in_sb, i
  * entering state is folded from the n_prev earlier parts, R <- D_s R + R_s for s = 0 ..
  * n_prev-1 (R from zero), where part s has R_s at prev_state + s*prev_stride (fp32
  * [B*H, 64, 64]) and D_s at prev_decay + s*prev_stride (fp32 [B*H]): the gathered
- * state_out / decay_out of hdc_slot_state_fwd on the earlier ranks.  `workspace` must be
+ * state_out / decay_out of hdc_slot_state_fwd on the earlier ranks.  prev_state must be
+ * 16-byte aligned and prev_stride a multiple of 4 (HDC_E_ALIGN otherwise).  `workspace` must be
  * the one that this rank's hdc_slot_state_fwd over the same k, v and shape filled (its
  * segment states are reused; only the output pass runs).  No single-launch counterpart in
  * the reference: it replaces _slot_all_fused's carry of `running` across chunks

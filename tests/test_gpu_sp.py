@@ -124,7 +124,7 @@ def test_slot_gate_carry_matches_whole_sequence(W, B, L, H, C):
     ops.slot_scan_gate(q, k, v, H, C, gate, gw, gb, ref, strides(L), gamma=gamma)
     Ls = L // W
     n_sl, n_dc = B * H * 4096, B * H
-    n = n_sl + n_dc + 4
+    n = (n_sl + n_dc + 4 + 3) // 4 * 4  # parts 16-byte aligned, as the entry point requires
     gathered = torch.full((W * n,), float("nan"), device="cuda")
     wss = []
     for r in range(W):
