@@ -252,6 +252,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c5")
+    ap.add_argument("--sp-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="sequence parallelism: peer stores into IPC-mapped mailboxes, or NCCL all-gathers")
     ap.add_argument("--parallel", default="auto", choices=["auto", "sp", "batch"],
                     help="N > 1: batch = split the global batch over the ranks (no collective, config 4); "
                          "sp = split the sequence (config 5); auto = batch when the batch divides evenly")
@@ -312,7 +314,7 @@ def main():
         from hdcmamba_b200.sp import SequenceParallel
         if cfg.seq_len % (world * cfg.chunk_size) != 0:
             raise SystemExit(f"L={cfg.seq_len} does not split into {world} chunk-aligned segments")
-        sp = SequenceParallel()
+        sp = SequenceParallel(transport=args.sp_transport)
         Ls = cfg.seq_len // world
         ids_host = synthetic_ids(cfg)[:, rank * Ls:(rank + 1) * Ls].contiguous().pin_memory()
 
@@ -447,7 +449,9 @@ def main():
                                    f"C{cfg.chunk_size}, vocab {cfg.vocab}, B{cfg.batch} L{cfg.seq_len}, full logits",
                        "global_batch": cfg.batch, "seq_len": cfg.seq_len,
                        "parallelism": {"single": "single",
-                                       "sp": f"sp{world} (sequence-parallel segments, NCCL carries)",
+                                       "sp": f"sp{world} (sequence-parallel segments, "
+                                             + ("peer-store carries and halos over NVLink)" if args.sp_transport == "p2p"
+                                                else "NCCL all-gather carries and halos)"),
                                        "batch": f"dp{world} (batch-sharded, no collective)"}[mode],
                        "launch": "eager" if args.eager else "cuda_graph",
                        "l2": "working set > L2 (projs 214 MB/layer, weights 153 MB): no explicit flush"},
@@ -476,6 +480,8 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         del graphed  # a graph holding NCCL calls must go before the process group
+        if mode == "sp":
+            sp.close()
         torch.cuda.synchronize()
         dist.destroy_process_group()
 

@@ -53,6 +53,17 @@ SIGNATURES = {
     "hdc_gate_cat_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
                                  c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_row_layernorm": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, c_float, c_vp]),
+    "hdc_peer_alloc": (c_int, [c_size, ctypes.POINTER(c_vp)]),
+    "hdc_peer_free": (c_int, [c_vp]),
+    "hdc_ipc_handle_bytes": (c_int, []),
+    "hdc_ipc_handle": (c_int, [c_vp, c_vp]),
+    "hdc_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "hdc_ipc_close": (c_int, [c_vp]),
+    "hdc_peer_put": (c_int, [c_vp, c_size, c_vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32, c_int, c_vp,
+                             c_vp]),
+    "hdc_peer_wait": (c_int, [c_vp, ctypes.c_uint32, c_vp, c_vp]),
+    "hdc_peer_gen_bump": (c_int, [c_vp, c_vp]),
+    "hdc_peer_barrier": (c_int, [c_vp, ctypes.c_uint64, c_int, c_int, c_vp, c_vp, c_vp]),
 }
 
 _lib = None

@@ -1,0 +1,190 @@
+// Peer-memory exchange for sequence parallelism over NVLink / NVSwitch, sm_100a.
+//
+// One process per GPU.  Every rank allocates one mailbox (hdc_peer_alloc) and shares it
+// with the other ranks through CUDA IPC (hdc_ipc_handle / hdc_ipc_open).  A producer then
+// stores its data straight into the consumers' mailboxes over NVLink (plain 16-byte peer
+// stores, no multicast) and raises a flag there; a consumer waits for the flags it needs
+// (bounded spins) before the kernels that read the data run.  This replaces a collective
+// where the data flow is one-directional: under sequence parallelism rank r only needs the
+// carries of ranks < r and the halo rows of rank r - 1.
+//
+// Flags carry a generation number: every rank bumps its own device counter once per
+// forward (hdc_peer_gen_bump) and all ranks run the same forwards, so a consumer waits for
+// its own generation (or a later one) and no flag ever needs clearing.  A flag barrier at the end of
+// each forward (hdc_peer_barrier) keeps a rank from writing a mailbox region of the next
+// forward while a slower rank still reads the current one.
+//
+// Memory ordering: the producer CTA's threads store the data, then __syncthreads(), then one
+// thread issues fence.acq_rel.sys and a relaxed system-scope flag store (the fence is
+// cumulative over the CTA's stores observed through the barrier).  The consumer loads the
+// flag with ld.acquire.sys; the kernels that read the data follow in stream order.
+//
+// Every wait gives up after ~2 s of %globaltimer, records an error code readable through
+// hdc_device_error() and returns, so a missing peer can not hang the GPU.
+#include <cstring>
+
+#include "tc.cuh"
+
+namespace hdc {
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// generation g has been reached (wrap-safe): a fast rank may already have written g + 1
+__device__ __forceinline__ bool reached(uint32_t v, uint32_t g) { return (int32_t)(v - g) >= 0; }
+
+// bounded spin until *flag has reached generation want; false (and the error code) on timeout
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, int code) {
+  if (reached(ld_acquire_sys(flag), want)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!reached(ld_acquire_sys(flag), want)) {
+    if (globaltimer_ns() - t0 > 2000000000ull) {
+      atomicCAS(&g_dev_error, 0, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// CTA t copies `bytes` from src to dst_base[t] + dst_off and then sets flag_base[t] +
+// flag_off to the generation; targets t with bit t of `mask` clear are skipped.
+__global__ void __launch_bounds__(512) peer_put_kernel(const uint4* src, size_t n16, const uint64_t* dst_base,
+                                                       uint64_t dst_off, uint64_t flag_off, uint32_t mask,
+                                                       const uint32_t* gen) {
+  const int t = blockIdx.x;
+  if (!((mask >> t) & 1u)) return;
+  uint4* dst = reinterpret_cast<uint4*>(dst_base[t] + dst_off);
+  // eight loads in flight per thread before their stores
+  for (size_t i0 = 0; i0 < n16; i0 += 8 * (size_t)blockDim.x) {
+    uint4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const size_t i = i0 + (size_t)k * blockDim.x + threadIdx.x;
+      if (i < n16) v[k] = src[i];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const size_t i = i0 + (size_t)k * blockDim.x + threadIdx.x;
+      if (i < n16) dst[i] = v[k];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    st_relaxed_sys(reinterpret_cast<uint32_t*>(dst_base[t] + flag_off), *gen);
+  }
+}
+
+// lane s waits for flags[s] == *gen for every bit s of mask (s < 32)
+__global__ void peer_wait_kernel(const uint32_t* flags, uint32_t mask, const uint32_t* gen) {
+  const int s = threadIdx.x;
+  if (s < 32 && ((mask >> s) & 1u)) wait_flag(flags + s, *gen, 41);
+}
+
+__global__ void peer_gen_bump_kernel(uint32_t* gen) { *gen += 1; }
+
+// every rank writes its generation into slot `rank` of every rank's barrier array, then
+// waits until all `world` slots of its own array hold its generation
+__global__ void peer_barrier_kernel(const uint64_t* base, uint64_t bar_off, int world, int rank,
+                                    const uint32_t* local_bar, const uint32_t* gen) {
+  const int s = threadIdx.x;
+  const uint32_t g = *gen;
+  if (s < world) {
+    fence_acq_rel_sys();
+    st_relaxed_sys(reinterpret_cast<uint32_t*>(base[s] + bar_off) + rank, g);
+  }
+  __syncwarp();
+  if (s < world) wait_flag(local_bar + s, g, 42);
+}
+
+}  // namespace hdc
+
+using namespace hdc;
+
+extern "C" int hdc_peer_alloc(size_t bytes, void** dev_ptr) {
+  if (!dev_ptr || bytes == 0) return fail(HDC_E_NULL, "peer_alloc: null output or zero bytes");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail((int)e, "peer_alloc: %s", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any peer can map it
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail((int)e, "peer_alloc: %s", cudaGetErrorString(e));
+  }
+  *dev_ptr = p;
+  return 0;
+}
+
+extern "C" int hdc_peer_free(void* dev_ptr) {
+  const cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? 0 : fail((int)e, "peer_free: %s", cudaGetErrorString(e));
+}
+
+extern "C" int hdc_ipc_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int hdc_ipc_handle(const void* dev_ptr, void* handle_out) {
+  if (!dev_ptr || !handle_out) return fail(HDC_E_NULL, "ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+  if (e != cudaSuccess) return fail((int)e, "ipc_handle: %s", cudaGetErrorString(e));
+  memcpy(handle_out, &h, sizeof(h));
+  return 0;
+}
+
+extern "C" int hdc_ipc_open(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return fail(HDC_E_NULL, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? 0 : fail((int)e, "ipc_open: %s", cudaGetErrorString(e));
+}
+
+extern "C" int hdc_ipc_close(void* dev_ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? 0 : fail((int)e, "ipc_close: %s", cudaGetErrorString(e));
+}
+
+extern "C" int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_base, uint64_t dst_off,
+                            uint64_t flag_off, uint32_t mask, int world, const uint32_t* gen,
+                            hdc_stream_t stream) {
+  if (!src || !dst_base || !gen) return fail(HDC_E_NULL, "peer_put: null pointer");
+  if (world < 1 || world > 32) return fail(HDC_E_SHAPE, "peer_put: world %d (1..32)", world);
+  if (bytes % 16 || !aligned16(src) || dst_off % 16 || flag_off % 4)
+    return fail(HDC_E_ALIGN, "peer_put: src / dst must be 16-byte aligned and sizes multiples of 16");
+  if (mask == 0) return 0;
+  peer_put_kernel<<<world, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), bytes / 16, dst_base, dst_off, flag_off, mask, gen);
+  return launch_status("peer_put_kernel");
+}
+
+extern "C" int hdc_peer_wait(const uint32_t* flags, uint32_t mask, const uint32_t* gen, hdc_stream_t stream) {
+  if (!flags || !gen) return fail(HDC_E_NULL, "peer_wait: null pointer");
+  if (mask == 0) return 0;
+  peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, mask, gen);
+  return launch_status("peer_wait_kernel");
+}
+
+extern "C" int hdc_peer_gen_bump(uint32_t* gen, hdc_stream_t stream) {
+  if (!gen) return fail(HDC_E_NULL, "peer_gen_bump: null pointer");
+  peer_gen_bump_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(gen);
+  return launch_status("peer_gen_bump_kernel");
+}
+
+extern "C" int hdc_peer_barrier(const uint64_t* base, uint64_t bar_off, int world, int rank,
+                                const uint32_t* local_bar, const uint32_t* gen, hdc_stream_t stream) {
+  if (!base || !local_bar || !gen) return fail(HDC_E_NULL, "peer_barrier: null pointer");
+  if (world < 1 || world > 32 || rank < 0 || rank >= world || bar_off % 4)
+    return fail(HDC_E_SHAPE, "peer_barrier: world %d rank %d", world, rank);
+  peer_barrier_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(base, bar_off, world, rank,
+                                                                            local_bar, gen);
+  return launch_status("peer_barrier_kernel");
+}

@@ -18,6 +18,15 @@ dependencies, and each is exchanged once per layer with ``all_gather`` (NCCL ove
      the output kernel (``hdc_slot_gate_carry_fwd``), which also reuses the segment states
      that ``hdc_slot_state_fwd`` left in the workspace.
 
+Two transports move the halo and the carries:
+
+* ``"nccl"``: two ``all_gather`` calls per layer (every rank receives every rank's data).
+* ``"p2p"``: each rank stores straight into the mailboxes of the ranks that need its data
+  (carries to every higher rank, the halo to rank r+1) over NVLink, through CUDA-IPC-mapped
+  buffers (``hdcmamba_b200.peer``), and raises a generation flag there; a rank waits
+  (bounded) only for the flags of its senders.  The mailbox regions have the rank-major
+  layout of the all-gather output, so the kernels read them the same way.
+
 The kernels are those of the single-GPU Block (fixed semantics).  Only batch-independent
 work crosses ranks, so batch sharding (config 4) needs no collective at all and uses the
 plain module on each rank.
@@ -45,16 +54,81 @@ def _all_gather(t, group):
     return out.reshape((world,) + tuple(t.shape))
 
 
+class _Mailboxes:
+    """Byte offsets of the per-layer regions in a rank's peer mailbox."""
+
+    def __init__(self, n_layers, world, n_pad, halo_bytes):
+        self.n_pad, self.world = n_pad, world
+        self.carry_layer = world * n_pad * 4
+        self.halo_bytes = (halo_bytes + 15) // 16 * 16
+        self.halo0 = n_layers * self.carry_layer
+        self.cflag0 = self.halo0 + n_layers * self.halo_bytes
+        self.hflag0 = self.cflag0 + (n_layers * world * 4 + 15) // 16 * 16
+        self.bar = self.hflag0 + (n_layers * 4 + 15) // 16 * 16
+        self.total = self.bar + (world * 4 + 15) // 16 * 16
+
+    def carries(self, layer, rank=0):
+        return layer * self.carry_layer + rank * self.n_pad * 4
+
+    def halo(self, layer):
+        return self.halo0 + layer * self.halo_bytes
+
+    def carry_flags(self, layer, rank=0):
+        return self.cflag0 + (layer * self.world + rank) * 4
+
+    def halo_flag(self, layer):
+        return self.hflag0 + layer * 4
+
+
 class SequenceParallel:
     """Runs HdcMamba blocks / LMs on this rank's segment of the sequence."""
 
-    def __init__(self, group=None, kernels=None):
+    def __init__(self, group=None, kernels=None, transport="nccl"):
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport {transport!r}: 'nccl' or 'p2p'")
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.k = kernels if kernels is not None else CudaKernels()
+        self.transport = transport
+        self._mb = None       # PeerMailbox (p2p)
+        self._lay = None      # _Mailboxes
+        self._mb_key = None
 
-    def block(self, blk, h):
+    @staticmethod
+    def _carry_len(B, N, ds, H):
+        return (B * N * 2 * ds + B * H * 4096 + B * H + 3) // 4 * 4
+
+    def _mailbox(self, n_layers, B, Ls, dm, ds, H, C, device):
+        """The p2p mailbox for this shape (collective on first use and on a shape change)."""
+        key = (n_layers, B, Ls, dm, ds, H, C)
+        if self._mb_key != key:
+            from .peer import PeerMailbox
+            if self._mb is not None:
+                self._mb.close()
+            self._lay = _Mailboxes(n_layers, self.world, self._carry_len(B, Ls // C, ds, H), B * 3 * dm * 2)
+            self._mb = PeerMailbox(self._lay.total, group=self.group, device=device)
+            self._mb_key = key
+        return self._mb, self._lay
+
+    def close(self):
+        """Release the p2p mailbox (collective)."""
+        if self._mb is not None:
+            self._mb.close()
+            self._mb = None
+            self._mb_key = None
+
+    def _begin(self, n_layers, h, blk):
+        if self.transport == "p2p":
+            B, Ls, dm = h.shape
+            mb, _ = self._mailbox(n_layers, B, Ls, dm, blk.d_state, blk.num_heads, blk.chunk_size, h.device)
+            mb.next_generation()
+
+    def _end(self):
+        if self.transport == "p2p":
+            self._mb.barrier(self._lay.bar)
+
+    def block(self, blk, h, layer=0):
         """One HdcMamba9v3Block on the local segment h [B, Ls, dm] (Ls a multiple of the
         chunk size; fixed semantics).  Returns the block output for the segment."""
         if blk.semantics != "fixed":
@@ -66,9 +140,25 @@ class SequenceParallel:
             raise ValueError(f"segment length {Ls} is not a multiple of the chunk size {C}")
         N = Ls // C
         h = h.contiguous()
-        # (1) halo: last three input rows of every rank; rank r uses rank r-1's
-        last3 = _all_gather(h[:, -3:, :], self.group)
-        halo = last3[self.rank - 1] if self.rank > 0 else None
+        p2p = self.transport == "p2p"
+        if p2p:
+            if self._mb is None:
+                raise RuntimeError("the p2p transport runs whole models: use SequenceParallel.model / .lm")
+            mb, lay = self._mb, self._lay
+        # (1) halo: the last three input rows of rank r-1
+        if p2p:
+            if self.rank < self.world - 1:
+                last3 = h[:, -3:, :]
+                if not last3.is_contiguous() or last3.data_ptr() % 16 or (last3.numel() * 2) % 16:
+                    last3 = last3.contiguous()
+                mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])
+            halo = None
+            if self.rank > 0:
+                mb.wait(lay.halo_flag(layer), [0])
+                halo = mb.view(lay.halo(layer), (B, 3, dm), h.dtype)
+        else:
+            last3 = _all_gather(h[:, -3:, :], self.group)
+            halo = last3[self.rank - 1] if self.rank > 0 else None
         x_conv = K.ln_conv(h, blk.norm.weight, blk.norm.bias, blk.conv1d.weight.squeeze(1), blk.conv1d.bias,
                            blk.norm.eps, halo=halo)
         projs = F.linear(x_conv, blk.in_proj.weight, blk.in_proj.bias)
@@ -79,13 +169,22 @@ class SequenceParallel:
         # (2) carries, written by the kernels straight into one flat fp32 buffer per rank:
         #     [SSM chunk statistics B*N*2ds | slot state B*H*4096 | slot decay B*H | pad]
         n_st, n_sl, n_dc = B * N * 2 * ds, B * H * 4096, B * H
-        n = (n_st + n_sl + n_dc + 3) // 4 * 4
-        flat = torch.empty(n, device=h.device, dtype=torch.float32)
+        n = self._carry_len(B, N, ds, H)
+        if p2p:  # this rank's slot of the layer's carry region
+            flat = mb.view(lay.carries(layer, self.rank), (n,), torch.float32)
+        else:
+            flat = torch.empty(n, device=h.device, dtype=torch.float32)
         K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
         ws = K.slot_workspace(B, Ls, H, hd, C, h.device)
         K.slot_state(k, v, H, C, gamma=gamma, state_out=flat[n_st:n_st + n_sl].view(B, H, 64, 64),
                      decay_out=flat[n_st + n_sl:n_st + n_sl + n_dc].view(B, H), workspace=ws)
-        g = _all_gather(flat, self.group).reshape(-1)                        # [W * n], rank-major
+        if p2p:  # to every higher rank; from every lower rank
+            mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
+                   range(self.rank + 1, self.world))
+            mb.wait(lay.carry_flags(layer), range(self.rank))
+            g = mb.view(lay.carries(layer), (self.world * n,), torch.float32)  # [W * n], rank-major
+        else:
+            g = _all_gather(flat, self.group).reshape(-1)                     # [W * n], rank-major
         combined = torch.empty(B, Ls, ds + dm, device=h.device, dtype=h.dtype)
         # SSM: exclusive prefix over the chunks of ranks < r, then this rank's, in place
         K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C, out=combined[..., :ds])
@@ -98,8 +197,10 @@ class SequenceParallel:
 
     def model(self, model, h):
         """HdcMamba9v3Model.forward on the local segment (hdcmamba/model.py:402-404)."""
-        for blk in model.layers:
-            h = self.block(blk, h)
+        self._begin(len(model.layers), h, model.layers[0])
+        for i, blk in enumerate(model.layers):
+            h = self.block(blk, h, layer=i)
+        self._end()
         return model.norm_final(h)
 
     def lm(self, lm, ids_local):
@@ -110,6 +211,8 @@ class SequenceParallel:
             if lm.use_model:
                 h = self.model(lm.backbone, h)
             else:
-                for blk in lm.layers:
-                    h = self.block(blk, h)
+                self._begin(len(lm.layers), h, lm.layers[0])
+                for i, blk in enumerate(lm.layers):
+                    h = self.block(blk, h, layer=i)
+                self._end()
             return F.linear(lm.norm(h), lm.embedding.weight)

@@ -255,6 +255,40 @@ int hdc_gate_cat_fwd(int dtype, const void* y_slot, int64_t slot_s_bh, int64_t s
 int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t rows, int64_t width,
                       float eps, hdc_stream_t stream);
 
+/*
+ * Peer-memory exchange for sequence parallelism (one process per GPU, NVLink / NVSwitch).
+ * No reference counterpart: it replaces the all-gathers of the sequence-parallel runner
+ * with direct peer stores where the data flow is one-directional (rank r needs the carries
+ * of ranks < r and the halo rows of rank r-1).  Every wait is bounded (~2 s) and reports a
+ * timeout through hdc_device_error().
+ *
+ * hdc_peer_alloc / hdc_peer_free: a zeroed device mailbox (cudaMalloc) that can be shared.
+ * hdc_ipc_handle / hdc_ipc_open / hdc_ipc_close: CUDA IPC handle (hdc_ipc_handle_bytes()
+ *   bytes) of a mailbox, and its mapping in another process of the same node.
+ * hdc_peer_put: for every target t with bit t of mask set, copy `bytes` from src (local,
+ *   16-byte aligned) to dst_base[t] + dst_off, then store *gen (a device counter) as a
+ *   uint32 flag at dst_base[t] + flag_off with release semantics at system scope.
+ *   dst_base is a device array of `world` mailbox base addresses as mapped in this process.
+ * hdc_peer_wait: wait until flags[s] has reached *gen (wrap-safe >=) for every bit s of mask
+ *   (acquire, system scope).
+ * hdc_peer_gen_bump: *gen += 1 (once per forward on every rank).
+ * hdc_peer_barrier: store *gen into slot `rank` of the uint32 array at base[s] + bar_off of
+ *   every rank s, then wait until all `world` slots of local_bar have reached *gen.
+ */
+int hdc_peer_alloc(size_t bytes, void** dev_ptr);
+int hdc_peer_free(void* dev_ptr);
+int hdc_ipc_handle_bytes(void);
+int hdc_ipc_handle(const void* dev_ptr, void* handle_out);
+int hdc_ipc_open(const void* handle, void** dev_ptr);
+int hdc_ipc_close(void* dev_ptr);
+int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_base, uint64_t dst_off,
+                 uint64_t flag_off, uint32_t mask, int world, const uint32_t* gen,
+                 hdc_stream_t stream);
+int hdc_peer_wait(const uint32_t* flags, uint32_t mask, const uint32_t* gen, hdc_stream_t stream);
+int hdc_peer_gen_bump(uint32_t* gen, hdc_stream_t stream);
+int hdc_peer_barrier(const uint64_t* base, uint64_t bar_off, int world, int rank,
+                     const uint32_t* local_bar, const uint32_t* gen, hdc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,7 @@ def _model():
     return reinit_(HdcMambaLM(4096, 256, 2, 64, 4, use_model=True)).eval()
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, transport="nccl"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -38,8 +38,9 @@ def _worker(rank, world, port, q):
         L = 4096
         ids = torch.randint(0, 4096, (1, L), generator=torch.Generator().manual_seed(1)).to(dev)
         Ls = L // world
-        sp = SequenceParallel()
+        sp = SequenceParallel(transport=transport)
         logits = sp.lm(lm, ids[:, rank * Ls:(rank + 1) * Ls].contiguous())
+        logits = sp.lm(lm, ids[:, rank * Ls:(rank + 1) * Ls].contiguous())  # a second generation
         out = torch.empty((world,) + tuple(logits.shape), device=dev, dtype=logits.dtype)
         dist.all_gather_into_tensor(out.reshape(-1), logits.contiguous().reshape(-1))
         torch.cuda.synchronize()
@@ -50,6 +51,7 @@ def _worker(rank, world, port, q):
             err = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
             q.put((err, _lib.load().hdc_device_error(1)))
         dist.barrier()
+        sp.close()
     except Exception as e:
         q.put(RuntimeError(f"rank {rank}: {type(e).__name__}: {e}"))
         raise
@@ -58,12 +60,15 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sequence_parallel_two_gpus_matches_one_gpu():
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_sequence_parallel_two_gpus_matches_one_gpu(transport):
+    """Both transports: NCCL all-gathers, and peer stores into IPC-mapped mailboxes with
+    generation flags (two forwards, so the second generation is exercised too)."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     res = q.get(timeout=600)
