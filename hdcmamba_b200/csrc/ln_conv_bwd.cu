@@ -1,0 +1,267 @@
+// Backward of the fused LayerNorm + causal depthwise conv1d (width 4), sm_100a.
+//
+// Same formulas as the reference _fused_norm_conv_bwd_kernel (hdcmamba/model.py:74-124)
+// and its launch (model.py:148-166), quirks included:
+//   dn[t]    = go[t] cw3 + go[t+1] cw2 + go[t+2] cw1 + go[t+3] cw0       (go = 0 past L)
+//   xhat[t]  = (x[t] - mean[t]) rstd[t]          (the forward's bf16-stored mean / rstd)
+//   dx[t]    = rstd[t] (dn nw - sum(dn nw)/D - xhat sum(dn nw xhat)/D)
+//   d_nw     = sum_t dn xhat,  d_nb = sum_t dn,  d_cb = sum_t go[t]
+//   d_cw[k]  = sum_t go[t] xhat[t-3+k] nw        (rows t-3+k < 0 contribute nothing, and
+//                                                 the norm bias is not part of the term)
+// Schedule (HBM-bound: read go, x; write dx):
+//   * one CTA walks a contiguous L-segment of one batch row; thread g owns channels
+//     [4g, 4g+4), loaded / stored as one 8-byte (bf16) or 16-byte (fp32) vector;
+//   * the four grad-output rows t..t+3 and the normalised rows t-3..t of its channels sit in
+//     register rings indexed by row mod 4; with segments of a multiple of 4 rows and the row
+//     loop unrolled by 4, every ring index is a compile-time constant;
+//   * the two row sums of the LayerNorm backward are reduced over the CTA once per 4 rows
+//     (warp shuffles, then shared memory; the two halves alternate, one barrier per group);
+//   * parameter gradients accumulate in registers per thread and are written per CTA to a
+//     workspace, which a second kernel sums over the CTAs in a fixed order (deterministic;
+//     the reference adds with fp32 atomics).
+#include "common.cuh"
+
+namespace hdc {
+
+struct LnConvBwdParams {
+  const void* go; const void* x; const __nv_bfloat16* mean; const __nv_bfloat16* rstd;
+  const void* nw; const void* cw; void* dx; float* part;
+  int L, D, seg_len, segs_per_b;
+};
+
+template <typename T>
+__device__ __forceinline__ void ld4(const T* p, float* f);
+template <>
+__device__ __forceinline__ void ld4<float>(const float* p, float* f) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+}
+template <>
+__device__ __forceinline__ void ld4<__nv_bfloat16>(const __nv_bfloat16* p, float* f) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  f[0] = __uint_as_float(v.x << 16); f[1] = __uint_as_float(v.x & 0xffff0000u);
+  f[2] = __uint_as_float(v.y << 16); f[3] = __uint_as_float(v.y & 0xffff0000u);
+}
+template <typename T>
+__device__ __forceinline__ void st4(T* p, const float* f);
+template <>
+__device__ __forceinline__ void st4<float>(float* p, const float* f) {
+  *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+}
+template <>
+__device__ __forceinline__ void st4<__nv_bfloat16>(__nv_bfloat16* p, const float* f) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), c = __floats2bfloat162_rn(f[2], f[3]);
+  uint2 v;
+  v.x = *reinterpret_cast<uint32_t*>(&a);
+  v.y = *reinterpret_cast<uint32_t*>(&c);
+  *reinterpret_cast<uint2*>(p) = v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512) ln_conv_bwd_kernel(LnConvBwdParams p) {
+  __shared__ float red[2][4][2][16];  // [half][row of the group][sum][warp]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int seg = blockIdx.x;
+  const int b = seg / p.segs_per_b;
+  const int l0 = (seg - b * p.segs_per_b) * p.seg_len;
+  const int l1 = min(l0 + p.seg_len, p.L);
+  const int c0 = tid * 4;
+  const bool act = c0 < p.D;
+  const int cc = act ? c0 : 0;
+  const size_t rowD = (size_t)p.D;
+  const T* go = static_cast<const T*>(p.go) + (size_t)b * p.L * rowD + cc;
+  const T* x = static_cast<const T*>(p.x) + (size_t)b * p.L * rowD + cc;
+  T* dx = static_cast<T*>(p.dx) + (size_t)b * p.L * rowD + cc;
+  const __nv_bfloat16* mean = p.mean + (size_t)b * p.L;
+  const __nv_bfloat16* rstd = p.rstd + (size_t)b * p.L;
+  const float invD = 1.0f / (float)p.D;
+
+  float nw[4], cw[4][4];  // cw[e][k]
+  ld4<T>(static_cast<const T*>(p.nw) + cc, nw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ld4<T>(static_cast<const T*>(p.cw) + (size_t)(cc + e) * 4, cw[e]);
+
+  auto load_go = [&](int t, float* f) {
+    if (act && t < p.L) ld4<T>(go + (size_t)t * rowD, f);
+    else f[0] = f[1] = f[2] = f[3] = 0.f;
+  };
+  auto xhat_nw = [&](int t, float* f) {  // xhat[t] * nw, zero for rows before the sequence
+    if (act && t >= 0) {
+      float v[4];
+      ld4<T>(x + (size_t)t * rowD, v);
+      const float m = __bfloat162float(mean[t]), r = __bfloat162float(rstd[t]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = (v[e] - m) * r * nw[e];
+    } else {
+      f[0] = f[1] = f[2] = f[3] = 0.f;
+    }
+  };
+  // rings: G[rho & 3] = go row l0 + rho, X[rho & 3] = xhat * nw of row l0 + rho
+  float G[4][4], X[4][4];
+  load_go(l0, G[0]);
+  load_go(l0 + 1, G[1]);
+  load_go(l0 + 2, G[2]);
+  xhat_nw(l0 - 3, X[1]);
+  xhat_nw(l0 - 2, X[2]);
+  xhat_nw(l0 - 1, X[3]);
+
+  float a_nw[4] = {0.f, 0.f, 0.f, 0.f}, a_nb[4] = {0.f, 0.f, 0.f, 0.f}, a_cb[4] = {0.f, 0.f, 0.f, 0.f};
+  float a_cw[4][4] = {};  // [k][e]
+  int half = 0;
+  for (int r4 = 0; r4 < l1 - l0; r4 += 4) {
+    float xh[4][4], dxh[4][4], s1[4], s2[4], rs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = l0 + r4 + u;
+      s1[u] = s2[u] = 0.f;
+      rs[u] = 0.f;
+      if (t < l1) {
+        load_go(t + 3, G[(u + 3) & 3]);
+        float v[4];
+        const float m = __bfloat162float(mean[t]), r = __bfloat162float(rstd[t]);
+        rs[u] = r;
+        if (act) ld4<T>(x + (size_t)t * rowD, v);
+        else v[0] = v[1] = v[2] = v[3] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float g0 = G[u][e];
+          const float dn = g0 * cw[e][3] + G[(u + 1) & 3][e] * cw[e][2] + G[(u + 2) & 3][e] * cw[e][1] +
+                           G[(u + 3) & 3][e] * cw[e][0];
+          const float xhat = act ? (v[e] - m) * r : 0.f;
+          const float xw = xhat * nw[e];
+          xh[u][e] = xhat;
+          dxh[u][e] = dn * nw[e];
+          s1[u] += dxh[u][e];
+          s2[u] += dxh[u][e] * xhat;
+          a_nw[e] += dn * xhat;
+          a_nb[e] += dn;
+          a_cb[e] += g0;
+          a_cw[3][e] += g0 * xw;
+          a_cw[2][e] += g0 * X[(u + 3) & 3][e];
+          a_cw[1][e] += g0 * X[(u + 2) & 3][e];
+          a_cw[0][e] += g0 * X[(u + 1) & 3][e];
+          X[u][e] = xw;
+        }
+      }
+    }
+    // the group's row sums over the CTA
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float a = warp_sum(s1[u]), c = warp_sum(s2[u]);
+      if (lane == 0) {
+        red[half][u][0][warp] = a;
+        red[half][u][1][warp] = c;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = l0 + r4 + u;
+      if (t >= l1 || !act) continue;
+      float S1 = 0.f, S2 = 0.f;
+      for (int w = 0; w < nwarps; ++w) {
+        S1 += red[half][u][0][w];
+        S2 += red[half][u][1][w];
+      }
+      S1 *= invD;
+      S2 *= invD;
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = rs[u] * (dxh[u][e] - S1 - xh[u][e] * S2);
+      st4<T>(dx + (size_t)t * rowD, o);
+    }
+    half ^= 1;
+  }
+  if (act) {
+    float* part = p.part + (size_t)seg * 7 * rowD + c0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      part[e] = a_nw[e];
+      part[rowD + e] = a_nb[e];
+      part[2 * rowD + e] = a_cb[e];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) part[(3 + k) * rowD + e] = a_cw[k][e];
+    }
+  }
+}
+
+// sums the per-CTA partials [nseg][7][D] in CTA order and casts to T:
+// dnw [D], dnb [D], dcb [D], dcw [D][4]
+template <typename T>
+__global__ void ln_conv_bwd_reduce_kernel(const float* part, int nseg, int D, T* dnw, T* dnb, T* dcw, T* dcb) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (row of 7, channel)
+  if (i >= 7 * D) return;
+  const int k = i / D, d = i - k * D;
+  float s = 0.f;
+  for (int c = 0; c < nseg; ++c) s += part[(size_t)c * 7 * D + i];
+  const T v = from_f<T>(s);
+  if (k == 0) dnw[d] = v;
+  else if (k == 1) dnb[d] = v;
+  else if (k == 2) dcb[d] = v;
+  else dcw[(size_t)d * 4 + (k - 3)] = v;
+}
+
+constexpr int kBwdMaxD = 2048;  // 512 threads x 4 channels
+
+static void bwd_plan(int64_t B, int64_t L, int* seg_len, int* segs_per_b) {
+  const int64_t target = (int64_t)num_sms() * 4;
+  int64_t spb = (target + B - 1) / B;
+  int64_t len = (L + spb - 1) / spb;
+  len = (len + 3) / 4 * 4;
+  if (len < 16) len = 16;
+  *seg_len = (int)len;
+  *segs_per_b = (int)((L + len - 1) / len);
+}
+
+}  // namespace hdc
+
+using namespace hdc;
+
+extern "C" size_t hdc_ln_conv_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D) {
+  if (B < 1 || L < 1 || D < 1) return 0;
+  int len, spb;
+  bwd_plan(B, L, &len, &spb);
+  return (size_t)B * spb * 7 * D * sizeof(float);
+}
+
+extern "C" int hdc_ln_conv_bwd(int dtype, const void* grad_out, const void* x, const void* mean, const void* rstd,
+                               const void* norm_w, const void* conv_w, void* dx, void* dnorm_w, void* dnorm_b,
+                               void* dconv_w, void* dconv_b, void* workspace, size_t workspace_bytes, int64_t B,
+                               int64_t L, int64_t D, hdc_stream_t stream) {
+  if (dtype != HDC_F32 && dtype != HDC_BF16) return fail(HDC_E_DTYPE, "ln_conv_bwd: dtype %d", dtype);
+  if (!grad_out || !x || !mean || !rstd || !norm_w || !conv_w || !dx || !dnorm_w || !dnorm_b || !dconv_w ||
+      !dconv_b || !workspace)
+    return fail(HDC_E_NULL, "ln_conv_bwd: null pointer");
+  if (B < 1 || L < 1 || D < 4 || D % 4 != 0 || D > kBwdMaxD || B * L > (int64_t)INT32_MAX)
+    return fail(HDC_E_SHAPE, "ln_conv_bwd: B=%lld L=%lld D=%lld (D a multiple of 4, <= %d)", (long long)B,
+                (long long)L, (long long)D, kBwdMaxD);
+  const size_t need = hdc_ln_conv_bwd_workspace_bytes(B, L, D);
+  if (workspace_bytes < need) return fail(HDC_E_WORKSPACE, "ln_conv_bwd: workspace %zu < %zu", workspace_bytes, need);
+  if (!aligned16(grad_out) || !aligned16(x) || !aligned16(dx) || !aligned16(norm_w) || !aligned16(conv_w) ||
+      !aligned16(workspace))
+    return fail(HDC_E_ALIGN, "ln_conv_bwd: pointers must be 16-byte aligned");
+  LnConvBwdParams p{};
+  p.go = grad_out; p.x = x; p.mean = static_cast<const __nv_bfloat16*>(mean);
+  p.rstd = static_cast<const __nv_bfloat16*>(rstd); p.nw = norm_w; p.cw = conv_w; p.dx = dx;
+  p.part = static_cast<float*>(workspace); p.L = (int)L; p.D = (int)D;
+  bwd_plan(B, L, &p.seg_len, &p.segs_per_b);
+  const int nseg = (int)(B * p.segs_per_b);
+  int threads = ((int)(D / 4) + 31) / 32 * 32;
+  if (threads < 64) threads = 64;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const int rgrid = (int)((7 * D + 255) / 256);
+  if (dtype == HDC_F32) {
+    ln_conv_bwd_kernel<float><<<nseg, threads, 0, s>>>(p);
+    if (int e = launch_status("ln_conv_bwd_kernel")) return e;
+    ln_conv_bwd_reduce_kernel<float><<<rgrid, 256, 0, s>>>(p.part, nseg, (int)D, static_cast<float*>(dnorm_w),
+                                                           static_cast<float*>(dnorm_b), static_cast<float*>(dconv_w),
+                                                           static_cast<float*>(dconv_b));
+  } else {
+    ln_conv_bwd_kernel<__nv_bfloat16><<<nseg, threads, 0, s>>>(p);
+    if (int e = launch_status("ln_conv_bwd_kernel")) return e;
+    ln_conv_bwd_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, s>>>(
+        p.part, nseg, (int)D, static_cast<__nv_bfloat16*>(dnorm_w), static_cast<__nv_bfloat16*>(dnorm_b),
+        static_cast<__nv_bfloat16*>(dconv_w), static_cast<__nv_bfloat16*>(dconv_b));
+  }
+  return launch_status("ln_conv_bwd_reduce_kernel");
+}

@@ -35,36 +35,24 @@ def _require_cuda(x):
 class FusedNormConv1dFunction(torch.autograd.Function):
     """LayerNorm + causal depthwise conv1d (hdcmamba/model.py:126-166).
 
-    forward(x, norm_weight, norm_bias, conv_weight[D,4], conv_bias, eps) -> out."""
+    forward(x, norm_weight, norm_bias, conv_weight[D,4], conv_bias, eps) -> out.
+    backward runs ``hdc_ln_conv_bwd``: the reference's backward formulas
+    (model.py:74-124), which leave the norm bias and the rows before the sequence out
+    of the conv-weight and norm-bias gradients."""
 
     @staticmethod
     def forward(ctx, x, norm_weight, norm_bias, conv_weight, conv_bias, eps):
         _require_cuda(x)
         out, mean, rstd = ops.ln_conv(x, norm_weight, norm_bias, conv_weight, conv_bias, eps, stats=True)
-        ctx.save_for_backward(x, norm_weight, norm_bias, conv_weight, conv_bias)
+        ctx.save_for_backward(x, norm_weight, conv_weight, mean, rstd)
         ctx.eps = eps
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        # Gradients by autograd through an fp32 recompute on the same device.
-        x, nw, nb, cw, cb = ctx.saved_tensors
-        with torch.enable_grad():
-            xs = x.detach().float().requires_grad_(x.requires_grad)
-            ps = [t.detach().float().requires_grad_(t.requires_grad) for t in (nw, nb, cw, cb)]
-            B, L, D = xs.shape
-            n = F.layer_norm(xs, (D,), ps[0], ps[1], ctx.eps)
-            # rows before t = 0 are LayerNorm(0) = norm_bias (hdcmamba/model.py:47-57)
-            npad = torch.cat([ps[1].expand(B, 3, D), n], 1)
-            y = F.conv1d(npad.transpose(1, 2), ps[2].reshape(D, 1, 4), ps[3], groups=D).transpose(1, 2)
-            grads = torch.autograd.grad(y, [t for t in [xs, *ps] if t.requires_grad], grad_out.float(),
-                                        allow_unused=True)
-        it = iter(grads)
-        out = []
-        for t, src in zip([xs, *ps], [x, nw, nb, cw, cb]):
-            g = next(it) if t.requires_grad else None
-            out.append(None if g is None else g.to(src.dtype))
-        return (*out, None)
+        x, nw, cw, mean, rstd = ctx.saved_tensors
+        dx, dnw, dnb, dcw, dcb = ops.ln_conv_bwd(grad_out, x, mean, rstd, nw, cw)
+        return dx, dnw.to(nw.dtype), dnb.to(nw.dtype), dcw.reshape(cw.shape).to(cw.dtype), dcb.to(nw.dtype), None
 
 
 def fused_norm_conv1d_trainable(x, norm_layer, conv_layer):

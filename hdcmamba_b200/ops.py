@@ -69,6 +69,32 @@ def ln_conv(x, norm_w, norm_b, conv_w, conv_b, eps=1e-5, act="none", halo=None, 
 
 
 # ------------------------------------------------------------------ SSM scan
+def ln_conv_bwd(grad_out, x, mean, rstd, norm_w, conv_w):
+    """Backward of ``ln_conv`` (act="none"): the reference's FusedNormConv1dFunction.backward
+    (hdcmamba/model.py:74-124, 148-166), its formulas included.  ``mean`` / ``rstd`` are the
+    forward's bf16 statistics.  Returns (dx, d_norm_w, d_norm_b, d_conv_w [D, 4], d_conv_b)
+    in x.dtype."""
+    _cuda(grad_out, x, mean, rstd, norm_w, conv_w)
+    B, L, D = x.shape
+    grad_out = grad_out.contiguous()
+    x = x.contiguous()
+    _same_dtype(x, grad_out)
+    nw = norm_w.to(x.dtype).contiguous()
+    cw = conv_w.reshape(D, 4).to(x.dtype).contiguous()
+    mean = mean.to(torch.bfloat16).contiguous()
+    rstd = rstd.to(torch.bfloat16).contiguous()
+    dx = torch.empty_like(x)
+    dnw = torch.empty(D, device=x.device, dtype=x.dtype)
+    dnb = torch.empty_like(dnw)
+    dcw = torch.empty(D, 4, device=x.device, dtype=x.dtype)
+    dcb = torch.empty_like(dnw)
+    ws = torch.empty(max(int(_lib.load().hdc_ln_conv_bwd_workspace_bytes(B, L, D)), 16), device=x.device,
+                     dtype=torch.uint8)
+    _lib.call("hdc_ln_conv_bwd", _code(x), _p(grad_out), _p(x), _p(mean), _p(rstd), _p(nw), _p(cw), _p(dx), _p(dnw),
+              _p(dnb), _p(dcw), _p(dcb), _p(ws), ws.numel(), B, L, D, _stream(x))
+    return dx, dnw, dnb, dcw, dcb
+
+
 def _row_view(t, what):
     """(batch stride, row stride) of a [B, L, cols] view whose last dim is unit-stride."""
     if t.dim() != 3 or t.stride(2) != 1:

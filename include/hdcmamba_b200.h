@@ -67,6 +67,24 @@ int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* no
                     hdc_stream_t stream);
 
 /*
+ * Backward of hdc_ln_conv_fwd (no activation): the reference's
+ * _fused_norm_conv_bwd_kernel + FusedNormConv1dFunction.backward (hdcmamba/model.py:74-124,
+ * 148-166), with its formulas: dx through the LayerNorm backward on the forward's bf16
+ * mean / rstd ([B*L] bf16 from hdc_ln_conv_fwd); d_conv_w[d][k] = sum_t go[t] *
+ * xhat[t-3+k] * nw (no norm-bias term, nothing from the rows before the sequence);
+ * d_norm_b = sum_t dn[t] over real rows; d_conv_b = sum_t go[t].  Parameter gradients are
+ * summed in fp32 (per CTA, then over the CTAs in a fixed order) and stored in dtype:
+ * d_norm_w / d_norm_b / d_conv_b [D], d_conv_w [D, 4].  grad_out, x, dx: [B, L, D]
+ * contiguous.  D a multiple of 4, at most 2048; pointers 16-byte aligned; workspace of
+ * hdc_ln_conv_bwd_workspace_bytes(B, L, D) bytes.
+ */
+size_t hdc_ln_conv_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D);
+int hdc_ln_conv_bwd(int dtype, const void* grad_out, const void* x, const void* mean, const void* rstd,
+                    const void* norm_w, const void* conv_w, void* dx, void* dnorm_w, void* dnorm_b,
+                    void* dconv_w, void* dconv_b, void* workspace, size_t workspace_bytes, int64_t B,
+                    int64_t L, int64_t D, hdc_stream_t stream);
+
+/*
  * Diagonal SSM chunk statistics (pass 1 of the chunked scan).
  * Replaces _ssm_intra_v2's last_state / chunk_decay outputs (hdcmamba/model.py:175-198,
  * launched at 345-350).  For batch b and chunk n (C steps), per channel j < ds:

@@ -38,7 +38,8 @@ import torch
 import torch.nn.functional as F
 
 __all__ = [
-    "kernel_rounding", "bf16r", "kbf16", "next_pow2", "feature_block", "ln_conv_fwd", "ssm_chunk_fwd",
+    "kernel_rounding", "bf16r", "kbf16", "next_pow2", "feature_block", "ln_conv_fwd", "ln_conv_bwd",
+    "ssm_chunk_fwd",
     "ssm_chunk_states", "ssm_prefix", "slot_fwd", "gnorm_gate_cat",
     "combined_layer_norm", "block_forward", "model_forward", "lm_forward",
     "slot_scan_decay_fwd",
@@ -143,6 +144,40 @@ def ln_conv_fwd(x, norm_w, norm_b, conv_w, conv_b, eps: float, act: str = "none"
     elif act != "none":
         raise ValueError(f"unknown activation {act!r}")
     return _kstore(out, dtype), _kstore(mean, torch.bfloat16), _kstore(rstd, torch.bfloat16)
+
+
+def ln_conv_bwd(grad_out, x, mean, rstd, norm_w, conv_w):
+    """Restates ``_fused_norm_conv_bwd_kernel`` (model.py:74-124) and its launch in
+    ``FusedNormConv1dFunction.backward`` (model.py:148-166), reference quirks included:
+
+    * ``dn[t] = sum_k go[t+3-k] cw[:,k]`` with go = 0 beyond the sequence end;
+    * dx is the LayerNorm backward with the forward's bf16-stored mean / rstd
+      (``mean.float()``, ``rstd.float()``, model.py:159);
+    * ``d_cw[:,k] = sum_t go[t] * xhat[t-3+k] * nw`` -- the normalised input *without* the
+      norm bias, and nothing from the three zero rows before the sequence (t-3+k < 0),
+      although the forward uses LayerNorm(0) = norm_b there (model.py:112-121);
+    * ``d_nb = sum_t dn[t]`` over real rows only; ``d_cb = sum_t go[t]``.
+
+    Returns (dx in x.dtype, dnorm_w, dnorm_b, dconv_w [D, 4], dconv_b), the parameter
+    gradients accumulated in fp32 and cast to x.dtype (model.py:166)."""
+    dtype = x.dtype
+    B, L, D = x.shape
+    go = grad_out.float()
+    xf = x.float()
+    m = mean.float()[..., None]
+    r = rstd.float()[..., None]
+    nw = norm_w.float()
+    cw = conv_w.reshape(D, 4).float()
+    gp = torch.cat([go, go.new_zeros(B, 3, D)], 1)
+    dn = gp[:, 0:L] * cw[:, 3] + gp[:, 1:L + 1] * cw[:, 2] + gp[:, 2:L + 2] * cw[:, 1] + gp[:, 3:L + 3] * cw[:, 0]
+    xhat = (xf - m) * r
+    dxhat = dn * nw
+    dx = r * (dxhat - dxhat.sum(-1, keepdim=True) / D - xhat * ((dxhat * xhat).sum(-1, keepdim=True) / D))
+    xw = xhat * nw
+    dcw = torch.stack([(go[:, 3:] * xw[:, :L - 3]).sum((0, 1)), (go[:, 2:] * xw[:, :L - 2]).sum((0, 1)),
+                       (go[:, 1:] * xw[:, :L - 1]).sum((0, 1)), (go * xw).sum((0, 1))], -1)
+    return (_kstore(dx, dtype), (dn * xhat).sum((0, 1)).to(dtype), dn.sum((0, 1)).to(dtype), dcw.to(dtype),
+            go.sum((0, 1)).to(dtype))
 
 
 # ---------------------------------------------------------------------------

@@ -95,6 +95,34 @@ def case_lnconv(M, triton):
     npsave("lnconv", **res)
 
 
+def case_lnconv_bwd(M, triton):
+    """The reference's own backward (FusedNormConv1dFunction.backward, model.py:148-166)
+    through autograd, with the forward's mean / rstd recorded for the restatement."""
+    g = torch.Generator().manual_seed(13)
+    res = {}
+    for tag, (B, L, D, dt) in {"f32": (2, 37, 96, torch.float32), "bf16": (2, 40, 72, torch.bfloat16)}.items():
+        x = h16(torch.randn(B, L, D, generator=g)).to(dt).requires_grad_(True)
+        nw = (1 + 0.1 * torch.randn(D, generator=g)).to(dt).requires_grad_(True)
+        nb = (0.1 * torch.randn(D, generator=g)).to(dt).requires_grad_(True)
+        cw = (0.3 * torch.randn(D, 4, generator=g)).to(dt).requires_grad_(True)
+        cb = (0.1 * torch.randn(D, generator=g)).to(dt).requires_grad_(True)
+        go = h16(torch.randn(B, L, D, generator=g)).to(dt)
+        out = M.FusedNormConv1dFunction.apply(x, nw, nb, cw, cb, 1e-5)
+        out.backward(go)
+        mean = torch.empty(B, L, dtype=torch.bfloat16)
+        rstd = torch.empty(B, L, dtype=torch.bfloat16)
+        out2 = torch.empty_like(x)
+        M._fused_norm_conv_fwd_kernel[(B, triton.cdiv(L, 16))](
+            x.detach(), nw.detach(), nb.detach(), cw.detach(), cb.detach(), out2, mean, rstd, B, L, D,
+            *x.stride(), *out2.stride(), eps=1e-5, BLOCK_L=16, BLOCK_D=triton.next_power_of_2(D), num_warps=4,
+            num_stages=1)
+        res.update({f"{tag}_x": x.detach(), f"{tag}_nw": nw.detach(), f"{tag}_nb": nb.detach(),
+                    f"{tag}_cw": cw.detach(), f"{tag}_cb": cb.detach(), f"{tag}_go": go, f"{tag}_mean": mean,
+                    f"{tag}_rstd": rstd, f"{tag}_dx": x.grad, f"{tag}_dnw": nw.grad, f"{tag}_dnb": nb.grad,
+                    f"{tag}_dcw": cw.grad, f"{tag}_dcb": cb.grad})
+    npsave("lnconv_bwd", **res)
+
+
 def run_ssm(M, projs, A_log, ds, C):
     B, L, _ = projs.shape
     N = L // C
@@ -296,7 +324,8 @@ def main():
     a = ap.parse_args()
     torch.set_num_threads(8)
     M, triton = load_reference(a.ref)
-    todo = {"lnconv": lambda: case_lnconv(M, triton), "ssm": lambda: case_ssm(M), "slot": lambda: case_slot(M),
+    todo = {"lnconv": lambda: case_lnconv(M, triton), "lnconv_bwd": lambda: case_lnconv_bwd(M, triton),
+            "ssm": lambda: case_ssm(M), "slot": lambda: case_slot(M),
             "gate": lambda: case_gate(M), "block": lambda: case_block(M),
             "fixed_c256": lambda: case_fixed_c256(M, triton), "c1": lambda: case_c1(M)}
     for name, fn in todo.items():

@@ -125,25 +125,51 @@ def test_train_mode_gradients_match_reference_behaviour():
     assert x.grad is not None
 
 
-def test_fused_norm_conv_function_backward():
-    torch.manual_seed(3)
-    B, L, D = 2, 50, 64
-    x = torch.randn(B, L, D, device=DEV, requires_grad=True)
-    nw = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_()
-    nb = (0.1 * torch.randn(D, device=DEV)).requires_grad_()
-    cw = (0.3 * torch.randn(D, 4, device=DEV)).requires_grad_()
-    cb = (0.1 * torch.randn(D, device=DEV)).requires_grad_()
+@pytest.mark.parametrize("dtype,B,L,D", [(torch.float32, 2, 50, 64), (torch.bfloat16, 2, 300, 768),
+                                         (torch.float32, 1, 37, 2048), (torch.bfloat16, 3, 129, 96)])
+def test_fused_norm_conv_function_backward(dtype, B, L, D):
+    """FusedNormConv1dFunction.backward (hdc_ln_conv_bwd) against the oracle restatement of
+    the reference's backward on the forward's bf16 statistics; dx also against autograd."""
+    import oracle as O
+    from hdcmamba_b200 import ops
+    g = torch.Generator().manual_seed(3 + D)
+    x = torch.randn(B, L, D, generator=g).to(dtype).to(DEV).requires_grad_()
+    nw = (1 + 0.1 * torch.randn(D, generator=g)).to(dtype).to(DEV).requires_grad_()
+    nb = (0.1 * torch.randn(D, generator=g)).to(dtype).to(DEV).requires_grad_()
+    cw = (0.3 * torch.randn(D, 4, generator=g)).to(dtype).to(DEV).requires_grad_()
+    cb = (0.1 * torch.randn(D, generator=g)).to(dtype).to(DEV).requires_grad_()
+    go = torch.randn(B, L, D, generator=g).to(dtype).to(DEV)
     out = FusedNormConv1dFunction.apply(x, nw, nb, cw, cb, 1e-5)
-    go = torch.randn_like(out)
     out.backward(go)
-    xs = x.detach().clone().requires_grad_()
-    ps = [t.detach().clone().requires_grad_() for t in (nw, nb, cw, cb)]
-    n = torch.nn.functional.layer_norm(xs, (D,), ps[0], ps[1], 1e-5)
-    npad = torch.cat([ps[1].expand(B, 3, D), n], 1)
-    ref = sum(npad[:, k:k + L] * ps[2][:, k] for k in range(4)) + ps[3]
-    ref.backward(go)
-    for a, b in zip([x, nw, nb, cw, cb], [xs, *ps]):
-        torch.testing.assert_close(a.grad, b.grad, rtol=1e-4, atol=1e-4)
+    torch.cuda.synchronize()
+    assert _lib.load().hdc_device_error(1) == 0
+    _, mean, rstd = ops.ln_conv(x.detach(), nw.detach(), nb.detach(), cw.detach(), cb.detach(), 1e-5, stats=True)
+    ref = O.ln_conv_bwd(go.cpu(), x.detach().cpu(), mean.cpu(), rstd.cpu(), nw.detach().cpu(), cw.detach().cpu())
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    for got, r, name in zip([x.grad, nw.grad, nb.grad, cw.grad, cb.grad], ref, ["dx", "dnw", "dnb", "dcw", "dcb"]):
+        assert got.dtype == dtype and got.shape == r.shape, name
+        assert rel(got, r) < tol, (name, rel(got, r))
+    # dx is the LayerNorm backward proper (on bf16-rounded statistics)
+    xs = x.detach().float().requires_grad_()
+    y = torch.nn.functional.layer_norm(xs, (D,), nw.detach().float(), None, 1e-5)
+    dn = sum(torch.cat([go.float(), go.new_zeros(B, 3, D).float()], 1)[:, 3 - k:3 - k + L] * cw.detach().float()[:, k]
+             for k in range(4))
+    y.backward(dn)
+    assert rel(x.grad, xs.grad) < 2e-2
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_ln_conv_bwd_reference_golden(tag):
+    """hdc_ln_conv_bwd on the inputs and bf16 statistics recorded from the reference's own
+    backward (interpreter; its bf16 stores truncate, the GPU rounds to nearest)."""
+    from hdcmamba_b200 import ops
+    import golden
+    gd = golden.load("lnconv_bwd")
+    d = {k: gd[f"{tag}_{k}"].to(DEV) for k in ("go", "x", "mean", "rstd", "nw", "cw")}
+    out = ops.ln_conv_bwd(d["go"], d["x"], d["mean"], d["rstd"], d["nw"], d["cw"])
+    for got, key in zip(out, ["dx", "dnw", "dnb", "dcw", "dcb"]):
+        r = gd[f"{tag}_{key}"]
+        assert rel(got, r) < (1e-4 if tag == "f32" else 2e-2), (key, rel(got, r))
 
 
 def test_repeated_forward_has_no_device_timeouts():

@@ -50,6 +50,36 @@ def test_lnconv_matches_reference(tag):
     torch.testing.assert_close(rstd.float(), g[f"{tag}_rstd"].float(), rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+@rtz
+def test_lnconv_bwd_matches_reference(tag):
+    """The restated backward against the reference's own FusedNormConv1dFunction.backward
+    (model.py:148-166) run under the interpreter, on the forward's bf16 mean / rstd."""
+    g = golden.load("lnconv_bwd")
+    dx, dnw, dnb, dcw, dcb = O.ln_conv_bwd(g[f"{tag}_go"], g[f"{tag}_x"], g[f"{tag}_mean"], g[f"{tag}_rstd"],
+                                           g[f"{tag}_nw"], g[f"{tag}_cw"])
+    for got, key in ((dx, "dx"), (dnw, "dnw"), (dnb, "dnb"), (dcw, "dcw"), (dcb, "dcb")):
+        ref = g[f"{tag}_{key}"]
+        assert got.dtype == ref.dtype and got.shape == ref.shape, key
+        # the reference sums rows per 16-row program and across programs with fp32 atomics
+        assert relmax(got, ref) < (1e-5 if tag == "f32" else 1e-2), (key, relmax(got, ref))
+
+
+def test_lnconv_bwd_quirks_are_material():
+    """The reference's conv-weight / norm-bias gradients leave out the norm bias and the
+    three zero rows before the sequence: they differ from autograd of the forward."""
+    g = golden.load("lnconv_bwd")
+    x, nw, nb, cw, cb, go = (g[f"f32_{k}"].clone().requires_grad_(True) for k in ("x", "nw", "nb", "cw", "cb", "go"))
+    B, L, D = x.shape
+    n = torch.nn.functional.layer_norm(x, (D,), nw, nb, 1e-5)
+    npad = torch.cat([nb.expand(B, 3, D), n], 1)
+    y = sum(npad[:, k:k + L] * cw[:, k] for k in range(4)) + cb
+    y.backward(go)
+    assert relmax(g["f32_dcw"], cw.grad) > 1e-2  # nb missing from xhat * nw
+    assert relmax(g["f32_dnb"], nb.grad) > 1e-3   # padded rows missing
+    torch.testing.assert_close(g["f32_dcb"], cb.grad, rtol=1e-4, atol=1e-4)
+
+
 @pytest.mark.parametrize("tag", ["f32c64", "f32c32", "bf16c64"])
 @rtz
 def test_ssm_matches_reference(tag):
