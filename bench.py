@@ -150,6 +150,24 @@ def kernel_c2(dev, iters, hbm):
             "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm}
 
 
+def kernel_c2bwd(dev, iters, hbm):
+    """Backward of config 2's LN + conv (the reference's FusedNormConv1dFunction.backward
+    formulas, hdc_ln_conv_bwd): grad_out and x read, dx written, bf16 [8, 8192, 2048]."""
+    from hdcmamba_b200 import ops
+    B, L, D = 8, 8192, 2048
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, L, D, device=dev, generator=g).bfloat16()
+    go = torch.randn(B, L, D, device=dev, generator=g).bfloat16()
+    cw = (0.02 * torch.randn(D, 4, device=dev, generator=g)).bfloat16()
+    nw, nb, cb = (torch.ones(D, device=dev).bfloat16(), torch.zeros(D, device=dev).bfloat16(),
+                  torch.zeros(D, device=dev).bfloat16())
+    _, mean, rstd = ops.ln_conv(x, nw, nb, cw, cb, 1e-5, stats=True)
+    ms = _time_cuda(lambda: ops.ln_conv_bwd(go, x, mean, rstd, nw, cw), iters)
+    nbytes = 3 * B * L * D * 2
+    return {"workload": "c2bwd: ln_conv backward bf16 [8,8192,2048]", "ms_per_launch": ms,
+            "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm}
+
+
 def kernel_c3(dev, iters, hbm):
     """slot scan with per-step decay, q/k/v bf16 [4, 32768, 16, 64],
     a = sigmoid(N(0,1)) fp32, chunk 64, zero initial state, final state returned."""
@@ -262,7 +280,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
     ap.add_argument("--eager", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--workload", default=None, choices=["c2", "c3", "c5slot"],
+    ap.add_argument("--workload", default=None, choices=["c2", "c2bwd", "c3", "c5slot"],
                     help="time one kernel workload alone (for profiling) and print its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -278,7 +296,7 @@ def main():
     if args.workload:
         torch.cuda.set_device(local)
         dev = torch.device("cuda", local)
-        fn = {"c2": kernel_c2, "c3": kernel_c3, "c5slot": kernel_c5slot}[args.workload]
+        fn = {"c2": kernel_c2, "c2bwd": kernel_c2bwd, "c3": kernel_c3, "c5slot": kernel_c5slot}[args.workload]
         print(json.dumps(fn(dev, args.steps, peaks()[0])), flush=True)
         return
 
@@ -472,7 +490,8 @@ def main():
             "clocks": clocks,
         }
         if world == 1 and not args.no_kernels:
-            line["kernels"] = [kernel_c2(dev, 20, hbm), kernel_c3(dev, 10, hbm), kernel_c5slot(dev, 10, hbm)]
+            line["kernels"] = [kernel_c2(dev, 20, hbm), kernel_c2bwd(dev, 10, hbm), kernel_c3(dev, 10, hbm),
+                               kernel_c5slot(dev, 10, hbm)]
         if world == 1 and not args.no_cpu_baseline:
             v, cores = cpu_oracle_tokens_per_s(cfg, args.cpu_tokens)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
