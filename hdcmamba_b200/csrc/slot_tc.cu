@@ -278,6 +278,9 @@ struct OutCfg {
   static constexpr int NWG = CT == 64 ? 2 : 4;           // warpgroups
   static constexpr int NT = NWG * 128;
   static constexpr int EPW = 64 / NWG;                   // accumulator columns per warpgroup
+  static constexpr int AG = EPW < 16 ? EPW : 16;         // accumulator columns per TMEM access
+  static constexpr int PW = NWG == 8 ? 16 : 32;          // columns of one S / P piece
+  static constexpr int SRED = 2 * NWG;                   // GroupNorm partials per row
   static constexpr int MINB = CT == 64 ? 2 : 1;          // resident CTAs per SM
   static constexpr bool INPLACE = RB == 128;             // Yi / Yx inside the S columns
   static constexpr int ncol(int rb) { return (rb + 1) * RB; }      // S columns of block rb
@@ -289,7 +292,7 @@ struct OutCfg {
   static constexpr int TMEM_COLS = RCOL + 64 <= 256 ? 256 : 512;
   static constexpr int pbase(int rb) { return rb == 0 ? 0 : RB * ncol(0) * 2; }  // bytes into sP
   static constexpr int PBYTES = NRB == 1 ? RB * ncol(0) * 2 : RB * (ncol(0) + ncol(1)) * 2;
-  static constexpr int NCHUNK = SCOLS / 32;              // 32-column pieces of S / P
+  static constexpr int NCHUNK = SCOLS / PW;              // PW-column pieces of S / P
   static constexpr int CPW = NCHUNK / NWG;               // pieces per warpgroup
   static_assert(CPW * NWG == NCHUNK, "S pieces must split evenly over the warpgroups");
 };
@@ -300,6 +303,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
                        const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
   using Cfg = OutCfg<CT>;
   constexpr int NT = Cfg::NT, RB = Cfg::RB, NRB = Cfg::NRB, NWG = Cfg::NWG, EPW = Cfg::EPW;
+  constexpr int AG = Cfg::AG, PW = Cfg::PW, SRED = Cfg::SRED;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   uint8_t* sK = base;                       // phi(K), then k~ = bf16(phi(K) * kdec) in place
@@ -309,11 +313,11 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   uint8_t* sR = sP + Cfg::PBYTES;           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
   float* sGn = sTab + CT + 4;                              // [128] gn weight | bias of this head
-  float* sRed = sGn + 128;                                 // [CT][8] GroupNorm partial sums
+  float* sRed = sGn + 128;                                 // [CT][SRED] GroupNorm partial sums
   // mbarriers: [0] K + V loads, [1] S products, [2] P.V / Yx / state products, [3] Q loads.
   // Each commit follows a CTA barrier, so no thread can fall two phases behind on a
   // barrier (which would alias the parity).
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * 8);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * SRED);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -364,16 +368,16 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   // [e0, e0 + EPW)) + sR (bf16)
   float Rr[EPW];
 #pragma unroll
-  for (int pc = 0; pc < EPW / 16; ++pc) {
-    float* Rp = Rr + pc * 16;
+  for (int pc = 0; pc < EPW / AG; ++pc) {
+    float* Rp = Rr + pc * AG;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) Rp[e] = 0.f;
-    const int c0 = e0 + pc * 16;
+    for (int e = 0; e < AG; ++e) Rp[e] = 0.f;
+    const int c0 = e0 + pc * AG;
     if (f_valid) {
       if (p.state_in) {
         const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + c0;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) Rp[e] = src[e];
+        for (int e = 0; e < AG; ++e) Rp[e] = src[e];
       }
       // (unrolled so that the loads of several parts are in flight together)
 #pragma unroll 4
@@ -382,7 +386,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         const float4* src = reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride +
                                                             (size_t)bh * 4096 + f_row * 64 + c0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < AG / 4; ++e) {
           const float4 v = src[e];
           Rp[4 * e] = Ds * Rp[4 * e] + v.x;
           Rp[4 * e + 1] = Ds * Rp[4 * e + 1] + v.y;
@@ -395,7 +399,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
         const float4* src = reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + c0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int e = 0; e < AG / 4; ++e) {
           const float4 v = src[e];
           Rp[4 * e] = Ds * Rp[4 * e] + v.x;
           Rp[4 * e + 1] = Ds * Rp[4 * e + 1] + v.y;
@@ -404,7 +408,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         }
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < AG / 8; ++c)
         *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (c0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rp[c * 8]);
     }
   }
@@ -488,27 +492,27 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 #pragma unroll
     for (int cc = 0; cc < Cfg::CPW; ++cc) {
       const int c = wg * Cfg::CPW + cc;
-      const int rb = (NRB == 2 && c * 32 >= Cfg::ncol(0)) ? 1 : 0;
-      const int j0 = c * 32 - (rb ? Cfg::ncol(0) : 0);           // first column of the piece
+      const int rb = (NRB == 2 && c * PW >= Cfg::ncol(0)) ? 1 : 0;
+      const int j0 = c * PW - (rb ? Cfg::ncol(0) : 0);           // first column of the piece
       const int ib = rb * RB;                                     // first row of the block
       uint8_t* pb = sP + Cfg::pbase(rb);
       if (j0 > ib + row_hi) {  // above the diagonal for every row of this warp: zeros
         if (my_row >= 0) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
+          for (int q = 0; q < PW / 8; ++q)
             *reinterpret_cast<uint4*>(pb + ((j0 + q * 8) >> 6) * (RB * 128) +
                                       sw128_chunk(my_row, ((j0 + q * 8) & 63) >> 3)) = make_uint4(0, 0, 0, 0);
         }
         continue;
       }
-      float sv[32];
-      tmem_ld32(tL + Cfg::scol(rb) + j0, sv);
+      float sv[PW];
+      tmem_ldn<PW>(tL + Cfg::scol(rb) + j0, sv);
       if (my_row < 0) continue;
       const int i = ib + my_row;
-      const bool full = j0 + 31 <= ib + row_lo;  // no masking for any row of this warp
+      const bool full = j0 + PW - 1 <= ib + row_lo;  // no masking for any row of this warp
       const float ci = PERSTEP ? sTab[i] : 0.f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < PW / 8; ++q) {
         float v[8];
         if (!PERSTEP && full) {
           // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e
@@ -564,11 +568,11 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
       const int i_row = rb * RB + (my_row >= 0 ? my_row : 0);
       const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
 #pragma unroll
-      for (int pc = 0; pc < EPW / 16; ++pc) {
-        float yi[16], yx[16];
-        tmem_ld16x2(tL + Cfg::yi(rb) + e0 + pc * 16, tL + Cfg::yx(rb) + e0 + pc * 16, yi, yx);
+      for (int pc = 0; pc < EPW / AG; ++pc) {
+        float yi[AG], yx[AG];
+        tmem_ldn2<AG>(tL + Cfg::yi(rb) + e0 + pc * AG, tL + Cfg::yx(rb) + e0 + pc * AG, yi, yx);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) o[rb][pc * 16 + e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is bf16
+        for (int e = 0; e < AG; ++e) o[rb][pc * AG + e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is bf16
       }
     }
     if (GATE) {
@@ -578,7 +582,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         float sum = 0.f;
 #pragma unroll
         for (int e = 0; e < EPW; ++e) sum += (e0 + e < p.hd) ? o[rb][e] : 0.f;
-        if (my_row >= 0) sRed[(rb * RB + my_row) * 8 + wg] = sum;
+        if (my_row >= 0) sRed[(rb * RB + my_row) * SRED + wg] = sum;
       }
       named_bar_sync(1 + quarter, NWG * 32);  // the warps holding these rows
 #pragma unroll
@@ -586,7 +590,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         mean[rb] = 0.f;
         if (my_row >= 0) {
 #pragma unroll
-          for (int w = 0; w < NWG; ++w) mean[rb] += sRed[(rb * RB + my_row) * 8 + w];
+          for (int w = 0; w < NWG; ++w) mean[rb] += sRed[(rb * RB + my_row) * SRED + w];
           mean[rb] *= fast_rcp((float)p.hd);
         }
         float sq = 0.f;
@@ -595,7 +599,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
           const float d = o[rb][e] - mean[rb];
           sq += (e0 + e < p.hd) ? d * d : 0.f;
         }
-        if (my_row >= 0) sRed[(rb * RB + my_row) * 8 + 4 + wg] = sq;
+        if (my_row >= 0) sRed[(rb * RB + my_row) * SRED + NWG + wg] = sq;
       }
       named_bar_sync(1 + quarter, NWG * 32);
       if (my_row >= 0) {
@@ -603,7 +607,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
         for (int rb = 0; rb < NRB; ++rb) {
           float ssq = 0.f;
 #pragma unroll
-          for (int w = 0; w < NWG; ++w) ssq += sRed[(rb * RB + my_row) * 8 + 4 + w];
+          for (int w = 0; w < NWG; ++w) ssq += sRed[(rb * RB + my_row) * SRED + NWG + w];
           // the reference's padded lanes (block width 64) add (64 - hd) * mean^2
           const float var = (ssq + (float)(64 - p.hd) * mean[rb] * mean[rb]) / (float)p.hd;
           const float inv = rsqrtf(var + 1e-5f);
@@ -646,16 +650,16 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     {
       const float gC = PERSTEP ? fast_exp(sTab[CT]) : sTab[CT];
 #pragma unroll
-      for (int pc = 0; pc < EPW / 16; ++pc) {
-        float u[16];
-        tmem_ld16(tR + e0 + pc * 16, u);
-        float* Rp = Rr + pc * 16;
+      for (int pc = 0; pc < EPW / AG; ++pc) {
+        float u[AG];
+        tmem_ldn<AG>(tR + e0 + pc * AG, u);
+        float* Rp = Rr + pc * AG;
 #pragma unroll
-        for (int e = 0; e < 16; ++e) Rp[e] = fmaf(Rp[e], gC, u[e]);
+        for (int e = 0; e < AG; ++e) Rp[e] = fmaf(Rp[e], gC, u[e]);
         if (f_valid) {
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, ((e0 + pc * 16) >> 3) + c)) =
+          for (int c = 0; c < AG / 8; ++c)
+            *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, ((e0 + pc * AG) >> 3) + c)) =
                 pack16<__nv_bfloat16>(&Rp[c * 8]);
         }
       }
@@ -672,12 +676,12 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   }
   if (ok && seg == p.nseg - 1 && p.state_out) {
 #pragma unroll
-    for (int pc = 0; pc < EPW / 16; ++pc) {
-      const float* r = Rr + pc * 16;
+    for (int pc = 0; pc < EPW / AG; ++pc) {
+      const float* r = Rr + pc * AG;
       if (f_valid) {
-        float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0 + pc * 16;
+        float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0 + pc * AG;
 #pragma unroll
-        for (int e = 0; e < 16; e += 4)
+        for (int e = 0; e < AG; e += 4)
           *reinterpret_cast<float4*>(dst + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
       }
     }
@@ -725,7 +729,7 @@ static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, 
 
 template <int CT>
 static size_t smem_out_bytes() {
-  return 1024 + 3 * CT * 128 + OutCfg<CT>::PBYTES + 64 * 128 + (CT + 4 + 128 + CT * 8) * 4 + 64;
+  return 1024 + 3 * CT * 128 + OutCfg<CT>::PBYTES + 64 * 128 + (CT + 4 + 128 + CT * OutCfg<CT>::SRED) * 4 + 64;
 }
 static size_t smem_state_bytes(int CT) { return 1024 + 4 * CT * 128 + (CT + 4) * 4 + 64; }
 

@@ -219,6 +219,46 @@ __device__ __forceinline__ float fast_sigmoid(float x) {
   return fmaf(0.5f, t, 0.5f);
 }
 
+// 8-column variants (warp lane quarter x 8 columns, 32-bit each) and one wait.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld8x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(ta), "r"(tb)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[8 + i]);
+  }
+}
+
+// Column-count dispatch of the loads above (N = 8, 16 or 32; the pair form N = 8 or 16).
+template <int N>
+__device__ __forceinline__ void tmem_ldn(uint32_t taddr, float* v) {
+  static_assert(N == 8 || N == 16 || N == 32, "tmem_ldn: 8, 16 or 32 columns");
+  if constexpr (N == 8) tmem_ld8(taddr, v);
+  else if constexpr (N == 16) tmem_ld16(taddr, v);
+  else tmem_ld32(taddr, v);
+}
+template <int N>
+__device__ __forceinline__ void tmem_ldn2(uint32_t ta, uint32_t tb, float* va, float* vb);
+
 // Two 16-column TMEM loads (columns [a, a+16) and [b, b+16)) and one wait.
 __device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
   uint32_t r[32];
@@ -239,6 +279,14 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va,
     va[i] = __uint_as_float(r[i]);
     vb[i] = __uint_as_float(r[16 + i]);
   }
+}
+template <>
+__device__ __forceinline__ void tmem_ldn2<8>(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  tmem_ld8x2(ta, tb, va, vb);
+}
+template <>
+__device__ __forceinline__ void tmem_ldn2<16>(uint32_t ta, uint32_t tb, float* va, float* vb) {
+  tmem_ld16x2(ta, tb, va, vb);
 }
 
 // Two 32-column TMEM loads (columns [a, a+32) and [b, b+32)) and one wait.
