@@ -134,8 +134,9 @@ __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float*
 // ---------------------------------------------------------------------------------
 constexpr int kStateThreads = 512;
 
+// (chunk 64 / 128: two CTAs per SM fit in shared memory, so registers are capped for it)
 template <int CT, bool PERSTEP>
-__global__ void __launch_bounds__(kStateThreads, 1)
+__global__ void __launch_bounds__(kStateThreads, CT == 256 ? 1 : 2)
     slot_tc_state_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
                          SlotTcParams p) {
   constexpr int NT = kStateThreads;
