@@ -168,6 +168,33 @@ def kernel_c2bwd(dev, iters, hbm):
             "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm}
 
 
+def decode_c5(dev, batch, steps=64):
+    """Recurrent decode of the config-5 model (hdcmamba_b200.decode): a 256-token prompt,
+    then ``steps`` single-token steps per sequence replayed as one CUDA graph; tokens/s =
+    batch / step time."""
+    from hdcmamba_b200.decode import GraphedDecode, prefill
+    from hdcmamba_b200.lm import CONFIGS, build_lm
+    cfg = CONFIGS["c5"]
+    lm = build_lm(cfg).to(dev).bfloat16()
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab, (batch, 256 + steps + 3), generator=g).to(dev)
+    _, st = prefill(lm, ids[:, :256])
+    gd = GraphedDecode(lm, st, ids[:, 256])
+    for t in range(3):
+        gd(ids[:, 256 + t])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(steps):
+        gd(ids[:, 259 + t])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del gd, st, lm
+    return {"workload": f"decode c5 (12x d768, 256-token prompt), batch {batch}", "ms_per_step": ms,
+            "tokens_per_s": batch / (ms * 1e-3)}
+
+
 def kernel_c3(dev, iters, hbm):
     """slot scan with per-step decay, q/k/v bf16 [4, 32768, 16, 64],
     a = sigmoid(N(0,1)) fp32, chunk 64, zero initial state, final state returned."""
@@ -492,6 +519,8 @@ def main():
         if world == 1 and not args.no_kernels:
             line["kernels"] = [kernel_c2(dev, 20, hbm), kernel_c2bwd(dev, 10, hbm), kernel_c3(dev, 10, hbm),
                                kernel_c5slot(dev, 10, hbm)]
+        if world == 1 and not args.no_kernels:
+            line["decode"] = [decode_c5(dev, 1), decode_c5(dev, 64)]
         if world == 1 and not args.no_cpu_baseline:
             v, cores = cpu_oracle_tokens_per_s(cfg, args.cpu_tokens)
             line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",

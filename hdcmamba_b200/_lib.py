@@ -56,6 +56,11 @@ SIGNATURES = {
     "hdc_gate_cat_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
                                  c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_row_layernorm": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, c_float, c_vp]),
+    "hdc_ln_conv_step": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_float, c_vp]),
+    "hdc_ssm_step": (c_int, [c_int, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
+    "hdc_ssm_carry_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "hdc_slot_step": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                              c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "hdc_peer_alloc": (c_int, [c_size, ctypes.POINTER(c_vp)]),
     "hdc_peer_free": (c_int, [c_vp]),
     "hdc_ipc_handle_bytes": (c_int, []),

@@ -377,3 +377,64 @@ def row_layernorm(x, eps=1e-5, out=None):
     width = x.shape[-1]
     _lib.call("hdc_row_layernorm", _code(x), _p(x), _p(out), x.numel() // width, width, float(eps), _stream(x))
     return out
+
+
+# ------------------------------------------------------------------ single-token decode
+def ln_conv_step(x, norm_w, norm_b, conv_w, conv_b, window, eps=1e-5, out=None):
+    """LN + conv of one new row per sequence, x [B, D]; ``window`` fp32 [B, 3, D] (the
+    normalised rows t-3..t-1) is shifted in place (hdc_ln_conv_step)."""
+    _cuda(x, norm_w, norm_b, conv_w, conv_b, window, out)
+    B, D = x.shape
+    x = x.contiguous()
+    if window.dtype != torch.float32 or tuple(window.shape) != (B, 3, D) or not window.is_contiguous():
+        raise ValueError(f"window must be a contiguous fp32 [{B}, 3, {D}] tensor")
+    dt = x.dtype
+    out = torch.empty_like(x) if out is None else out
+    _lib.call("hdc_ln_conv_step", _code(x), _p(x), _p(norm_w.to(dt).contiguous()), _p(norm_b.to(dt).contiguous()),
+              _p(conv_w.reshape(D, 4).to(dt).contiguous()), _p(conv_b.to(dt).contiguous()), _p(window), _p(out), B, D,
+              float(eps), _stream(x))
+    return out
+
+
+def ssm_step(projs, A_log, h, cum, G, d_state, pos, chunk, out):
+    """One diagonal-SSM step for rows projs [B, P]; h / cum / G fp32 [B, ds] updated in
+    place; ``pos`` a device int32 tensor holding the row index within the chunk (the chunk
+    is folded into G at row chunk-1); writes out [B, >=ds] (unit column stride)."""
+    _cuda(projs, A_log, h, cum, G, out, pos)
+    B = projs.shape[0]
+    if projs.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("projs / out need a unit column stride")
+    a = A_log.to(projs.dtype).contiguous()
+    _lib.call("hdc_ssm_step", _code(projs), _p(projs), projs.stride(0), _p(a), _p(h), _p(cum), _p(G), _p(out),
+              out.stride(0), B, d_state, _p(pos), chunk, _stream(projs))
+    return out
+
+
+def ssm_carry(stats, dtype):
+    """Carry G [B, ds] fp32 after the chunks of ``stats`` [B, N, 2ds] (hdc_ssm_carry_fwd);
+    ``dtype`` is the activation dtype (selects the exp of that prefill path)."""
+    _cuda(stats)
+    B, N, two_ds = stats.shape
+    G = torch.empty(B, two_ds // 2, device=stats.device, dtype=torch.float32)
+    code = 1 if dtype == torch.bfloat16 else 0
+    _lib.call("hdc_ssm_carry_fwd", code, _p(stats.contiguous()), B, N, two_ds // 2, _p(G), _stream(stats))
+    return G
+
+
+def slot_step(q, k, v, gate, num_heads, gamma, gn_w, gn_b, R, U, k_cache, v_cache, out, pos):
+    """The next row (index in the device int32 ``pos``) of the current chunk of the slot
+    scan with GroupNorm(head) * sigmoid(gate) (hdc_slot_step).  q / k / v / gate: [B, H*hd] views sharing one batch stride; R / U fp32
+    [B, H, 64, 64]; k_cache / v_cache [B, H, C, 64]; out [B, H*hd] view (unit column stride)."""
+    _cuda(q, k, v, gate, gamma, gn_w, gn_b, R, U, k_cache, v_cache, out, pos)
+    B, W = q.shape
+    H = num_heads
+    hd = W // H
+    C = k_cache.shape[2]
+    if not (q.stride() == k.stride() == v.stride() == gate.stride()) or q.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("q / k / v / gate must share strides with unit column stride")
+    dt = q.dtype
+    _lib.call("hdc_slot_step", _code(q), _p(q), _p(k), _p(v), _p(gate), q.stride(0), _p(gamma.to(dt).contiguous()),
+              _p(gn_w.to(dt).contiguous()), _p(gn_b.to(dt).contiguous()), _p(R), _p(U), _p(k_cache), _p(v_cache),
+              _p(out), out.stride(0), B, H, hd, C, _p(pos), _stream(q))
+    return out
+

@@ -274,6 +274,41 @@ int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t rows, int64_
                       float eps, hdc_stream_t stream);
 
 /*
+ * Recurrent single-token decode (no reference counterpart: the reference's generation
+ * re-runs the whole prefix).  The state continues the chunked prefill one row at a time
+ * with the prefill's formulas and rounding points (bf16 activations: the tcgen05 path's;
+ * fp32: the CUDA-core path and the gate kernel's):
+ * hdc_ln_conv_step: x [B, D] -> out [B, D]; window fp32 [B, 3, D] holds the normalised
+ *   rows t-3, t-2, t-1 and is shifted in place.
+ * hdc_ssm_step: one step of the diagonal SSM from projs rows [B, >=3ds] (batch stride
+ *   proj_sb); h / cum / G fp32 [B, ds] are the chunk-local state, its summed log decay and
+ *   the carry of the earlier chunks; *pos (device int32, the row index within the chunk of
+ *   C rows) == C-1 folds the chunk into G.  y element (b, j) at y + b*y_sb + j.
+ * hdc_ssm_carry_fwd: G after the N chunks whose statistics (hdc_ssm_chunk_stats, fp32
+ *   [B, N, 2ds]) are given, folded in chunk order.
+ * hdc_slot_step: row i of the current chunk of the slot scan, fused with GroupNorm(head) *
+ *   sigmoid(gate); one CTA per (batch, head).  q / k / v / gate: [B, H*hd] rows of projs
+ *   (batch stride proj_sb); R / U fp32 [B*H, 64, 64] (state at the chunk start, update of
+ *   the chunk so far); k_cache / v_cache [B*H, C, 64] in dtype (the chunk's phi(k) / v rows);
+ *   out element (b, h, d) at out + b*out_sb + h*hd + d.  The row index i is read from the
+ *   device int32 *pos (0 <= i < C; otherwise nothing is written and hdc_device_error
+ *   reports 51).  hd <= 64, C <= 256.  The position lives on the device so that a decode
+ *   step can be replayed as a CUDA graph.
+ */
+int hdc_ln_conv_step(int dtype, const void* x, const void* norm_w, const void* norm_b, const void* conv_w,
+                     const void* conv_b, float* window, void* out, int64_t B, int64_t D, float eps,
+                     hdc_stream_t stream);
+int hdc_ssm_step(int dtype, const void* projs, int64_t proj_sb, const void* A_log, float* h, float* cum,
+                 float* G, void* y, int64_t y_sb, int64_t B, int64_t ds, const int32_t* pos, int64_t C,
+                 hdc_stream_t stream);
+int hdc_ssm_carry_fwd(int dtype, const float* stats, int64_t B, int64_t N, int64_t ds, float* G,
+                      hdc_stream_t stream);
+int hdc_slot_step(int dtype, const void* q, const void* k, const void* v, const void* gate, int64_t proj_sb,
+                  const void* gamma, const void* gn_w, const void* gn_b, float* R, float* U, void* k_cache,
+                  void* v_cache, void* out, int64_t out_sb, int64_t B, int64_t H, int64_t hd, int64_t C,
+                  const int32_t* pos, hdc_stream_t stream);
+
+/*
  * Peer-memory exchange for sequence parallelism (one process per GPU, NVLink / NVSwitch).
  * No reference counterpart: it replaces the all-gathers of the sequence-parallel runner
  * with direct peer stores where the data flow is one-directional (rank r needs the carries
