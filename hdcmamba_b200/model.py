@@ -27,6 +27,18 @@ from . import ops
 __all__ = ["HdcMamba9v3Block", "HdcMamba9v3Model", "FusedNormConv1dFunction", "fused_norm_conv1d_trainable"]
 
 
+_SIDE_STREAMS = {}
+
+
+def _side_stream(device):
+    """A second stream per device for work that overlaps the slot scan (the SSM scan)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _SIDE_STREAMS.get(idx)
+    if st is None:
+        st = _SIDE_STREAMS[idx] = torch.cuda.Stream(device=idx)
+    return st
+
+
 def _require_cuda(x):
     if not x.is_cuda:
         raise RuntimeError("hdcmamba_b200 runs on CUDA devices only; move the module and input to a B200")
@@ -111,11 +123,16 @@ class HdcMamba9v3Block(nn.Module):
         combined = torch.empty(B, L, ds + dm, device=x.device, dtype=x.dtype)
         P = projs.shape[-1]
         if self.semantics == "fixed" and ops.slot_gate_supported(q, H, C):
-            # SSM written into combined[..., :ds]; slot scan with GroupNorm * sigmoid(gate)
-            # fused into its epilogue, written into combined[..., ds:]
-            ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
+            # SSM written into combined[..., :ds] on a side stream, concurrently with the slot
+            # scan (GroupNorm * sigmoid(gate) fused into its epilogue) into combined[..., ds:]
+            cur = torch.cuda.current_stream(x.device)
+            side = _side_stream(x.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
             ops.slot_scan_gate(q, k, v, H, C, projs[..., so + 3 * dm:], self.group_norm.weight,
                                self.group_norm.bias, combined[..., ds:], (L * (ds + dm), hd, ds + dm), gamma=gamma)
+            cur.wait_stream(side)
         elif self.semantics == "fixed":
             y_ssm = ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
             y_slot = torch.empty(B * H, N, C, hd, device=x.device, dtype=x.dtype)

@@ -118,6 +118,13 @@ class SequenceParallel:
             self._mb = None
             self._mb_key = None
 
+    def _side(self, h):
+        """The side stream for the SSM kernels (CUDA kernels only; None for CPU stand-ins)."""
+        if not h.is_cuda or not isinstance(self.k, CudaKernels):
+            return None
+        from .model import _side_stream
+        return _side_stream(h.device)
+
     def _begin(self, n_layers, h, blk):
         if self.transport == "p2p":
             B, Ls, dm = h.shape
@@ -174,10 +181,19 @@ class SequenceParallel:
             flat = mb.view(lay.carries(layer, self.rank), (n,), torch.float32)
         else:
             flat = torch.empty(n, device=h.device, dtype=torch.float32)
-        K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
+        side = self._side(h)
+        if side is not None:  # the SSM kernels overlap the slot kernels on a second stream
+            cur = torch.cuda.current_stream(h.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
+        else:
+            K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
         ws = K.slot_workspace(B, Ls, H, hd, C, h.device)
         K.slot_state(k, v, H, C, gamma=gamma, state_out=flat[n_st:n_st + n_sl].view(B, H, 64, 64),
                      decay_out=flat[n_st + n_sl:n_st + n_sl + n_dc].view(B, H), workspace=ws)
+        if side is not None:
+            cur.wait_stream(side)  # the carries are complete before they are exchanged
         if p2p:  # to every higher rank; from every lower rank
             mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
                    range(self.rank + 1, self.world))
@@ -186,12 +202,21 @@ class SequenceParallel:
         else:
             g = _all_gather(flat, self.group).reshape(-1)                     # [W * n], rank-major
         combined = torch.empty(B, Ls, ds + dm, device=h.device, dtype=h.dtype)
-        # SSM: exclusive prefix over the chunks of ranks < r, then this rank's, in place
-        K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C, out=combined[..., :ds])
+        # SSM: exclusive prefix over the chunks of ranks < r, then this rank's, in place (on
+        # the side stream, next to the slot output kernel)
+        if side is not None:
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C,
+                                       out=combined[..., :ds])
+        else:
+            K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C, out=combined[..., :ds])
         # slot: fold the states of ranks < r in rank order, then the local segments
         K.slot_scan_gate_carry(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias, combined[..., ds:],
                                (Ls * (ds + dm), hd, ds + dm), g[n_st:], g[n_st + n_sl:], n, self.rank, ws,
                                gamma=gamma)
+        if side is not None:
+            cur.wait_stream(side)
         combined = K.row_layernorm(combined, 1e-5, out=combined)
         return torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
 
