@@ -36,7 +36,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
-template <typename T, int VPT>
+template <typename T, int VPT, bool SILU>
 __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   constexpr int VEC = Vec<T>::N;
   extern __shared__ uint8_t smem_raw[];
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
               float v = fmaf(W[kk][(u + 1) & 3][e], c0[kk][e],
                              fmaf(W[kk][(u + 2) & 3][e], c1[kk][e],
                                   fmaf(W[kk][(u + 3) & 3][e], c2[kk][e], fmaf(n0, c3[kk][e], cb[kk][e]))));
-              if (p.act == HDC_ACT_SILU) v *= fast_sigmoid(v);
+              if (SILU) v *= fast_sigmoid(v);
               o[e] = v;
               W[kk][u][e] = n0;
             }
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   }
 }
 
-template <typename T, int VPT>
+template <typename T, int VPT, bool SILU>
 static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   const int G = p.D / Vec<T>::N;
   int threads = ((G + VPT - 1) / VPT + 31) / 32 * 32;
@@ -244,9 +244,9 @@ static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   while (smem_of(tile, nst) > 110 * 1024 && nst > 2) --nst;
   while (smem_of(tile, nst) > 200 * 1024 && tile > 4) tile -= 4;
   const size_t smem = smem_of(tile, nst);
-  cudaFuncSetAttribute(ln_conv_kernel<T, VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaFuncSetAttribute(ln_conv_kernel<T, VPT, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int occ = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ln_conv_kernel<T, VPT>, threads, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ln_conv_kernel<T, VPT, SILU>, threads, smem);
   if (occ < 1) occ = 1;
   const int64_t target = (int64_t)num_sms() * occ;
   int64_t segs_per_b = (target + B - 1) / B;
@@ -259,14 +259,15 @@ static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   p.total_segs = (int)(B * segs_per_b);
   p.tile = tile;
   p.nst = nst;
-  ln_conv_kernel<T, VPT><<<p.total_segs, threads, smem, stream>>>(p);
+  ln_conv_kernel<T, VPT, SILU><<<p.total_segs, threads, smem, stream>>>(p);
   return launch_status("ln_conv_kernel");
 }
 
 template <typename T>
 static int ln_conv_dispatch(LnConvParams p, int64_t B, cudaStream_t stream) {
   const int G = p.D / Vec<T>::N;
-  if (G <= 512) return launch_ln_conv<T, 1>(p, B, stream);
+  if (G <= 512)
+    return p.act == HDC_ACT_SILU ? launch_ln_conv<T, 1, true>(p, B, stream) : launch_ln_conv<T, 1, false>(p, B, stream);
   return fail(HDC_E_SHAPE, "ln_conv: D=%d too large", p.D);
 }
 
