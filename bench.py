@@ -195,6 +195,70 @@ def decode_c5(dev, batch, steps=64):
             "tokens_per_s": batch / (ms * 1e-3)}
 
 
+def layer_c5(dev, hbm, seq_len=32768, iters=10):
+    """Per-op device time of one config-5 layer (B1, d768, H12, ds64, C256) at ``seq_len``:
+    each op replayed as a CUDA graph between CUDA events, after a read-only pass over 512 MB
+    that leaves L2 clean; ``floor_us`` is the same measurement of an empty op (graph launch
+    and event overhead, included in every figure)."""
+    import statistics as st_
+    import torch.nn.functional as F
+    from hdcmamba_b200 import ops
+    from hdcmamba_b200.lm import CONFIGS, build_lm
+    cfg = CONFIGS["c5"]
+    torch.manual_seed(0)
+    blk = build_lm(cfg).backbone.layers[0].to(dev).bfloat16()
+    flush = torch.ones(256 << 20, dtype=torch.float16, device=dev)
+    sink = torch.empty((), dtype=torch.float16, device=dev)
+
+    def timed(fn):
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        ev = []
+        for _ in range(iters + 1):
+            torch.amax(flush, dim=0, out=sink)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            ev.append((a, b))
+        torch.cuda.synchronize()
+        return round(st_.mean(a.elapsed_time(b) for a, b in ev[1:]) * 1000, 1)
+
+    B, L, dm, ds, H, C = 1, seq_len, cfg.d_model, cfg.d_state, cfg.num_heads, cfg.chunk_size
+    hd = dm // H
+    h = torch.randn(B, L, dm, device=dev).bfloat16()
+    res = {"workload": f"c5 layer ops, B1 L{L} d{dm}", "unit": "us per op (includes floor_us)"}
+    with torch.no_grad():
+        lnargs = (blk.norm.weight, blk.norm.bias, blk.conv1d.weight.squeeze(1), blk.conv1d.bias, 1e-5)
+        xc = ops.ln_conv(h, *lnargs)
+        projs = F.linear(xc, blk.in_proj.weight, blk.in_proj.bias)
+        so = 3 * ds
+        q, k, v = projs[..., so:so + dm], projs[..., so + dm:so + 2 * dm], projs[..., so + 2 * dm:so + 3 * dm]
+        gate = projs[..., so + 3 * dm:]
+        gamma = blk.gamma_buf.to(h.dtype)
+        stats = ops.ssm_chunk_stats(projs, blk.A_log, ds, C)
+        comb = torch.empty(B, L, ds + dm, device=dev, dtype=h.dtype)
+        res["floor_us"] = timed(lambda: sink.add_(0))
+        res["ln_conv"] = timed(lambda: ops.ln_conv(h, *lnargs))
+        res["in_proj"] = timed(lambda: F.linear(xc, blk.in_proj.weight, blk.in_proj.bias))
+        res["ssm_chunk_stats"] = timed(lambda: ops.ssm_chunk_stats(projs, blk.A_log, ds, C))
+        res["ssm_scan_out"] = timed(lambda: ops.ssm_scan_out(projs, blk.A_log, stats, 0, ds, C, out=comb[..., :ds]))
+        res["slot_scan_gate"] = timed(lambda: ops.slot_scan_gate(q, k, v, H, C, gate, blk.group_norm.weight,
+                                                                 blk.group_norm.bias, comb[..., ds:],
+                                                                 (L * (ds + dm), hd, ds + dm), gamma=gamma))
+        res["row_layernorm"] = timed(lambda: ops.row_layernorm(comb, 1e-5, out=comb))
+        res["out_proj"] = timed(lambda: torch.addmm(h.reshape(-1, dm), comb.reshape(-1, ds + dm),
+                                                    blk.out_proj.weight.t()))
+    del flush
+    return res
+
+
 def kernel_c3(dev, iters, hbm):
     """slot scan with per-step decay, q/k/v bf16 [4, 32768, 16, 64],
     a = sigmoid(N(0,1)) fp32, chunk 64, zero initial state, final state returned."""
@@ -307,7 +371,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
     ap.add_argument("--eager", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--workload", default=None, choices=["c2", "c2bwd", "c3", "c5slot"],
+    ap.add_argument("--workload", default=None, choices=["c2", "c2bwd", "c3", "c5slot", "c5layer"],
                     help="time one kernel workload alone (for profiling) and print its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -323,6 +387,10 @@ def main():
     if args.workload:
         torch.cuda.set_device(local)
         dev = torch.device("cuda", local)
+        if args.workload == "c5layer":
+            for L in (4096, 32768):  # a sequence-parallel rank's length at 8 GPUs, and one GPU's
+                print(json.dumps(layer_c5(dev, peaks()[0], seq_len=L, iters=args.steps)), flush=True)
+            return
         fn = {"c2": kernel_c2, "c2bwd": kernel_c2bwd, "c3": kernel_c3, "c5slot": kernel_c5slot}[args.workload]
         print(json.dumps(fn(dev, args.steps, peaks()[0])), flush=True)
         return
