@@ -29,12 +29,6 @@ struct LnConvParams {
   float eps; int act;
 };
 
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
 
 template <typename T, int VPT, bool SILU>
 __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {

@@ -19,7 +19,7 @@
 //   * parameter gradients accumulate in registers per thread and are written per CTA to a
 //     workspace, which a second kernel sums over the CTAs in a fixed order (deterministic;
 //     the reference adds with fp32 atomics).
-#include "common.cuh"
+#include "tc.cuh"
 
 namespace hdc {
 
@@ -154,17 +154,18 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_kernel(LnConvBwdParams p) {
       }
     }
     __syncthreads();
+    // every warp reduces the warps' partials itself: one shared load per lane, then shuffles
+    float S1v[4], S2v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      S1v[u] = warp_sum(lane < nwarps ? red[half][u][0][lane] : 0.f) * invD;
+      S2v[u] = warp_sum(lane < nwarps ? red[half][u][1][lane] : 0.f) * invD;
+    }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int t = l0 + r4 + u;
       if (t >= l1 || !act) continue;
-      float S1 = 0.f, S2 = 0.f;
-      for (int w = 0; w < nwarps; ++w) {
-        S1 += red[half][u][0][w];
-        S2 += red[half][u][1][w];
-      }
-      S1 *= invD;
-      S2 *= invD;
+      const float S1 = S1v[u], S2 = S2v[u];
       float o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[e] = rs[u] * (dxh[u][e] - S1 - xh[u][e] * S2);
@@ -182,6 +183,186 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_kernel(LnConvBwdParams p) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) part[(3 + k) * rowD + e] = a_cw[k][e];
     }
+  }
+}
+
+// The same computation with the rows staged through shared memory: tile k of a CTA holds the
+// x rows of its steps [l0 + k TR, +TR) and the grad rows three ahead, brought in by bulk TMA
+// copies (rows are contiguous) into a two-stage ring; a stage is refilled after the CTA
+// barrier that ends the last 4-row group of its tile.  Rows of a multiple of 16 bytes.
+template <typename T>
+__global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams p, int TR) {
+  __shared__ float red[2][4][2][16];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int seg = blockIdx.x;
+  const int b = seg / p.segs_per_b;
+  const int l0 = (seg - b * p.segs_per_b) * p.seg_len;
+  const int l1 = min(l0 + p.seg_len, p.L);
+  const int c0 = tid * 4;
+  const bool act = c0 < p.D;
+  const int cc = act ? c0 : 0;
+  const size_t rowD = (size_t)p.D;
+  const uint32_t row_bytes = (uint32_t)(p.D * sizeof(T));
+  const uint32_t tile_bytes = (uint32_t)TR * row_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + 4 * (size_t)tile_bytes);  // [2]
+  const T* gob = static_cast<const T*>(p.go) + (size_t)b * p.L * rowD;
+  const T* xb = static_cast<const T*>(p.x) + (size_t)b * p.L * rowD;
+  const T* go = gob + cc;
+  const T* x = xb + cc;
+  T* dx = static_cast<T*>(p.dx) + (size_t)b * p.L * rowD + cc;
+  const __nv_bfloat16* mean = p.mean + (size_t)b * p.L;
+  const __nv_bfloat16* rstd = p.rstd + (size_t)b * p.L;
+  const float invD = 1.0f / (float)p.D;
+  const int ntiles = (l1 - l0 + TR - 1) / TR;
+
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int k) {  // tile k: x rows t0.., grad rows t0+3.. (clipped to the sequence)
+    const int st = k & 1;
+    const int t0 = l0 + k * TR;
+    const int nx = min(TR, l1 - t0);
+    const int ng = max(0, min(TR, p.L - (t0 + 3)));
+    uint8_t* sx = ring + (size_t)st * 2 * tile_bytes;
+    mbar_expect_tx(&bars[st], (uint32_t)(nx + ng) * row_bytes);
+    bulk_g2s(sx, xb + (size_t)t0 * rowD, (uint32_t)nx * row_bytes, &bars[st]);
+    if (ng > 0) bulk_g2s(sx + tile_bytes, gob + (size_t)(t0 + 3) * rowD, (uint32_t)ng * row_bytes, &bars[st]);
+  };
+  if (tid == 0) {
+    if (ntiles > 0) issue(0);
+    if (ntiles > 1) issue(1);
+  }
+
+  float nw[4], cw[4][4];
+  ld4<T>(static_cast<const T*>(p.nw) + cc, nw);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ld4<T>(static_cast<const T*>(p.cw) + (size_t)(cc + e) * 4, cw[e]);
+  auto load_go = [&](int t, float* f) {
+    if (act && t < p.L) ld4<T>(go + (size_t)t * rowD, f);
+    else f[0] = f[1] = f[2] = f[3] = 0.f;
+  };
+  auto xhat_nw = [&](int t, float* f) {
+    if (act && t >= 0) {
+      float v[4];
+      ld4<T>(x + (size_t)t * rowD, v);
+      const float m = __bfloat162float(mean[t]), r = __bfloat162float(rstd[t]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) f[e] = (v[e] - m) * r * nw[e];
+    } else {
+      f[0] = f[1] = f[2] = f[3] = 0.f;
+    }
+  };
+  float G[4][4], X[4][4];
+  load_go(l0, G[0]);
+  load_go(l0 + 1, G[1]);
+  load_go(l0 + 2, G[2]);
+  xhat_nw(l0 - 3, X[1]);
+  xhat_nw(l0 - 2, X[2]);
+  xhat_nw(l0 - 1, X[3]);
+
+  float a_nw[4] = {0.f, 0.f, 0.f, 0.f}, a_nb[4] = {0.f, 0.f, 0.f, 0.f}, a_cb[4] = {0.f, 0.f, 0.f, 0.f};
+  float a_cw[4][4] = {};
+  int half = 0;
+  uint32_t ph0 = 0, ph1 = 0;
+  bool ok = true;
+  for (int r4 = 0; r4 < l1 - l0 && ok; r4 += 4) {
+    const int k = r4 / TR, rk = r4 - k * TR, st = k & 1;
+    if (rk == 0) {  // first group of tile k: its rows have landed
+      if (!mbar_wait_warp(&bars[st], st ? ph1 : ph0, 34)) { ok = false; break; }
+      if (st) ph1 ^= 1; else ph0 ^= 1;
+    }
+    const uint8_t* sx = ring + (size_t)st * 2 * tile_bytes;
+    float xh[4][4], dxh[4][4], s1[4], s2[4], rs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = l0 + r4 + u;
+      s1[u] = s2[u] = 0.f;
+      rs[u] = 0.f;
+      if (t < l1) {
+        const int r = rk + u;
+        if (act && t + 3 < p.L) ld4<T>(reinterpret_cast<const T*>(sx + tile_bytes + (size_t)r * row_bytes) + cc,
+                                       G[(u + 3) & 3]);
+        else G[(u + 3) & 3][0] = G[(u + 3) & 3][1] = G[(u + 3) & 3][2] = G[(u + 3) & 3][3] = 0.f;
+        float v[4];
+        const float m = __bfloat162float(mean[t]), rr = __bfloat162float(rstd[t]);
+        rs[u] = rr;
+        if (act) ld4<T>(reinterpret_cast<const T*>(sx + (size_t)r * row_bytes) + cc, v);
+        else v[0] = v[1] = v[2] = v[3] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float g0 = G[u][e];
+          const float dn = g0 * cw[e][3] + G[(u + 1) & 3][e] * cw[e][2] + G[(u + 2) & 3][e] * cw[e][1] +
+                           G[(u + 3) & 3][e] * cw[e][0];
+          const float xhat = act ? (v[e] - m) * rr : 0.f;
+          const float xw = xhat * nw[e];
+          xh[u][e] = xhat;
+          dxh[u][e] = dn * nw[e];
+          s1[u] += dxh[u][e];
+          s2[u] += dxh[u][e] * xhat;
+          a_nw[e] += dn * xhat;
+          a_nb[e] += dn;
+          a_cb[e] += g0;
+          a_cw[3][e] += g0 * xw;
+          a_cw[2][e] += g0 * X[(u + 3) & 3][e];
+          a_cw[1][e] += g0 * X[(u + 2) & 3][e];
+          a_cw[0][e] += g0 * X[(u + 1) & 3][e];
+          X[u][e] = xw;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float a = warp_sum(s1[u]), c = warp_sum(s2[u]);
+      if (lane == 0) {
+        red[half][u][0][warp] = a;
+        red[half][u][1][warp] = c;
+      }
+    }
+    __syncthreads();
+    // tile k fully read by every thread after its last group: refill its stage
+    if (tid == 0 && (rk + 4 >= TR || r4 + 4 >= l1 - l0) && k + 2 < ntiles) {
+      fence_proxy_async_smem();
+      issue(k + 2);
+    }
+    // every warp reduces the warps' partials itself: one shared load per lane, then shuffles
+    float S1v[4], S2v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      S1v[u] = warp_sum(lane < nwarps ? red[half][u][0][lane] : 0.f) * invD;
+      S2v[u] = warp_sum(lane < nwarps ? red[half][u][1][lane] : 0.f) * invD;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = l0 + r4 + u;
+      if (t >= l1 || !act) continue;
+      const float S1 = S1v[u], S2 = S2v[u];
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[e] = rs[u] * (dxh[u][e] - S1 - xh[u][e] * S2);
+      st4<T>(dx + (size_t)t * rowD, o);
+    }
+    half ^= 1;
+  }
+  if (act) {
+    float* part = p.part + (size_t)seg * 7 * rowD + c0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      part[e] = a_nw[e];
+      part[rowD + e] = a_nb[e];
+      part[2 * rowD + e] = a_cb[e];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) part[(3 + k) * rowD + e] = a_cw[k][e];
+    }
+  }
+  // after a timed-out wait: let this CTA's own copies land (bounded) before exit
+  if (!ok && tid == 0) {
+    mbar_wait(&bars[0], ph0, 35);
+    mbar_wait(&bars[1], ph1, 35);
   }
 }
 
@@ -250,14 +431,31 @@ extern "C" int hdc_ln_conv_bwd(int dtype, const void* grad_out, const void* x, c
   if (threads < 64) threads = 64;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   const int rgrid = (int)((7 * D + 255) / 256);
+  const size_t es = dtype == HDC_F32 ? 4 : 2;
+  const size_t row_bytes = (size_t)D * es;
+  const bool staged = row_bytes % 16 == 0;
+  int TR = 8;
+  while (TR > 4 && 4 * (size_t)TR * row_bytes > 160 * 1024) TR -= 4;
+  const size_t smem = 128 + 4 * (size_t)TR * row_bytes + 16;
   if (dtype == HDC_F32) {
-    ln_conv_bwd_kernel<float><<<nseg, threads, 0, s>>>(p);
+    if (staged) {
+      cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      ln_conv_bwd_staged_kernel<float><<<nseg, threads, smem, s>>>(p, TR);
+    } else {
+      ln_conv_bwd_kernel<float><<<nseg, threads, 0, s>>>(p);
+    }
     if (int e = launch_status("ln_conv_bwd_kernel")) return e;
     ln_conv_bwd_reduce_kernel<float><<<rgrid, 256, 0, s>>>(p.part, nseg, (int)D, static_cast<float*>(dnorm_w),
                                                            static_cast<float*>(dnorm_b), static_cast<float*>(dconv_w),
                                                            static_cast<float*>(dconv_b));
   } else {
-    ln_conv_bwd_kernel<__nv_bfloat16><<<nseg, threads, 0, s>>>(p);
+    if (staged) {
+      cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      ln_conv_bwd_staged_kernel<__nv_bfloat16><<<nseg, threads, smem, s>>>(p, TR);
+    } else {
+      ln_conv_bwd_kernel<__nv_bfloat16><<<nseg, threads, 0, s>>>(p);
+    }
     if (int e = launch_status("ln_conv_bwd_kernel")) return e;
     ln_conv_bwd_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, s>>>(
         p.part, nseg, (int)D, static_cast<__nv_bfloat16*>(dnorm_w), static_cast<__nv_bfloat16*>(dnorm_b),

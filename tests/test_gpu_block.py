@@ -129,7 +129,8 @@ def test_train_mode_gradients_match_reference_behaviour():
                                          (torch.float32, 1, 37, 2048), (torch.bfloat16, 3, 129, 96)])
 def test_fused_norm_conv_function_backward(dtype, B, L, D):
     """FusedNormConv1dFunction.backward (hdc_ln_conv_bwd) against the oracle restatement of
-    the reference's backward on the forward's bf16 statistics; dx also against autograd."""
+    the reference's backward on the forward's bf16 statistics; dx also against autograd.
+    (Rows of a multiple of 16 bytes: the shared-memory-staged kernel.)"""
     import oracle as O
     from hdcmamba_b200 import ops
     g = torch.Generator().manual_seed(3 + D)
@@ -156,6 +157,24 @@ def test_fused_norm_conv_function_backward(dtype, B, L, D):
              for k in range(4))
     y.backward(dn)
     assert rel(x.grad, xs.grad) < 2e-2
+
+
+def test_ln_conv_bwd_direct_load_path():
+    """bf16 rows that are not a multiple of 16 bytes (D = 100) take the direct-load backward
+    kernel (the forward needs D % 8 == 0, so the statistics come from the oracle)."""
+    import oracle as O
+    from hdcmamba_b200 import ops
+    g = torch.Generator().manual_seed(17)
+    B, L, D = 2, 45, 100
+    x = torch.randn(B, L, D, generator=g).bfloat16()
+    nw, nb = (1 + 0.1 * torch.randn(D, generator=g)).bfloat16(), (0.1 * torch.randn(D, generator=g)).bfloat16()
+    cw, cb = (0.3 * torch.randn(D, 4, generator=g)).bfloat16(), torch.zeros(D).bfloat16()
+    go = torch.randn(B, L, D, generator=g).bfloat16()
+    _, mean, rstd = O.ln_conv_fwd(x, nw, nb, cw, cb, 1e-5)
+    got = ops.ln_conv_bwd(go.to(DEV), x.to(DEV), mean.to(DEV), rstd.to(DEV), nw.to(DEV), cw.to(DEV))
+    ref = O.ln_conv_bwd(go, x, mean, rstd, nw, cw)
+    for a, r in zip(got, ref):
+        assert rel(a, r) < 2e-2, rel(a, r)
 
 
 @pytest.mark.parametrize("tag", ["f32", "bf16"])
