@@ -693,6 +693,406 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 }
 
 // ---------------------------------------------------------------------------------
+// Pass B for chunk 256, software-pipelined across chunks (slot_tc_pipe_kernel).
+// 512 threads; Q, K and V of two chunks in shared memory (stages alternate), P in TMEM.
+// Per chunk n (stage cur; the next chunk's stage nxt):
+//   wait S(n)                 S_rb = phi(Q_rb) phi(K)^T, issued during chunk n-1
+//   k~ = bf16(phi(k) kdec_j), Qs = bf16(phi(q) qdec_i) in place (the reference rounds the
+//   q-decayed queries before the state product, hdcmamba/model.py:267-268);
+//   P = bf16(mask(S) decay) stored into TMEM over the S columns it came from
+//   issue  Y_rb = Qs_rb bf16(R) + P_rb V,  U = k~^T V
+//   phi of chunk n+1's Q and K (its loads landed during chunk n-1)    || products
+//   wait; next loads into stage cur; y = bf16(Y) and GroupNorm partial sums;
+//   R <- gC R + U -> bf16 R
+//   issue S(n+1); GroupNorm * sigmoid(gate) and stores of chunk n    || S(n+1)
+// TMEM (512 columns): S of row block 0 in [0,128), of row block 1 in [128,384), cut in
+// 32-column pieces; piece c keeps its P (16 packed columns) in its first half when c is
+// even and in its second half when c is odd, so [16,48) and [80,112) hold no P and take
+// the two 32-column halves of U.  Y_rb in [384 + 64 rb, +64).
+// ---------------------------------------------------------------------------------
+namespace pipe {
+constexpr int CT = 256, RB = 128, NWG = 4, NT = NWG * 128, EPW = 16, PW = 32;
+constexpr int NPIECE = 3 * RB / PW;  // 12 pieces of S (4 of row block 0, 8 of row block 1)
+constexpr int CPW = NPIECE / NWG;    // per warpgroup
+constexpr int YCOL = 3 * RB;
+constexpr int UCOL0 = 16, UCOL1 = 80;
+constexpr int TILE = CT * 128;       // one [CT x 64] bf16 tile
+constexpr int STAGE = 3 * TILE;      // K, V, Q
+constexpr int TABN = CT + 4;
+constexpr size_t SMEM = 1024 + 2 * STAGE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + CT * NWG * 8 + 8 * 8;
+__device__ __forceinline__ uint32_t pcol(int c) { return (uint32_t)(c * PW + ((c & 1) ? 16 : 0)); }
+}  // namespace pipe
+
+template <bool PERSTEP, bool GATE>
+__global__ void __launch_bounds__(pipe::NT, 1)
+    slot_tc_pipe_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                        const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
+  using namespace pipe;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  uint8_t* sR = base + 2 * STAGE;                          // [64 rows][128 B], MN-major bf16 R
+  float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [2][TABN] (per-step: one per stage)
+  float* sGn = sTab + 2 * TABN;                            // [128] gn weight | bias of this head
+  float2* sRed = reinterpret_cast<float2*>(sGn + 128);     // [CT][NWG] GroupNorm (sum, sum of squares)
+  // mbarriers: [0], [1] loads of stage 0 / 1, [2] S products, [3] Y and U products.  Every
+  // commit and every load issue follows a CTA barrier that all waits of the previous phase
+  // precede, so no thread falls two phases behind on a barrier.
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * NWG);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, wg = warp >> 2;
+  const int bh = blockIdx.x / p.nseg, seg = blockIdx.x - bh * p.nseg;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
+  const int my_row = quarter * 32 + lane;  // accumulator row within a row block
+  const int row_lo = quarter * 32, row_hi = row_lo + 31;
+  const bool f_valid = lane < 16;          // holds row f_row of the M=64 products (U)
+  const int f_row = quarter * 16 + lane;
+  const int e0 = wg * EPW;                 // this thread's accumulator columns [e0, e0 + 16)
+
+  auto tile = [&](int st, int which) { return base + st * STAGE + which * TILE; };  // 0 K, 1 V, 2 Q
+  auto tab = [&](int st) { return sTab + (PERSTEP ? st * TABN : 0); };
+
+  if (warp == 0) {
+    tmem_alloc(sTmem, 512);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+    tma_prefetch_map(&mapQ);
+    tma_prefetch_map(&mapK);
+    tma_prefetch_map(&mapV);
+  }
+  if (!PERSTEP) {
+    const float lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
+    for (int k = tid; k <= CT; k += NT) sTab[k] = expf((float)k * lg);
+  }
+  if (GATE) {
+    for (int d = tid; d < 64; d += NT) {
+      const bool in = d < p.hd;
+      sGn[d] = in ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_w)[h * p.hd + d]) : 0.f;
+      sGn[64 + d] = in ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_b)[h * p.hd + d]) : 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *sTmem;
+  const uint32_t tL = tmem + ((uint32_t)(quarter * 32) << 16);  // this warp's TMEM lanes
+
+  int pending = 0;  // thread 0: bit s set while stage s has loads in flight
+  auto issue = [&](int n, int st) {
+    mbar_expect_tx(&bars[st], 3 * TILE);
+    tma_load_3d(tile(st, 0), &mapK, h * p.hd, n * CT, b, &bars[st]);
+    tma_load_3d(tile(st, 1), &mapV, h * p.hd, n * CT, b, &bars[st]);
+    tma_load_3d(tile(st, 2), &mapQ, h * p.hd, n * CT, b, &bars[st]);
+    pending |= 1 << st;
+  };
+  if (tid == 0) {
+    if (n0 < n1) issue(n0, 0);
+    if (n0 + 1 < n1) issue(n0 + 1, 1);
+  }
+
+  // entering state: state_in, then earlier sequence parts, then the earlier segments'
+  // local states (lanes < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR
+  float Rr[EPW];
+#pragma unroll
+  for (int e = 0; e < EPW; ++e) Rr[e] = 0.f;
+  if (f_valid) {
+    if (p.state_in) {
+      const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + e0;
+#pragma unroll
+      for (int e = 0; e < EPW; ++e) Rr[e] = src[e];
+    }
+#pragma unroll 4
+    for (int s = 0; s < p.nprev; ++s) {
+      const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
+      const float4* src =
+          reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride + (size_t)bh * 4096 + f_row * 64 + e0);
+#pragma unroll
+      for (int e = 0; e < EPW / 4; ++e) {
+        const float4 v = src[e];
+        Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+        Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+        Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+        Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+      }
+    }
+#pragma unroll 4
+    for (int s = 0; s < seg; ++s) {
+      const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+      const float4* src = reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
+#pragma unroll
+      for (int e = 0; e < EPW / 4; ++e) {
+        const float4 v = src[e];
+        Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+        Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+        Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+        Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < EPW / 8; ++c)
+      *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
+  }
+
+  constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
+  constexpr uint32_t idU = idesc_bf16_f32(64, 32, true, true);
+  uint32_t lph0 = 0, lph1 = 0, sph = 0, yph = 0;
+  bool ok = true;
+
+  // phi of a stage's Q and K in place (padding: ones), per-step decay table by warp 0
+  auto prep = [&](int n, int st) {
+    if (!mbar_wait_warp(&bars[st], st ? lph1 : lph0, 41)) return false;
+    if (st) lph1 ^= 1; else lph0 ^= 1;
+    if (tid == 0) pending &= ~(1 << st);
+    if (PERSTEP && warp == 0)
+      chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, tab(st));
+    prep_tile_u<NT, CT, true>(tile(st, 0), p.hd, 1.f);
+    prep_tile_u<NT, CT, true>(tile(st, 2), p.hd, 1.f);
+    if (p.hd < 64) prep_tile_u<NT, CT, false>(tile(st, 1), p.hd, 0.f);
+    fence_proxy_async_smem();
+    return true;
+  };
+  auto issue_s = [&](int st) {  // S_rb = phi(Q_rb) phi(K[0 : 128 (rb + 1)])^T
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      const uint32_t aq = smem_u32(tile(st, 2)) + rb * RB * 128;
+      const uint32_t idS = idesc_bf16_f32(RB, RB * (rb + 1), false, false);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        umma_bf16(tmem + rb * RB, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(tile(st, 0)) + k * 32, 16, 1024),
+                  idS, k > 0 ? 1u : 0u);
+    }
+    umma_commit(&bars[2]);
+  };
+
+  if (n0 < n1) {
+    ok = prep(n0, 0);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (ok && tid == 0) issue_s(0);
+  }
+
+  for (int n = n0; n < n1 && ok; ++n) {
+    const int cur = (n - n0) & 1, nxt = cur ^ 1;
+    uint8_t* sK = tile(cur, 0);
+    uint8_t* sV = tile(cur, 1);
+    uint8_t* sQ = tile(cur, 2);
+    const float* T = tab(cur);
+    // this thread's gate values of chunk n (consumed at the end of the iteration)
+    uint4 graw[2][EPW / 8];
+    if (GATE) {
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        const int t_row = n * CT + rb * RB + my_row;
+        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) + (size_t)b * p.g_sb +
+                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + e0;
+#pragma unroll
+        for (int c = 0; c < EPW / 8; ++c) graw[rb][c] = ldg16_pred(gp + c * 8, e0 + c * 8 < p.hd);
+      }
+    }
+    if (!mbar_wait_warp(&bars[2], sph, 42)) { ok = false; break; }
+    sph ^= 1;
+    tc_fence_after();
+    // k~ = bf16(phi(k) kdec_j) and Qs = bf16(phi(q) qdec_i) in place
+    {
+      constexpr int IT = CT * 8 / NT;
+      uint4 kv[IT], qv[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        kv[it] = reinterpret_cast<const uint4*>(sK)[tid + it * NT];
+        qv[it] = reinterpret_cast<const uint4*>(sQ)[tid + it * NT];
+      }
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = tid + it * NT, row = idx >> 3;
+        const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
+        const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
+        float f[8];
+        unpack16<__nv_bfloat16>(kv[it], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= kd;
+        reinterpret_cast<uint4*>(sK)[idx] = pack16<__nv_bfloat16>(f);
+        unpack16<__nv_bfloat16>(qv[it], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] *= qd;
+        reinterpret_cast<uint4*>(sQ)[idx] = pack16<__nv_bfloat16>(f);
+      }
+    }
+    // P = bf16(mask(S) decay) of this warpgroup's pieces -> TMEM (packed pairs)
+#pragma unroll
+    for (int cc = 0; cc < CPW; ++cc) {
+      const int c = wg * CPW + cc;
+      const int rb = c * PW >= RB ? 1 : 0;
+      const int j0 = c * PW - rb * RB;  // chunk position of the piece's first column
+      const int ib = rb * RB;           // chunk position of the block's first row
+      uint32_t pk[PW / 2];
+      if (j0 > ib + row_hi) {           // above the diagonal for every row of this warp
+#pragma unroll
+        for (int q = 0; q < PW / 2; ++q) pk[q] = 0u;
+      } else {
+        float sv[PW];
+        tmem_ld32(tL + c * PW, sv);
+        const int i = ib + my_row;
+        const bool full = j0 + PW - 1 <= ib + row_lo;  // no masking for any row of this warp
+        const float ci = PERSTEP ? T[i] : 0.f;
+#pragma unroll
+        for (int q = 0; q < PW / 8; ++q) {
+          float v[8];
+          if (!PERSTEP && full) {
+            // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e
+            const float rf = T[i - j0 - q * 8 - 7];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = sv[q * 8 + e] * (rf * T[7 - e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int j = j0 + q * 8 + e;
+              float dm = 0.f;
+              if (j <= i) dm = PERSTEP ? fast_exp(ci - T[j]) : T[i - j];
+              v[e] = (j <= i) ? sv[q * 8 + e] * dm : 0.f;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 t2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+            pk[q * 4 + e] = *reinterpret_cast<uint32_t*>(&t2);
+          }
+        }
+      }
+      tmem_st16_async(tL + pcol(c), pk);
+    }
+    tmem_wait_st();
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // Y_rb = Qs_rb bf16(R) + P_rb V;  U = k~^T V in two 32-column halves
+    if (tid == 0) {
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        const uint32_t dY = tmem + YCOL + 64 * rb;
+        const uint32_t aq = smem_u32(sQ) + rb * RB * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_bf16(dY, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV,
+                    k > 0 ? 1u : 0u);
+        for (int kk = 0; kk < (rb + 1) * RB / 16; ++kk) {
+          const int c = rb * (RB / PW) + (kk >> 1);
+          umma_bf16_ts(dY, tmem + pcol(c) + (kk & 1) * 8, sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, 1u);
+        }
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half)
+        for (int kk = 0; kk < CT / 16; ++kk)
+          umma_bf16(tmem + (half ? UCOL1 : UCOL0), sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
+                    sdesc_sw128(smem_u32(sV) + kk * 2048 + half * 64, 0, 1024), idU, kk > 0 ? 1u : 0u);
+      umma_commit(&bars[3]);
+    }
+    // meanwhile: the next chunk's phi
+    if (n + 1 < n1 && !prep(n + 1, nxt)) { ok = false; break; }
+    if (!mbar_wait_warp(&bars[3], yph, 43)) { ok = false; break; }
+    yph ^= 1;
+    tc_fence_after();
+    if (tid == 0 && n + 2 < n1) issue(n + 2, cur);  // every product reading stage cur is done
+    // y = bf16(Y) (y_slot is bf16); GroupNorm partial sums
+    float o[2][EPW];
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      float yv[EPW];
+      tmem_ld16(tL + YCOL + 64 * rb + e0, yv);
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPW; ++e) {
+        o[rb][e] = bf16_round(yv[e]);
+        if (e0 + e < p.hd) {
+          s1 += o[rb][e];
+          s2 += o[rb][e] * o[rb][e];
+        }
+      }
+      if (GATE) sRed[(rb * RB + my_row) * NWG + wg] = make_float2(s1, s2);
+    }
+    // R <- gC R + U (fp32) -> sR (bf16) for the next chunk
+    {
+      const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
+      float u[EPW];
+      tmem_ld16(tL + (e0 < 32 ? UCOL0 + e0 : UCOL1 + e0 - 32), u);
+#pragma unroll
+      for (int e = 0; e < EPW; ++e) Rr[e] = fmaf(Rr[e], gC, u[e]);
+      if (f_valid) {
+#pragma unroll
+        for (int c = 0; c < EPW / 8; ++c)
+          *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0 && n + 1 < n1) issue_s(nxt);
+    // outputs of chunk n (GroupNorm * sigmoid(gate), or plain y) while S(n+1) runs
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      const int t_row = n * CT + rb * RB + my_row;
+      __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
+                          (size_t)t_row * p.y_st + e0;
+      if (GATE) {
+        float S1 = 0.f, S2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          const float2 v = sRed[(rb * RB + my_row) * NWG + w];
+          S1 += v.x;
+          S2 += v.y;
+        }
+        const float mean = S1 / (float)p.hd;
+        // sum over the hd lanes of (y - mean)^2 plus the reference's padded lanes (block
+        // width 64), which add (64 - hd) mean^2
+        const float var = fmaxf(S2 - S1 * mean, 0.f) / (float)p.hd + (float)(64 - p.hd) * mean * mean / (float)p.hd;
+        const float inv = rsqrtf(var + 1e-5f);
+#pragma unroll
+        for (int c = 0; c < EPW / 8; ++c) {
+          if (e0 + c * 8 >= p.hd) continue;
+          float g[8], r[8];
+          unpack16<__nv_bfloat16>(graw[rb][c], g);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int d = e0 + c * 8 + e;
+            const float ygn = ((o[rb][c * 8 + e] - mean) * inv) * sGn[d] + sGn[64 + d];
+            r[e] = ygn * fast_sigmoid(g[e]);
+          }
+          stg16(op + c * 8, pack16<__nv_bfloat16>(r));
+        }
+      } else if (p.y_vec) {
+#pragma unroll
+        for (int c = 0; c < EPW / 8; ++c)
+          if (e0 + c * 8 < p.hd) stg16(op + c * 8, pack16<__nv_bfloat16>(&o[rb][c * 8]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPW; ++e)
+          if (e0 + e < p.hd) op[e] = __float2bfloat16_rn(o[rb][e]);
+      }
+    }
+  }
+  // after a timed-out wait: let this CTA's own loads in flight land (bounded) before exit
+  if (!ok && tid == 0) {
+    if (pending & 1) mbar_wait(&bars[0], lph0, 44);
+    if (pending & 2) mbar_wait(&bars[1], lph1, 44);
+  }
+  if (ok && seg == p.nseg - 1 && p.state_out && f_valid) {
+    float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0;
+#pragma unroll
+    for (int e = 0; e < EPW; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(Rr[e], Rr[e + 1], Rr[e + 2], Rr[e + 3]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -792,6 +1192,12 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
     cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), kStateThreads, sm, s>>>(mk, mv, p);
     if (int e = launch_status("slot_tc_state_kernel")) return e;
+  }
+  if constexpr (CT == 256) {
+    const size_t sm = pipe::SMEM;
+    cudaFuncSetAttribute(slot_tc_pipe_kernel<PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    slot_tc_pipe_kernel<PS, GATE><<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq, mk, mv, p);
+    return launch_status("slot_tc_pipe_kernel");
   }
   const size_t sm = smem_out_bytes<CT>();
   cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
