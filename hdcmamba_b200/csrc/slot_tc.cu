@@ -5,24 +5,23 @@
 //
 //   * Work unit: one CTA per (batch*head, segment of consecutive chunks).  Pass A
 //     (slot_tc_state_kernel) computes every segment's local state (from zero) and decay
-//     product; pass B (slot_tc_out_kernel) folds the states of the earlier segments into
-//     its entering state, then walks its chunks producing outputs.
-//   * Per chunk, TMA loads K and V (C x 64 bf16, 128-byte swizzle) and Q per 128-row
-//     block into shared memory; phi and the reference's feature padding (ones for q/k,
-//     zeros for v beyond head_dim) are applied in place.
-//   * Tensor-core products (one thread issues tcgen05.mma; fp32 accumulators in TMEM,
-//     256 columns per CTA):
-//       S   = phi(Q_blk) phi(K_cb)^T         M=rows, N=64, K=64    TMEM cols [0,64)
-//       Yi += P_cb V_cb                      M=rows, N=64, K=64    TMEM cols [64,128)
-//       Yx  = phi(Q_blk) bf16(R)             M=rows, N=64, K=64    TMEM cols [128,192)
-//       R  += bf16(phi(K) kdec)^T V          M=64,   N=64, K=C     TMEM cols [192,256)
-//     P_cb = bf16(mask(S) * decay) is written back to shared memory by the threads; the
-//     fp32 state R stays in TMEM (scaled by the chunk decay in place before the update).
-//   * Pass B runs two warpgroups: both cover all TMEM lanes (rows) and split the columns
-//     of each S block and of the epilogue (warpgroup w takes columns [32w, 32w+32)).
-//   * Epilogue: y = bf16(Yi + qdec_i * Yx), stored; or, with the fused gate epilogue,
+//     product; pass B folds the states of the earlier segments into its entering state,
+//     then walks its chunks producing outputs.
+//   * Per chunk, TMA loads K, V and Q (C x 64 bf16, 128-byte swizzle) into shared memory;
+//     phi and the reference's feature padding (ones for q/k, zeros for v beyond head_dim)
+//     are applied in place.
+//   * Tensor-core products (one thread issues tcgen05.mma; fp32 accumulators in TMEM):
+//       S  = phi(Q_blk) phi(K)^T               per row block (causal columns only)
+//       Y  = Qs_blk bf16(R) + P_blk V          Qs = bf16(phi(q) qdec_i), as the reference
+//                                              rounds it (model.py:267-268)
+//       U  = k~^T V                            k~ = bf16(phi(k) kdec_j); R <- gC R + U (fp32)
+//     P = bf16(mask(S) * decay) is formed by the threads from S.
+//   * Epilogue: y = bf16(Y), stored; or, with the fused gate epilogue,
 //     combined = bf16(GroupNorm_head(y) * sigmoid(gate)) (hdcmamba/model.py:286-293)
 //     written straight into the concatenated row.
+//   * Two pass-B kernels: slot_tc_out_kernel (any chunk 64 / 128 / 256, P through shared
+//     memory, all threads in lock step) and slot_tc_pipe_kernel (chunk 256 with the fused
+//     gate and head_dim 64: warp-specialized, pipelined across chunks, P in TMEM).
 // Decays: a table pw[k] = exp(k * log(gamma)) (constant gamma: the same expression the
 // reference evaluates per element) or the chunk's cumulative log decay c_i (per-step).
 #include "slot.cuh"
@@ -58,7 +57,9 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-__device__ __forceinline__ float phi_fast(float z) { return z > 0.f ? z + 1.f : fast_exp(z); }
+// phi(z) = elu(z) + 1 = (z > 0 ? z + 1 : exp(z)), branch-free: max(z, 0) + exp(min(z, 0))
+// (exp(0) = 1 exactly, and adding +0 to exp(z) is exact)
+__device__ __forceinline__ float phi_fast(float z) { return fmaxf(z, 0.f) + fast_exp(fminf(z, 0.f)); }
 
 // phi in place on a [rows x 64] swizzled bf16 tile; columns >= hd become `pad`.
 template <int NT>
@@ -267,8 +268,9 @@ __global__ void __launch_bounds__(kStateThreads, CT == 256 ? 1 : 2)
 // (row) and split the columns.  Both row blocks of a chunk go through the tensor cores
 // together, so a chunk takes two round trips:
 //   1. S_rb = phi(Q_rb) phi(K[0:ncol_rb])^T for every row block rb (causal columns only);
-//   2. Yi_rb = P_rb V, Yx_rb = phi(Q_rb) bf16(R) and the state update R += k~^T V.
-// With 128-row blocks Yi / Yx reuse the S columns of their block once P is read out.
+//   2. Y_rb = Qs_rb bf16(R) + P_rb V and the state update U = k~^T V (k~ and Qs are
+//      formed in place between the two rounds).
+// With 128-row blocks Y reuses the S columns of its block once P is read out.
 // The fp32 state R stays in registers (R <- gC R + U after round 2); while round 1 runs
 // the threads fetch the gate; the next chunk's loads start as soon as round 2 completes.
 // ---------------------------------------------------------------------------------
@@ -287,9 +289,8 @@ struct OutCfg {
   static constexpr int ncol(int rb) { return (rb + 1) * RB; }      // S columns of block rb
   static constexpr int scol(int rb) { return rb == 0 ? 0 : ncol(0); }
   static constexpr int SCOLS = NRB == 1 ? ncol(0) : ncol(0) + ncol(1);
-  static constexpr int yi(int rb) { return INPLACE ? scol(rb) : SCOLS; }
-  static constexpr int yx(int rb) { return INPLACE ? scol(rb) + 64 : SCOLS + 64; }
-  static constexpr int RCOL = INPLACE ? SCOLS : SCOLS + 128;      // U = k~^T V (64 columns)
+  static constexpr int yi(int rb) { return INPLACE ? scol(rb) : SCOLS; }  // Y (64 columns)
+  static constexpr int RCOL = INPLACE ? SCOLS : SCOLS + 64;       // U = k~^T V (64 columns)
   static constexpr int TMEM_COLS = RCOL + 64 <= 256 ? 256 : 512;
   static constexpr int pbase(int rb) { return rb == 0 ? 0 : RB * ncol(0) * 2; }  // bytes into sP
   static constexpr int PBYTES = NRB == 1 ? RB * ncol(0) * 2 : RB * (ncol(0) + ncol(1)) * 2;
@@ -479,15 +480,22 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     if (!mbar_wait_warp(&bars[1], sph, 23)) { ok = false; break; }
     sph ^= 1;
     tc_fence_after();
-    // k~ = bf16(phi(k) * kdec_j) in place (the S products no longer read sK)
+    // k~ = bf16(phi(k) * kdec_j) and Qs = bf16(phi(q) * qdec_i) in place (the S products no
+    // longer read sK / sQ; the reference rounds the q-decayed queries before the state
+    // product, hdcmamba/model.py:267-268)
     for (int idx = tid; idx < CT * 8; idx += NT) {
       const int row = idx >> 3;
       const float kd = PERSTEP ? fast_exp(sTab[CT - 1] - sTab[row]) : sTab[CT - 1 - row];
+      const float qd = PERSTEP ? fast_exp(sTab[row]) : sTab[row];
       float f[8];
       unpack16<__nv_bfloat16>(reinterpret_cast<const uint4*>(sK)[idx], f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] *= kd;
       reinterpret_cast<uint4*>(sK)[idx] = pack16<__nv_bfloat16>(f);
+      unpack16<__nv_bfloat16>(reinterpret_cast<const uint4*>(sQ)[idx], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= qd;
+      reinterpret_cast<uint4*>(sQ)[idx] = pack16<__nv_bfloat16>(f);
     }
     // P = bf16(mask(S) * decay): this warpgroup's 32-column pieces of S -> sP
 #pragma unroll
@@ -538,19 +546,19 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // ---- round 2: Yi = P V, Yx = phi(Q) bf16(R) per row block; U = k~^T V
+    // ---- round 2: Y = Qs bf16(R) + P V per row block; U = k~^T V
     if (tid == 0) {
 #pragma unroll
       for (int rb = 0; rb < NRB; ++rb) {
-        const uint32_t ap = smem_u32(sP + Cfg::pbase(rb));
-        for (int kk = 0; kk < Cfg::ncol(rb) / 16; ++kk)
-          umma_bf16(tmem + Cfg::yi(rb), sdesc_sw128(ap + ((kk * 16) >> 6) * (RB * 128) + ((kk * 16) & 63) * 2, 16, 1024),
-                    sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, kk > 0 ? 1u : 0u);
         const uint32_t aq = smem_u32(sQ) + rb * RB * 128;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_bf16(tmem + Cfg::yx(rb), sdesc_sw128(aq + k * 32, 16, 1024),
+          umma_bf16(tmem + Cfg::yi(rb), sdesc_sw128(aq + k * 32, 16, 1024),
                     sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV, k > 0 ? 1u : 0u);
+        const uint32_t ap = smem_u32(sP + Cfg::pbase(rb));
+        for (int kk = 0; kk < Cfg::ncol(rb) / 16; ++kk)
+          umma_bf16(tmem + Cfg::yi(rb), sdesc_sw128(ap + ((kk * 16) >> 6) * (RB * 128) + ((kk * 16) & 63) * 2, 16, 1024),
+                    sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, 1u);
       }
 #pragma unroll
       for (int kk = 0; kk < CT / 16; ++kk)  // U = k~^T V
@@ -562,18 +570,16 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     pph ^= 1;
     tc_fence_after();
     if (tid == 0 && n + 1 < n1) issue(n + 1);  // every buffer of this chunk is free
-    // ---- epilogue: y = bf16(Yi + qdec_i * Yx), plain or GroupNorm * sigmoid(gate)
+    // ---- epilogue: y = bf16(Y), plain or GroupNorm * sigmoid(gate)
     float o[NRB][EPW];
 #pragma unroll
     for (int rb = 0; rb < NRB; ++rb) {
-      const int i_row = rb * RB + (my_row >= 0 ? my_row : 0);
-      const float qd = PERSTEP ? fast_exp(sTab[i_row]) : sTab[i_row];
 #pragma unroll
       for (int pc = 0; pc < EPW / AG; ++pc) {
-        float yi[AG], yx[AG];
-        tmem_ldn2<AG>(tL + Cfg::yi(rb) + e0 + pc * AG, tL + Cfg::yx(rb) + e0 + pc * AG, yi, yx);
+        float yi[AG];
+        tmem_ldn<AG>(tL + Cfg::yi(rb) + e0 + pc * AG, yi);
 #pragma unroll
-        for (int e = 0; e < AG; ++e) o[rb][pc * AG + e] = bf16_round(yi[e] + qd * yx[e]);  // y_slot is bf16
+        for (int e = 0; e < AG; ++e) o[rb][pc * AG + e] = bf16_round(yi[e]);  // y_slot is bf16
       }
     }
     if (GATE) {
@@ -693,55 +699,69 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 }
 
 // ---------------------------------------------------------------------------------
-// Pass B for chunk 256, software-pipelined across chunks (slot_tc_pipe_kernel).
-// 512 threads; Q, K and V of two chunks in shared memory (stages alternate), P in TMEM.
-// Per chunk n (stage cur; the next chunk's stage nxt):
-//   wait S(n)                 S_rb = phi(Q_rb) phi(K)^T, issued during chunk n-1
+// Pass B for chunk 256, warp-specialized and software-pipelined across chunks
+// (slot_tc_pipe_kernel).  16 compute warps (512 threads) and one issue warp (warp 16,
+// one thread): TMA loads and stores, tcgen05.mma, commits.  Shared memory: phi(K) / phi(Q)
+// of two chunks (stages alternate), V of one chunk, the gate tile of one chunk (the gated
+// outputs are written over it and leave by one TMA store), R as bf16.  P lives in TMEM.
+// Per chunk n (stage cur, next chunk's stage nxt), compute warps:
+//   wait S(n)                 S_rb = phi(Q_rb) phi(K)^T
 //   k~ = bf16(phi(k) kdec_j), Qs = bf16(phi(q) qdec_i) in place (the reference rounds the
 //   q-decayed queries before the state product, hdcmamba/model.py:267-268);
-//   P = bf16(mask(S) decay) stored into TMEM over the S columns it came from
-//   issue  Y_rb = Qs_rb bf16(R) + P_rb V,  U = k~^T V
-//   phi of chunk n+1's Q and K (its loads landed during chunk n-1)    || products
-//   wait; next loads into stage cur; y = bf16(Y) and GroupNorm partial sums;
-//   R <- gC R + U -> bf16 R
-//   issue S(n+1); GroupNorm * sigmoid(gate) and stores of chunk n    || S(n+1)
+//   P = bf16(mask(S) decay) into TMEM over the S columns it came from     -> arrive P
+//   phi of chunk n+1's Q and K                      || issue warp: Y_rb = Qs_rb bf16(R) + P_rb V,
+//                                                                  U = k~^T V
+//   wait Y; y = bf16(Y), GroupNorm partial sums; R <- gC R + U -> bf16 R  -> arrive ready
+//   GroupNorm * sigmoid(gate) over the gate tile                        -> arrive out
+//                                                   || issue warp: S(n+1), TMA store of
+//                                                      chunk n's outputs, gate of n+1
 // TMEM (512 columns): S of row block 0 in [0,128), of row block 1 in [128,384), cut in
 // 32-column pieces; piece c keeps its P (16 packed columns) in its first half when c is
 // even and in its second half when c is odd, so [16,48) and [80,112) hold no P and take
 // the two 32-column halves of U.  Y_rb in [384 + 64 rb, +64).
+// Every wait is bounded; compute warps synchronise with each other through an mbarrier
+// (bounded wait), never through bar.sync inside the loop.
 // ---------------------------------------------------------------------------------
 namespace pipe {
-constexpr int CT = 256, RB = 128, NWG = 4, NT = NWG * 128, EPW = 16, PW = 32;
+constexpr int CT = 256, RB = 128, NWG = 4, NCW = NWG * 4, NTC = NCW * 32, NT = NTC + 32, EPW = 16, PW = 32;
 constexpr int NPIECE = 3 * RB / PW;  // 12 pieces of S (4 of row block 0, 8 of row block 1)
 constexpr int CPW = NPIECE / NWG;    // per warpgroup
 constexpr int YCOL = 3 * RB;
 constexpr int UCOL0 = 16, UCOL1 = 80;
 constexpr int TILE = CT * 128;       // one [CT x 64] bf16 tile
-constexpr int STAGE = 3 * TILE;      // K, V, Q
 constexpr int TABN = CT + 4;
-constexpr size_t SMEM = 1024 + 2 * STAGE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + CT * NWG * 8 + 8 * 8;
+// mbarriers
+enum { B_L0, B_L1, B_V, B_G, B_S, B_Y, B_READY, B_P, B_OUT, B_SYNC, NBAR };
+constexpr size_t SMEM = 1024 + 6 * TILE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + CT * NWG * 8 + NBAR * 8 + 16;
 __device__ __forceinline__ uint32_t pcol(int c) { return (uint32_t)(c * PW + ((c & 1) ? 16 : 0)); }
 }  // namespace pipe
 
-template <bool PERSTEP, bool GATE>
+// gate / output tensor maps travel with the parameters
+struct SlotPipeMaps {
+  CUtensorMap gate, out;
+};
+
+template <bool PERSTEP>
 __global__ void __launch_bounds__(pipe::NT, 1)
     slot_tc_pipe_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
-                        const __grid_constant__ CUtensorMap mapV, SlotTcParams p) {
+                        const __grid_constant__ CUtensorMap mapV, const __grid_constant__ SlotPipeMaps mg,
+                        SlotTcParams p) {
   using namespace pipe;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
-  uint8_t* sR = base + 2 * STAGE;                          // [64 rows][128 B], MN-major bf16 R
+  // [0,4): K0 Q0 K1 Q1, [4] V, [5] gate / outputs
+  uint8_t* sV = base + 4 * TILE;
+  uint8_t* sG = base + 5 * TILE;
+  uint8_t* sR = base + 6 * TILE;                           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [2][TABN] (per-step: one per stage)
   float* sGn = sTab + 2 * TABN;                            // [128] gn weight | bias of this head
   float2* sRed = reinterpret_cast<float2*>(sGn + 128);     // [CT][NWG] GroupNorm (sum, sum of squares)
-  // mbarriers: [0], [1] loads of stage 0 / 1, [2] S products, [3] Y and U products.  Every
-  // commit and every load issue follows a CTA barrier that all waits of the previous phase
-  // precede, so no thread falls two phases behind on a barrier.
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * NWG);
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + NBAR);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, wg = warp >> 2;
+  const bool issuer = warp == NCW;
   const int bh = blockIdx.x / p.nseg, seg = blockIdx.x - bh * p.nseg;
   const int b = bh / p.H, h = bh - b * p.H;
   const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
@@ -751,7 +771,8 @@ __global__ void __launch_bounds__(pipe::NT, 1)
   const int f_row = quarter * 16 + lane;
   const int e0 = wg * EPW;                 // this thread's accumulator columns [e0, e0 + 16)
 
-  auto tile = [&](int st, int which) { return base + st * STAGE + which * TILE; };  // 0 K, 1 V, 2 Q
+  auto sK = [&](int st) { return base + (2 * st) * TILE; };
+  auto sQ = [&](int st) { return base + (2 * st + 1) * TILE; };
   auto tab = [&](int st) { return sTab + (PERSTEP ? st * TABN : 0); };
 
   if (warp == 0) {
@@ -759,333 +780,350 @@ __global__ void __launch_bounds__(pipe::NT, 1)
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < NBAR; ++i)
+      mbar_init(&bars[i], (i == B_READY || i == B_P || i == B_OUT || i == B_SYNC) ? NCW : 1);
     fence_mbar_init();
-    tma_prefetch_map(&mapQ);
-    tma_prefetch_map(&mapK);
-    tma_prefetch_map(&mapV);
   }
   if (!PERSTEP) {
     const float lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
     for (int k = tid; k <= CT; k += NT) sTab[k] = expf((float)k * lg);
   }
-  if (GATE) {
-    for (int d = tid; d < 64; d += NT) {
-      const bool in = d < p.hd;
-      sGn[d] = in ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_w)[h * p.hd + d]) : 0.f;
-      sGn[64 + d] = in ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_b)[h * p.hd + d]) : 0.f;
-    }
+  for (int d = tid; d < 64; d += NT) {
+    sGn[d] = __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_w)[h * 64 + d]);
+    sGn[64 + d] = __bfloat162float(static_cast<const __nv_bfloat16*>(p.gn_b)[h * 64 + d]);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sTmem;
-  const uint32_t tL = tmem + ((uint32_t)(quarter * 32) << 16);  // this warp's TMEM lanes
 
-  int pending = 0;  // thread 0: bit s set while stage s has loads in flight
-  auto issue = [&](int n, int st) {
-    mbar_expect_tx(&bars[st], 3 * TILE);
-    tma_load_3d(tile(st, 0), &mapK, h * p.hd, n * CT, b, &bars[st]);
-    tma_load_3d(tile(st, 1), &mapV, h * p.hd, n * CT, b, &bars[st]);
-    tma_load_3d(tile(st, 2), &mapQ, h * p.hd, n * CT, b, &bars[st]);
-    pending |= 1 << st;
-  };
-  if (tid == 0) {
-    if (n0 < n1) issue(n0, 0);
-    if (n0 + 1 < n1) issue(n0 + 1, 1);
-  }
-
-  // entering state: state_in, then earlier sequence parts, then the earlier segments'
-  // local states (lanes < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR
-  float Rr[EPW];
+  if (issuer) {
+    // ------------------------------------------------------------ issue warp
+    if (lane == 0 && n0 < n1) {
+      tma_prefetch_map(&mapQ);
+      tma_prefetch_map(&mapK);
+      tma_prefetch_map(&mapV);
+      auto load_kq = [&](int n, int st) {
+        mbar_expect_tx(&bars[B_L0 + st], 2 * TILE);
+        tma_load_3d(sK(st), &mapK, h * p.hd, n * CT, b, &bars[B_L0 + st]);
+        tma_load_3d(sQ(st), &mapQ, h * p.hd, n * CT, b, &bars[B_L0 + st]);
+      };
+      auto load_v = [&](int n) {
+        mbar_expect_tx(&bars[B_V], TILE);
+        tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[B_V]);
+      };
+      auto load_g = [&](int n) {
+        mbar_expect_tx(&bars[B_G], TILE);
+        tma_load_3d(sG, &mg.gate, h * p.hd, n * CT, b, &bars[B_G]);
+      };
+      load_kq(n0, 0);
+      load_v(n0);
+      load_g(n0);
+      if (n0 + 1 < n1) load_kq(n0 + 1, 1);
+      constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
+      constexpr uint32_t idU = idesc_bf16_f32(64, 32, true, true);
+      uint32_t rph = 0, pph = 0, yph = 0, oph = 0;
+      for (int n = n0; n < n1; ++n) {
+        const int cur = (n - n0) & 1;
+        // S_rb = phi(Q_rb) phi(K[0 : 128 (rb + 1)])^T once phi(n) is in place and U(n-1) was read
+        if (!mbar_wait(&bars[B_READY], rph, 51)) break;
+        rph ^= 1;
+        tc_fence_after();
 #pragma unroll
-  for (int e = 0; e < EPW; ++e) Rr[e] = 0.f;
-  if (f_valid) {
-    if (p.state_in) {
-      const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + e0;
+        for (int rb = 0; rb < 2; ++rb) {
+          const uint32_t aq = smem_u32(sQ(cur)) + rb * RB * 128;
+          const uint32_t idS = idesc_bf16_f32(RB, RB * (rb + 1), false, false);
 #pragma unroll
-      for (int e = 0; e < EPW; ++e) Rr[e] = src[e];
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(tmem + rb * RB, sdesc_sw128(aq + k * 32, 16, 1024),
+                      sdesc_sw128(smem_u32(sK(cur)) + k * 32, 16, 1024), idS, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[B_S]);
+        // outputs of chunk n-1 out, gate of chunk n in
+        if (n > n0) {
+          if (!mbar_wait(&bars[B_OUT], oph, 52)) break;
+          oph ^= 1;
+          tma_store_3d(&mg.out, sG, h * p.hd, (n - 1) * CT, b);
+          bulk_commit();
+          bulk_wait_read0();
+          load_g(n);
+        }
+        // Y_rb = Qs_rb bf16(R) + P_rb V;  U = k~^T V in two 32-column halves
+        if (!mbar_wait(&bars[B_P], pph, 53)) break;
+        pph ^= 1;
+        if (!mbar_wait(&bars[B_V], (uint32_t)((n - n0) & 1), 54)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int rb = 0; rb < 2; ++rb) {
+          const uint32_t dY = tmem + YCOL + 64 * rb;
+          const uint32_t aq = smem_u32(sQ(cur)) + rb * RB * 128;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(dY, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV,
+                      k > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < (rb + 1) * RB / 16; ++kk) {
+            const int c = rb * (RB / PW) + (kk >> 1);
+            umma_bf16_ts(dY, tmem + pcol(c) + (kk & 1) * 8, sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024),
+                         idPV, 1u);
+          }
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int kk = 0; kk < CT / 16; ++kk)
+            umma_bf16(tmem + (half ? UCOL1 : UCOL0), sdesc_sw128(smem_u32(sK(cur)) + kk * 2048, 0, 1024),
+                      sdesc_sw128(smem_u32(sV) + kk * 2048 + half * 64, 0, 1024), idU, kk > 0 ? 1u : 0u);
+        umma_commit(&bars[B_Y]);
+        // every product reading stage cur and V is done: next loads
+        if (!mbar_wait(&bars[B_Y], yph, 55)) break;
+        yph ^= 1;
+        if (n + 1 < n1) load_v(n + 1);
+        if (n + 2 < n1) load_kq(n + 2, cur);
+      }
+      // outputs of the last chunk
+      if (mbar_wait(&bars[B_OUT], oph, 56)) {
+        tma_store_3d(&mg.out, sG, h * p.hd, (n1 - 1) * CT, b);
+        bulk_commit();
+      }
+      bulk_wait0();
     }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const uint32_t tL = tmem + ((uint32_t)(quarter * 32) << 16);  // this warp's TMEM lanes
+    // entering state: state_in, then earlier sequence parts, then the earlier segments'
+    // local states (lanes < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR
+    float Rr[EPW];
+#pragma unroll
+    for (int e = 0; e < EPW; ++e) Rr[e] = 0.f;
+    if (f_valid) {
+      if (p.state_in) {
+        const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + e0;
+#pragma unroll
+        for (int e = 0; e < EPW; ++e) Rr[e] = src[e];
+      }
 #pragma unroll 4
-    for (int s = 0; s < p.nprev; ++s) {
-      const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
-      const float4* src =
-          reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride + (size_t)bh * 4096 + f_row * 64 + e0);
+      for (int s = 0; s < p.nprev; ++s) {
+        const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
+        const float4* src = reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride +
+                                                            (size_t)bh * 4096 + f_row * 64 + e0);
 #pragma unroll
-      for (int e = 0; e < EPW / 4; ++e) {
-        const float4 v = src[e];
-        Rr[4 * e] = Ds * Rr[4 * e] + v.x;
-        Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
-        Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
-        Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+        for (int e = 0; e < EPW / 4; ++e) {
+          const float4 v = src[e];
+          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+        }
       }
-    }
 #pragma unroll 4
-    for (int s = 0; s < seg; ++s) {
-      const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
-      const float4* src = reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
+      for (int s = 0; s < seg; ++s) {
+        const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+        const float4* src =
+            reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
 #pragma unroll
-      for (int e = 0; e < EPW / 4; ++e) {
-        const float4 v = src[e];
-        Rr[4 * e] = Ds * Rr[4 * e] + v.x;
-        Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
-        Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
-        Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < EPW / 8; ++c)
-      *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
-  }
-
-  constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
-  constexpr uint32_t idU = idesc_bf16_f32(64, 32, true, true);
-  uint32_t lph0 = 0, lph1 = 0, sph = 0, yph = 0;
-  bool ok = true;
-
-  // phi of a stage's Q and K in place (padding: ones), per-step decay table by warp 0
-  auto prep = [&](int n, int st) {
-    if (!mbar_wait_warp(&bars[st], st ? lph1 : lph0, 41)) return false;
-    if (st) lph1 ^= 1; else lph0 ^= 1;
-    if (tid == 0) pending &= ~(1 << st);
-    if (PERSTEP && warp == 0)
-      chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, tab(st));
-    prep_tile_u<NT, CT, true>(tile(st, 0), p.hd, 1.f);
-    prep_tile_u<NT, CT, true>(tile(st, 2), p.hd, 1.f);
-    if (p.hd < 64) prep_tile_u<NT, CT, false>(tile(st, 1), p.hd, 0.f);
-    fence_proxy_async_smem();
-    return true;
-  };
-  auto issue_s = [&](int st) {  // S_rb = phi(Q_rb) phi(K[0 : 128 (rb + 1)])^T
-#pragma unroll
-    for (int rb = 0; rb < 2; ++rb) {
-      const uint32_t aq = smem_u32(tile(st, 2)) + rb * RB * 128;
-      const uint32_t idS = idesc_bf16_f32(RB, RB * (rb + 1), false, false);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        umma_bf16(tmem + rb * RB, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(tile(st, 0)) + k * 32, 16, 1024),
-                  idS, k > 0 ? 1u : 0u);
-    }
-    umma_commit(&bars[2]);
-  };
-
-  if (n0 < n1) {
-    ok = prep(n0, 0);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (ok && tid == 0) issue_s(0);
-  }
-
-  for (int n = n0; n < n1 && ok; ++n) {
-    const int cur = (n - n0) & 1, nxt = cur ^ 1;
-    uint8_t* sK = tile(cur, 0);
-    uint8_t* sV = tile(cur, 1);
-    uint8_t* sQ = tile(cur, 2);
-    const float* T = tab(cur);
-    // this thread's gate values of chunk n (consumed at the end of the iteration)
-    uint4 graw[2][EPW / 8];
-    if (GATE) {
-#pragma unroll
-      for (int rb = 0; rb < 2; ++rb) {
-        const int t_row = n * CT + rb * RB + my_row;
-        const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(p.gate) + (size_t)b * p.g_sb +
-                                  (size_t)t_row * p.g_st + (size_t)h * p.hd + e0;
-#pragma unroll
-        for (int c = 0; c < EPW / 8; ++c) graw[rb][c] = ldg16_pred(gp + c * 8, e0 + c * 8 < p.hd);
-      }
-    }
-    if (!mbar_wait_warp(&bars[2], sph, 42)) { ok = false; break; }
-    sph ^= 1;
-    tc_fence_after();
-    // k~ = bf16(phi(k) kdec_j) and Qs = bf16(phi(q) qdec_i) in place
-    {
-      constexpr int IT = CT * 8 / NT;
-      uint4 kv[IT], qv[IT];
-#pragma unroll
-      for (int it = 0; it < IT; ++it) {
-        kv[it] = reinterpret_cast<const uint4*>(sK)[tid + it * NT];
-        qv[it] = reinterpret_cast<const uint4*>(sQ)[tid + it * NT];
+        for (int e = 0; e < EPW / 4; ++e) {
+          const float4 v = src[e];
+          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+        }
       }
 #pragma unroll
-      for (int it = 0; it < IT; ++it) {
-        const int idx = tid + it * NT, row = idx >> 3;
-        const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
-        const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
-        float f[8];
-        unpack16<__nv_bfloat16>(kv[it], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] *= kd;
-        reinterpret_cast<uint4*>(sK)[idx] = pack16<__nv_bfloat16>(f);
-        unpack16<__nv_bfloat16>(qv[it], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] *= qd;
-        reinterpret_cast<uint4*>(sQ)[idx] = pack16<__nv_bfloat16>(f);
-      }
+      for (int c = 0; c < EPW / 8; ++c)
+        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
     }
-    // P = bf16(mask(S) decay) of this warpgroup's pieces -> TMEM (packed pairs)
+
+    uint32_t lph0 = 0, lph1 = 0, sph = 0, yph = 0, gph = 0;
+    bool ok = true;
+    // one arrival per compute warp, after every lane's writes and fences
+    auto warp_arrive = [&](int which) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[which]);
+    };
+    // phi of a stage's Q and K in place (padding: ones), per-step decay table by warp 0
+    auto prep = [&](int n, int st) {
+      if (!mbar_wait_warp(&bars[B_L0 + st], st ? lph1 : lph0, 57)) return false;
+      if (st) lph1 ^= 1; else lph0 ^= 1;
+      if (PERSTEP && warp == 0)
+        chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, tab(st));
+      prep_tile_u<NTC, CT, true>(sK(st), 64, 1.f);
+      prep_tile_u<NTC, CT, true>(sQ(st), 64, 1.f);
+      fence_proxy_async_smem();
+      return true;
+    };
+
+    if (n0 < n1) {
+      ok = prep(n0, 0);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      warp_arrive(B_READY);
+      // warp 0's per-step table of chunk n0 is visible to every compute warp
+      warp_arrive(B_SYNC);
+      if (ok && !mbar_wait_warp(&bars[B_SYNC], 0, 63)) ok = false;
+    }
+    uint32_t cph = 1;
+    for (int n = n0; n < n1 && ok; ++n) {
+      const int cur = (n - n0) & 1, nxt = cur ^ 1;
+      uint8_t* K_ = sK(cur);
+      uint8_t* Q_ = sQ(cur);
+      const float* T = tab(cur);
+      if (!mbar_wait_warp(&bars[B_S], sph, 58)) { ok = false; break; }
+      sph ^= 1;
+      tc_fence_after();
+      // k~ = bf16(phi(k) kdec_j) and Qs = bf16(phi(q) qdec_i) in place
+      {
+        constexpr int IT = CT * 8 / NTC;
+        uint4 kv[IT], qv[IT];
 #pragma unroll
-    for (int cc = 0; cc < CPW; ++cc) {
-      const int c = wg * CPW + cc;
-      const int rb = c * PW >= RB ? 1 : 0;
-      const int j0 = c * PW - rb * RB;  // chunk position of the piece's first column
-      const int ib = rb * RB;           // chunk position of the block's first row
-      uint32_t pk[PW / 2];
-      if (j0 > ib + row_hi) {           // above the diagonal for every row of this warp
+        for (int it = 0; it < IT; ++it) {
+          kv[it] = reinterpret_cast<const uint4*>(K_)[tid + it * NTC];
+          qv[it] = reinterpret_cast<const uint4*>(Q_)[tid + it * NTC];
+        }
 #pragma unroll
-        for (int q = 0; q < PW / 2; ++q) pk[q] = 0u;
-      } else {
-        float sv[PW];
-        tmem_ld32(tL + c * PW, sv);
-        const int i = ib + my_row;
-        const bool full = j0 + PW - 1 <= ib + row_lo;  // no masking for any row of this warp
-        const float ci = PERSTEP ? T[i] : 0.f;
+        for (int it = 0; it < IT; ++it) {
+          const int idx = tid + it * NTC, row = idx >> 3;
+          const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
+          const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
+          float f[8];
+          unpack16<__nv_bfloat16>(kv[it], f);
 #pragma unroll
-        for (int q = 0; q < PW / 8; ++q) {
-          float v[8];
-          if (!PERSTEP && full) {
-            // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e
-            const float rf = T[i - j0 - q * 8 - 7];
+          for (int e = 0; e < 8; ++e) f[e] *= kd;
+          reinterpret_cast<uint4*>(K_)[idx] = pack16<__nv_bfloat16>(f);
+          unpack16<__nv_bfloat16>(qv[it], f);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = sv[q * 8 + e] * (rf * T[7 - e]);
-          } else {
+          for (int e = 0; e < 8; ++e) f[e] *= qd;
+          reinterpret_cast<uint4*>(Q_)[idx] = pack16<__nv_bfloat16>(f);
+        }
+      }
+      // P = bf16(mask(S) decay) of this warpgroup's pieces -> TMEM (packed pairs)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int j = j0 + q * 8 + e;
-              float dm = 0.f;
-              if (j <= i) dm = PERSTEP ? fast_exp(ci - T[j]) : T[i - j];
-              v[e] = (j <= i) ? sv[q * 8 + e] * dm : 0.f;
+      for (int cc = 0; cc < CPW; ++cc) {
+        const int c = wg * CPW + cc;
+        const int rb = c * PW >= RB ? 1 : 0;
+        const int j0 = c * PW - rb * RB;  // chunk position of the piece's first column
+        const int ib = rb * RB;           // chunk position of the block's first row
+        uint32_t pk[PW / 2];
+        if (j0 > ib + row_hi) {           // above the diagonal for every row of this warp
+#pragma unroll
+          for (int q = 0; q < PW / 2; ++q) pk[q] = 0u;
+        } else {
+          float sv[PW];
+          tmem_ld32(tL + c * PW, sv);
+          const int i = ib + my_row;
+          const bool full = j0 + PW - 1 <= ib + row_lo;  // no masking for any row of this warp
+          const float ci = PERSTEP ? T[i] : 0.f;
+#pragma unroll
+          for (int q = 0; q < PW / 8; ++q) {
+            float v[8];
+            if (!PERSTEP && full) {
+              // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e
+              const float rf = T[i - j0 - q * 8 - 7];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] = sv[q * 8 + e] * (rf * T[7 - e]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const int j = j0 + q * 8 + e;
+                float dm = 0.f;
+                if (j <= i) dm = PERSTEP ? fast_exp(ci - T[j]) : T[i - j];
+                v[e] = (j <= i) ? sv[q * 8 + e] * dm : 0.f;
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 t2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+              pk[q * 4 + e] = *reinterpret_cast<uint32_t*>(&t2);
             }
           }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            __nv_bfloat162 t2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
-            pk[q * 4 + e] = *reinterpret_cast<uint32_t*>(&t2);
-          }
         }
+        tmem_st16_async(tL + pcol(c), pk);
       }
-      tmem_st16_async(tL + pcol(c), pk);
-    }
-    tmem_wait_st();
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    // Y_rb = Qs_rb bf16(R) + P_rb V;  U = k~^T V in two 32-column halves
-    if (tid == 0) {
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      warp_arrive(B_P);
+      // meanwhile: the next chunk's phi
+      if (n + 1 < n1 && !prep(n + 1, nxt)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars[B_Y], yph, 60)) { ok = false; break; }
+      yph ^= 1;
+      tc_fence_after();
+      // y = bf16(Y) (y_slot is bf16); GroupNorm partial sums
+      float o[2][EPW];
 #pragma unroll
       for (int rb = 0; rb < 2; ++rb) {
-        const uint32_t dY = tmem + YCOL + 64 * rb;
-        const uint32_t aq = smem_u32(sQ) + rb * RB * 128;
+        float yv[EPW];
+        tmem_ld16(tL + YCOL + 64 * rb + e0, yv);
+        float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_bf16(dY, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV,
-                    k > 0 ? 1u : 0u);
-        for (int kk = 0; kk < (rb + 1) * RB / 16; ++kk) {
-          const int c = rb * (RB / PW) + (kk >> 1);
-          umma_bf16_ts(dY, tmem + pcol(c) + (kk & 1) * 8, sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024), idPV, 1u);
-        }
-      }
-#pragma unroll
-      for (int half = 0; half < 2; ++half)
-        for (int kk = 0; kk < CT / 16; ++kk)
-          umma_bf16(tmem + (half ? UCOL1 : UCOL0), sdesc_sw128(smem_u32(sK) + kk * 2048, 0, 1024),
-                    sdesc_sw128(smem_u32(sV) + kk * 2048 + half * 64, 0, 1024), idU, kk > 0 ? 1u : 0u);
-      umma_commit(&bars[3]);
-    }
-    // meanwhile: the next chunk's phi
-    if (n + 1 < n1 && !prep(n + 1, nxt)) { ok = false; break; }
-    if (!mbar_wait_warp(&bars[3], yph, 43)) { ok = false; break; }
-    yph ^= 1;
-    tc_fence_after();
-    if (tid == 0 && n + 2 < n1) issue(n + 2, cur);  // every product reading stage cur is done
-    // y = bf16(Y) (y_slot is bf16); GroupNorm partial sums
-    float o[2][EPW];
-#pragma unroll
-    for (int rb = 0; rb < 2; ++rb) {
-      float yv[EPW];
-      tmem_ld16(tL + YCOL + 64 * rb + e0, yv);
-      float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPW; ++e) {
-        o[rb][e] = bf16_round(yv[e]);
-        if (e0 + e < p.hd) {
+        for (int e = 0; e < EPW; ++e) {
+          o[rb][e] = bf16_round(yv[e]);
           s1 += o[rb][e];
           s2 += o[rb][e] * o[rb][e];
         }
+        sRed[(rb * RB + my_row) * NWG + wg] = make_float2(s1, s2);
       }
-      if (GATE) sRed[(rb * RB + my_row) * NWG + wg] = make_float2(s1, s2);
-    }
-    // R <- gC R + U (fp32) -> sR (bf16) for the next chunk
-    {
-      const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
-      float u[EPW];
-      tmem_ld16(tL + (e0 < 32 ? UCOL0 + e0 : UCOL1 + e0 - 32), u);
+      // R <- gC R + U (fp32) -> sR (bf16) for the next chunk
+      {
+        const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
+        float u[EPW];
+        tmem_ld16(tL + (e0 < 32 ? UCOL0 + e0 : UCOL1 + e0 - 32), u);
 #pragma unroll
-      for (int e = 0; e < EPW; ++e) Rr[e] = fmaf(Rr[e], gC, u[e]);
-      if (f_valid) {
+        for (int e = 0; e < EPW; ++e) Rr[e] = fmaf(Rr[e], gC, u[e]);
+        if (f_valid) {
 #pragma unroll
-        for (int c = 0; c < EPW / 8; ++c)
-          *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
+          for (int c = 0; c < EPW / 8; ++c)
+            *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
+        }
       }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (tid == 0 && n + 1 < n1) issue_s(nxt);
-    // outputs of chunk n (GroupNorm * sigmoid(gate), or plain y) while S(n+1) runs
+      fence_proxy_async_smem();
+      tc_fence_before();
+      if (n + 1 < n1) warp_arrive(B_READY);  // S(n+1) may overwrite U and P now
+      // the GroupNorm partials of every warp (and warp 0's per-step table) are in place
+      warp_arrive(B_SYNC);
+      if (!mbar_wait_warp(&bars[B_SYNC], cph, 61)) { ok = false; break; }
+      cph ^= 1;
+      // outputs of chunk n: GroupNorm(y) * sigmoid(gate) over the gate tile
+      if (!mbar_wait_warp(&bars[B_G], gph, 62)) { ok = false; break; }
+      gph ^= 1;
 #pragma unroll
-    for (int rb = 0; rb < 2; ++rb) {
-      const int t_row = n * CT + rb * RB + my_row;
-      __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
-                          (size_t)t_row * p.y_st + e0;
-      if (GATE) {
+      for (int rb = 0; rb < 2; ++rb) {
+        const int row = rb * RB + my_row;
         float S1 = 0.f, S2 = 0.f;
 #pragma unroll
         for (int w = 0; w < NWG; ++w) {
-          const float2 v = sRed[(rb * RB + my_row) * NWG + w];
+          const float2 v = sRed[row * NWG + w];
           S1 += v.x;
           S2 += v.y;
         }
-        const float mean = S1 / (float)p.hd;
-        // sum over the hd lanes of (y - mean)^2 plus the reference's padded lanes (block
-        // width 64), which add (64 - hd) mean^2
-        const float var = fmaxf(S2 - S1 * mean, 0.f) / (float)p.hd + (float)(64 - p.hd) * mean * mean / (float)p.hd;
+        const float mean = S1 * (1.f / 64.f);
+        const float var = fmaxf(S2 - S1 * mean, 0.f) * (1.f / 64.f);
         const float inv = rsqrtf(var + 1e-5f);
 #pragma unroll
         for (int c = 0; c < EPW / 8; ++c) {
-          if (e0 + c * 8 >= p.hd) continue;
+          uint4* gs = reinterpret_cast<uint4*>(sG + sw128_chunk(row, (e0 >> 3) + c));
           float g[8], r[8];
-          unpack16<__nv_bfloat16>(graw[rb][c], g);
+          unpack16<__nv_bfloat16>(*gs, g);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int d = e0 + c * 8 + e;
             const float ygn = ((o[rb][c * 8 + e] - mean) * inv) * sGn[d] + sGn[64 + d];
             r[e] = ygn * fast_sigmoid(g[e]);
           }
-          stg16(op + c * 8, pack16<__nv_bfloat16>(r));
+          *gs = pack16<__nv_bfloat16>(r);
         }
-      } else if (p.y_vec) {
-#pragma unroll
-        for (int c = 0; c < EPW / 8; ++c)
-          if (e0 + c * 8 < p.hd) stg16(op + c * 8, pack16<__nv_bfloat16>(&o[rb][c * 8]));
-      } else {
-#pragma unroll
-        for (int e = 0; e < EPW; ++e)
-          if (e0 + e < p.hd) op[e] = __float2bfloat16_rn(o[rb][e]);
       }
+      fence_proxy_async_smem();
+      warp_arrive(B_OUT);
     }
-  }
-  // after a timed-out wait: let this CTA's own loads in flight land (bounded) before exit
-  if (!ok && tid == 0) {
-    if (pending & 1) mbar_wait(&bars[0], lph0, 44);
-    if (pending & 2) mbar_wait(&bars[1], lph1, 44);
-  }
-  if (ok && seg == p.nseg - 1 && p.state_out && f_valid) {
-    float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0;
+    if (ok && seg == p.nseg - 1 && p.state_out && f_valid) {
+      float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0;
 #pragma unroll
-    for (int e = 0; e < EPW; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(Rr[e], Rr[e + 1], Rr[e + 2], Rr[e + 3]);
+      for (int e = 0; e < EPW; e += 4)
+        *reinterpret_cast<float4*>(dst + e) = make_float4(Rr[e], Rr[e + 1], Rr[e + 2], Rr[e + 3]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1193,11 +1231,24 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
     slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), kStateThreads, sm, s>>>(mk, mv, p);
     if (int e = launch_status("slot_tc_state_kernel")) return e;
   }
-  if constexpr (CT == 256) {
-    const size_t sm = pipe::SMEM;
-    cudaFuncSetAttribute(slot_tc_pipe_kernel<PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    slot_tc_pipe_kernel<PS, GATE><<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq, mk, mv, p);
-    return launch_status("slot_tc_pipe_kernel");
+  // chunk 256 with the fused gate and head_dim 64: the warp-specialized kernel, when a
+  // head's 64 columns of the gate and of the outputs are contiguous and 16-byte aligned
+  // (gate tile in by TMA, one TMA store of the gated outputs per chunk)
+  if constexpr (CT == 256 && GATE) {
+    const bool pipe_ok = sp.hd == 64 && sp.y_sh == 64 && aligned16(sp.y) && sp.y_st % 8 == 0 &&
+                         (B == 1 || sp.y_sb % 8 == 0) && aligned16(gt->gate) && gt->g_st % 8 == 0 &&
+                         (B == 1 || gt->g_sb % 8 == 0) && aligned16(gt->gn_w) && aligned16(gt->gn_b);
+    if (pipe_ok) {
+      SlotPipeMaps mg{};
+      if (int e = make_map(&mg.gate, gt->gate, W, sp.L, B, gt->g_st, B > 1 ? gt->g_sb : (int64_t)sp.L * gt->g_st, CT))
+        return e;
+      if (int e = make_map(&mg.out, sp.y, W, sp.L, B, sp.y_st, B > 1 ? sp.y_sb : (int64_t)sp.L * sp.y_st, CT))
+        return e;
+      const size_t sm = pipe::SMEM;
+      cudaFuncSetAttribute(slot_tc_pipe_kernel<PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      slot_tc_pipe_kernel<PS><<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq, mk, mv, mg, p);
+      return launch_status("slot_tc_pipe_kernel");
+    }
   }
   const size_t sm = smem_out_bytes<CT>();
   cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);

@@ -169,3 +169,37 @@ def test_fused_gate_epilogue_vs_oracle(B, L, ds, dm, H, C):
     ref = O.gnorm_gate_cat(y_slot, torch.zeros(B, L, ds).bfloat16(), projs, gw, gb, ds, H, C, mode="fixed")
     assert rel(comb[..., ds:], ref[..., ds:]) < BF16_TOL, rel(comb[..., ds:], ref[..., ds:])
     assert float(comb[..., :ds].abs().max()) == 0.0  # the epilogue writes only its own columns
+
+
+@pytest.mark.parametrize("per_step", [False, True])
+def test_fused_gate_long_segments_vs_oracle(per_step):
+    """Config-5 head layout (H 12, head_dim 64, chunk 256) at L 16384: 64 chunks per head
+    over 11 segments, so every CTA of the chunk-256 gate kernel walks several chunks
+    (alternating shared-memory stages, gate tile in and outputs out by TMA) after folding
+    the earlier segments' states; constant and per-step decay."""
+    B, L, ds, dm, H, C = 1, 16384, 64, 768, 12, 256
+    hd, P, so = dm // H, 3 * ds + 4 * dm, 3 * ds
+    g = torch.Generator().manual_seed(77 + int(per_step))
+    projs = (0.6 * torch.randn(B, L, P, generator=g)).bfloat16()
+    gw = (1 + 0.2 * torch.randn(dm, generator=g)).bfloat16()
+    gb = (0.2 * torch.randn(dm, generator=g)).bfloat16()
+    gamma = torch.exp(-torch.nn.functional.softplus(torch.randn(H, generator=g) - 3.0)).bfloat16()
+    log_a = torch.log(torch.sigmoid(torch.randn(B, L, H, generator=g) + 4.0))
+    pj = projs.to(DEV)
+    comb = torch.zeros(B, L, ds + dm, device=DEV, dtype=torch.bfloat16)
+    kw = {"log_a": log_a.to(DEV)} if per_step else {"gamma": gamma.to(DEV)}
+    _, R = ops.slot_scan_gate(pj[..., so:so + dm], pj[..., so + dm:so + 2 * dm], pj[..., so + 2 * dm:so + 3 * dm],
+                              H, C, pj[..., so + 3 * dm:], gw.to(DEV), gb.to(DEV), comb[..., ds:],
+                              (L * (ds + dm), hd, ds + dm), return_state=True, **kw)
+    torch.cuda.synchronize()
+    assert no_device_error()
+    if per_step:
+        qkv = [projs[..., so + i * dm:so + (i + 1) * dm].reshape(B, L, H, hd) for i in range(3)]
+        y, Rr = O.slot_scan_decay_fwd(*qkv, log_a, C)
+        y_slot = y.permute(0, 2, 1, 3).reshape(B * H, L // C, C, hd)
+    else:
+        y_slot, Rr = O.slot_fwd(projs, gamma, dm, H, C, so, block_c=C, return_state=True)
+    ref = O.gnorm_gate_cat(y_slot, torch.zeros(B, L, ds).bfloat16(), projs, gw, gb, ds, H, C, mode="fixed")
+    assert rel(comb[..., ds:], ref[..., ds:]) < BF16_TOL, rel(comb[..., ds:], ref[..., ds:])
+    assert float(comb[..., :ds].abs().max()) == 0.0
+    assert rel(R.reshape(-1, 64, 64), Rr.reshape(-1, 64, 64)) < STATE_TOL
