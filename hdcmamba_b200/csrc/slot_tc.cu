@@ -264,6 +264,170 @@ __global__ void __launch_bounds__(kStateThreads, CT == 256 ? 1 : 2)
 }
 
 // ---------------------------------------------------------------------------------
+// Pass A for chunk 256, warp-specialized (slot_tc_state_pipe_kernel): 16 compute warps
+// form k~ = bf16(bf16(phi(k)) kdec_j) in place and fold R <- gC R + U in registers; one
+// issue warp keeps three chunks of K and V in flight (TMA ring) and issues U = k~^T V
+// into one of two TMEM buffers, so the next chunk's k~ overlaps the current product.
+// Barrier phases follow from the chunk index (stage st = i % 3 completes once per 3
+// chunks, U buffer i & 1 once per 2), and every wait is bounded.
+// ---------------------------------------------------------------------------------
+namespace spipe {
+constexpr int CT = 256, NS = 3, NCW = 16, NTC = NCW * 32, NT = NTC + 32;
+constexpr int TILE = CT * 128, TABN = CT + 4;
+// mbarriers: TMA stage full [NS], k~ ready [NS] (per compute warp), per-step table ready
+// [NS] (warp 0), U product done [2], U read [2] (per compute warp)
+enum { B_FULL = 0, B_PREP = NS, B_TAB = 2 * NS, B_UFULL = 3 * NS, B_UFREE = 3 * NS + 2, NBAR = 3 * NS + 4 };
+constexpr size_t SMEM = 1024 + NS * 2 * TILE + NS * TABN * 4 + NBAR * 8 + 16;
+}  // namespace spipe
+
+template <bool PERSTEP>
+__global__ void __launch_bounds__(spipe::NT, 1)
+    slot_tc_state_pipe_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
+                              SlotTcParams p) {
+  using namespace spipe;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = align1024(smem_raw);
+  float* sTab = reinterpret_cast<float*>(base + NS * 2 * TILE);  // [NS][TABN] (constant decay: [0])
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + NS * TABN);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + NBAR);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, cgrp = warp >> 2;
+  const int nseg_a = p.nseg_a;
+  const int bh = blockIdx.x / nseg_a, seg = blockIdx.x - bh * nseg_a;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
+  auto sK = [&](int st) { return base + st * 2 * TILE; };
+  auto sV = [&](int st) { return base + st * 2 * TILE + TILE; };
+  auto tab = [&](int st) { return sTab + (PERSTEP ? st * TABN : 0); };
+
+  if (warp == 0) {
+    tmem_alloc(sTmem, 128);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < NBAR; ++i)
+      mbar_init(&bars[i], ((i >= B_PREP && i < B_PREP + NS) || i >= B_UFREE) ? NCW : 1);
+    fence_mbar_init();
+  }
+  if (!PERSTEP) {
+    const float lg = logf(__bfloat162float(static_cast<const __nv_bfloat16*>(p.gamma)[h]));
+    for (int k = tid; k <= CT; k += NT) sTab[k] = expf((float)k * lg);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tU = *sTmem;
+  bool ok = true;
+
+  if (warp == NCW) {
+    // ------------------------------------------------------------ issue warp
+    if (lane == 0 && n0 < n1) {
+      tma_prefetch_map(&mapK);
+      tma_prefetch_map(&mapV);
+      auto load = [&](int n) {
+        const int st = (n - n0) % NS;
+        mbar_expect_tx(&bars[B_FULL + st], 2 * TILE);
+        tma_load_3d(sK(st), &mapK, h * p.hd, n * CT, b, &bars[B_FULL + st]);
+        tma_load_3d(sV(st), &mapV, h * p.hd, n * CT, b, &bars[B_FULL + st]);
+      };
+      for (int n = n0; n < min(n1, n0 + NS); ++n) load(n);
+      constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
+      for (int n = n0; n < n1; ++n) {
+        const int i = n - n0, st = i % NS, ub = i & 1;
+        if (!mbar_wait(&bars[B_PREP + st], (uint32_t)((i / NS) & 1), 71)) break;
+        if (i >= 2 && !mbar_wait(&bars[B_UFREE + ub], (uint32_t)(((i >> 1) - 1) & 1), 72)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < CT / 16; ++kk)
+          umma_bf16(tU + ub * 64, sdesc_sw128(smem_u32(sK(st)) + kk * 2048, 0, 1024),
+                    sdesc_sw128(smem_u32(sV(st)) + kk * 2048, 0, 1024), idU, kk > 0 ? 1u : 0u);
+        umma_commit(&bars[B_UFULL + ub]);
+        if (n + NS < n1) {  // this stage's product is done: refill it
+          if (!mbar_wait(&bars[B_UFULL + ub], (uint32_t)((i >> 1) & 1), 73)) break;
+          load(n + NS);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float R[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) R[e] = 0.f;
+    float D = 1.f, g_even = 1.f, g_odd = 1.f;  // gC of the chunks whose U is pending
+    auto warp_arrive = [&](int which) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[which]);
+    };
+    auto prep = [&](int n) {
+      const int i = n - n0, st = i % NS;
+      const uint32_t ph = (uint32_t)((i / NS) & 1);
+      if (!mbar_wait_warp(&bars[B_FULL + st], ph, 74)) return false;
+      const float* T = tab(st);
+      if (PERSTEP) {
+        if (warp == 0) {
+          chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, tab(st));
+          warp_arrive(B_TAB + st);
+        }
+        if (!mbar_wait_warp(&bars[B_TAB + st], ph, 75)) return false;
+      }
+      const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
+      if (i & 1) g_odd = gC; else g_even = gC;
+      // k~ = bf16(bf16(phi(k)) * kdec_j) in place (feature padding: k = 1)
+      constexpr int IT = CT * 8 / NTC;
+      uint8_t* K_ = sK(st);
+      uint4 kv[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) kv[it] = reinterpret_cast<const uint4*>(K_)[tid + it * NTC];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = tid + it * NTC, row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
+        const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
+        float f[8];
+        unpack16<__nv_bfloat16>(kv[it], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = ((c0 + e < p.hd) ? bf16_round(phi_fast(f[e])) : 1.f) * kd;
+        reinterpret_cast<uint4*>(K_)[idx] = pack16<__nv_bfloat16>(f);
+      }
+      if (p.hd < 64) prep_tile<NTC>(sV(st), CT, p.hd, false, 0.f);
+      fence_proxy_async_smem();
+      warp_arrive(B_PREP + st);
+      return true;
+    };
+    if (n0 < n1) ok = prep(n0);
+    for (int n = n0; n < n1 && ok; ++n) {
+      const int i = n - n0, ub = i & 1;
+      if (n + 1 < n1 && !prep(n + 1)) { ok = false; break; }
+      if (!mbar_wait_warp(&bars[B_UFULL + ub], (uint32_t)((i >> 1) & 1), 76)) { ok = false; break; }
+      tc_fence_after();
+      float u[16];
+      tmem_ld16(tU + ub * 64 + lane_base + cgrp * 16, u);
+      tc_fence_before();
+      warp_arrive(B_UFREE + ub);
+      const float gC = ub ? g_odd : g_even;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) R[e] = R[e] * gC + u[e];
+      D *= gC;
+    }
+    if (ok && lane < 16) {
+      const int f = quarter * 16 + lane;
+      float* dst = p.Rseg + ((size_t)bh * p.nseg + seg) * 4096 + f * 64 + cgrp * 16;
+#pragma unroll
+      for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
+    }
+    if (ok && tid == 0) p.Dseg[(size_t)bh * p.nseg + seg] = D;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tU, 128);
+}
+
+template <int CT, bool PS>
+static int launch_state(const CUtensorMap& mk, const CUtensorMap& mv, const SlotTcParams& p, unsigned grid,
+                        cudaStream_t s);
+
+// ---------------------------------------------------------------------------------
 // Pass B: outputs.  NWG warpgroups (NWG*128 threads); all of them cover every TMEM lane
 // (row) and split the columns.  Both row blocks of a chunk go through the tensor cores
 // together, so a chunk takes two round trips:
@@ -1172,6 +1336,23 @@ static size_t smem_out_bytes() {
 }
 static size_t smem_state_bytes(int CT) { return 1024 + 4 * CT * 128 + (CT + 4) * 4 + 64; }
 
+// pass A: the warp-specialized kernel for chunk 256, the lock-step one otherwise
+template <int CT, bool PS>
+static int launch_state(const CUtensorMap& mk, const CUtensorMap& mv, const SlotTcParams& p, unsigned grid,
+                        cudaStream_t s) {
+  if constexpr (CT == 256) {
+    cudaFuncSetAttribute(slot_tc_state_pipe_kernel<PS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)spipe::SMEM);
+    slot_tc_state_pipe_kernel<PS><<<grid, spipe::NT, spipe::SMEM, s>>>(mk, mv, p);
+    return launch_status("slot_tc_state_pipe_kernel");
+  } else {
+    const size_t sm = smem_state_bytes(CT);
+    cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    slot_tc_state_kernel<CT, PS><<<grid, kStateThreads, sm, s>>>(mk, mv, p);
+    return launch_status("slot_tc_state_kernel");
+  }
+}
+
 // One output CTA per SM for chunk 128 / 256 (512 TMEM columns), two for chunk 64.
 static void plan_segments(int64_t BH, int N, int C, int* nseg, int* seg_len) {
   const int slots = num_sms() * (C == 64 ? 2 : 1);
@@ -1226,10 +1407,7 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
   // with a carry the workspace already holds every segment's state (hdc_slot_state_fwd)
   if (p.nseg > 1 && !carry) {
     p.nseg_a = p.nseg - 1;
-    const size_t sm = smem_state_bytes(CT);
-    cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg_a), kStateThreads, sm, s>>>(mk, mv, p);
-    if (int e = launch_status("slot_tc_state_kernel")) return e;
+    if (int e = launch_state<CT, PS>(mk, mv, p, (unsigned)(BH * p.nseg_a), s)) return e;
   }
   // chunk 256 with the fused gate and head_dim 64: the warp-specialized kernel, when a
   // head's 64 columns of the gate and of the outputs are contiguous and 16-byte aligned
@@ -1293,10 +1471,7 @@ static int run_tc_state(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t 
   const int64_t sb = B > 1 ? in_sb : (int64_t)sp.L * in_st;
   if (int e = make_map(&mk, sp.k, W, sp.L, B, in_st, sb, CT)) return e;
   if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
-  const size_t sm = smem_state_bytes(CT);
-  cudaFuncSetAttribute(slot_tc_state_kernel<CT, PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  slot_tc_state_kernel<CT, PS><<<(unsigned)(BH * p.nseg), kStateThreads, sm, s>>>(mk, mv, p);
-  if (int e = launch_status("slot_tc_state_kernel")) return e;
+  if (int e = launch_state<CT, PS>(mk, mv, p, (unsigned)(BH * p.nseg), s)) return e;
   slot_fold_kernel<<<(unsigned)BH, 256, 0, s>>>(p);
   return launch_status("slot_fold_kernel");
 }
