@@ -91,7 +91,14 @@ __device__ __forceinline__ void prep_tile_u(uint8_t* tile, int hd, float pad) {
     const int idx = threadIdx.x + it * NT;
     const int row = idx >> 3, pc = idx & 7;
     const int c0 = ((pc ^ (row & 7)) << 3);
-    if (!PHI && c0 + 8 <= hd) continue;
+    if (c0 + 8 <= hd) {  // no padding in this 16-byte chunk
+      if (!PHI) continue;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v[it]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = phi_bf2(w[i]);
+      reinterpret_cast<uint4*>(tile)[idx] = v[it];
+      continue;
+    }
     float f[8];
     unpack16<__nv_bfloat16>(v[it], f);
 #pragma unroll
@@ -384,11 +391,19 @@ __global__ void __launch_bounds__(spipe::NT, 1)
       for (int it = 0; it < IT; ++it) {
         const int idx = tid + it * NTC, row = idx >> 3, pc = idx & 7, c0 = ((pc ^ (row & 7)) << 3);
         const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
-        float f[8];
-        unpack16<__nv_bfloat16>(kv[it], f);
+        if (c0 + 8 <= p.hd) {  // packed: phi in bf16 pairs, then the fp32 product, rounded
+          const uint64_t kd2 = f2_make(kd, kd);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&kv[it]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = ((c0 + e < p.hd) ? bf16_round(phi_fast(f[e])) : 1.f) * kd;
-        reinterpret_cast<uint4*>(K_)[idx] = pack16<__nv_bfloat16>(f);
+          for (int i = 0; i < 4; ++i) w[i] = f2_to_bf2(f2_mul(bf2_to_f2(phi_bf2(w[i])), kd2));
+          reinterpret_cast<uint4*>(K_)[idx] = kv[it];
+        } else {
+          float f[8];
+          unpack16<__nv_bfloat16>(kv[it], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = ((c0 + e < p.hd) ? bf16_round(phi_fast(f[e])) : 1.f) * kd;
+          reinterpret_cast<uint4*>(K_)[idx] = pack16<__nv_bfloat16>(f);
+        }
       }
       if (p.hd < 64) prep_tile<NTC>(sV(st), CT, p.hd, false, 0.f);
       fence_proxy_async_smem();
@@ -872,7 +887,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 //   wait S(n)                 S_rb = phi(Q_rb) phi(K)^T
 //   k~ = bf16(phi(k) kdec_j), Qs = bf16(phi(q) qdec_i) in place (the reference rounds the
 //   q-decayed queries before the state product, hdcmamba/model.py:267-268);
-//   P = bf16(mask(S) decay) into TMEM over the S columns it came from     -> arrive P
+//   P = bf16(mask(S) decay) into TMEM                                      -> arrive P
 //   phi of chunk n+1's Q and K                      || issue warp: Y_rb = Qs_rb bf16(R) + P_rb V,
 //                                                                  U = k~^T V
 //   wait Y; y = bf16(Y), GroupNorm partial sums; R <- gC R + U -> bf16 R  -> arrive ready
@@ -880,9 +895,10 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 //                                                   || issue warp: S(n+1), TMA store of
 //                                                      chunk n's outputs, gate of n+1
 // TMEM (512 columns): S of row block 0 in [0,128), of row block 1 in [128,384), cut in
-// 32-column pieces; piece c keeps its P (16 packed columns) in its first half when c is
-// even and in its second half when c is odd, so [16,48) and [80,112) hold no P and take
-// the two 32-column halves of U.  Y_rb in [384 + 64 rb, +64).
+// 32-column pieces.  A row-block-0 piece keeps its P (16 packed columns) in its own first
+// half; row block 1's P goes to [384,512).  Y and U are written only by the second round of
+// products, which starts after every warp has read its S pieces, so they take row block
+// 1's S columns: Y_rb in [128 + 64 rb, +64), U in [256,320).
 // Every wait is bounded; compute warps synchronise with each other through an mbarrier
 // (bounded wait), never through bar.sync inside the loop.
 // ---------------------------------------------------------------------------------
@@ -890,14 +906,16 @@ namespace pipe {
 constexpr int CT = 256, RB = 128, NWG = 4, NCW = NWG * 4, NTC = NCW * 32, NT = NTC + 32, EPW = 16, PW = 32;
 constexpr int NPIECE = 3 * RB / PW;  // 12 pieces of S (4 of row block 0, 8 of row block 1)
 constexpr int CPW = NPIECE / NWG;    // per warpgroup
-constexpr int YCOL = 3 * RB;
-constexpr int UCOL0 = 16, UCOL1 = 80;
+constexpr int YCOL = RB, UCOL = 2 * RB, P1COL = 3 * RB;
 constexpr int TILE = CT * 128;       // one [CT x 64] bf16 tile
 constexpr int TABN = CT + 4;
 // mbarriers
 enum { B_L0, B_L1, B_V, B_G, B_S, B_Y, B_READY, B_P, B_OUT, B_SYNC, NBAR };
 constexpr size_t SMEM = 1024 + 6 * TILE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + CT * NWG * 8 + NBAR * 8 + 16;
-__device__ __forceinline__ uint32_t pcol(int c) { return (uint32_t)(c * PW + ((c & 1) ? 16 : 0)); }
+// TMEM column of the packed P of piece c (row block 0: in place; row block 1: [384,512))
+__device__ __forceinline__ uint32_t pcol(int c) {
+  return c < RB / PW ? (uint32_t)(c * PW) : (uint32_t)(P1COL + (c - RB / PW) * (PW / 2));
+}
 }  // namespace pipe
 
 // gate / output tensor maps travel with the parameters
@@ -985,7 +1003,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       load_g(n0);
       if (n0 + 1 < n1) load_kq(n0 + 1, 1);
       constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
-      constexpr uint32_t idU = idesc_bf16_f32(64, 32, true, true);
+      constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
       uint32_t rph = 0, pph = 0, yph = 0, oph = 0;
       for (int n = n0; n < n1; ++n) {
         const int cur = (n - n0) & 1;
@@ -1012,7 +1030,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           bulk_wait_read0();
           load_g(n);
         }
-        // Y_rb = Qs_rb bf16(R) + P_rb V;  U = k~^T V in two 32-column halves
+        // Y_rb = Qs_rb bf16(R) + P_rb V;  U = k~^T V
         if (!mbar_wait(&bars[B_P], pph, 53)) break;
         pph ^= 1;
         if (!mbar_wait(&bars[B_V], (uint32_t)((n - n0) & 1), 54)) break;
@@ -1033,11 +1051,9 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           }
         }
 #pragma unroll
-        for (int half = 0; half < 2; ++half)
-#pragma unroll
-          for (int kk = 0; kk < CT / 16; ++kk)
-            umma_bf16(tmem + (half ? UCOL1 : UCOL0), sdesc_sw128(smem_u32(sK(cur)) + kk * 2048, 0, 1024),
-                      sdesc_sw128(smem_u32(sV) + kk * 2048 + half * 64, 0, 1024), idU, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < CT / 16; ++kk)
+          umma_bf16(tmem + UCOL, sdesc_sw128(smem_u32(sK(cur)) + kk * 2048, 0, 1024),
+                    sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, kk > 0 ? 1u : 0u);
         umma_commit(&bars[B_Y]);
         // every product reading stage cur and V is done: next loads
         if (!mbar_wait(&bars[B_Y], yph, 55)) break;
@@ -1151,15 +1167,16 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           const int idx = tid + it * NTC, row = idx >> 3;
           const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
           const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
-          float f[8];
-          unpack16<__nv_bfloat16>(kv[it], f);
+          const uint64_t kd2 = f2_make(kd, kd), qd2 = f2_make(qd, qd);
+          uint32_t* wk = reinterpret_cast<uint32_t*>(&kv[it]);
+          uint32_t* wq = reinterpret_cast<uint32_t*>(&qv[it]);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] *= kd;
-          reinterpret_cast<uint4*>(K_)[idx] = pack16<__nv_bfloat16>(f);
-          unpack16<__nv_bfloat16>(qv[it], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] *= qd;
-          reinterpret_cast<uint4*>(Q_)[idx] = pack16<__nv_bfloat16>(f);
+          for (int i = 0; i < 4; ++i) {
+            wk[i] = f2_to_bf2(f2_mul(bf2_to_f2(wk[i]), kd2));
+            wq[i] = f2_to_bf2(f2_mul(bf2_to_f2(wq[i]), qd2));
+          }
+          reinterpret_cast<uint4*>(K_)[idx] = kv[it];
+          reinterpret_cast<uint4*>(Q_)[idx] = qv[it];
         }
       }
       // P = bf16(mask(S) decay) of this warpgroup's pieces -> TMEM (packed pairs)
@@ -1183,10 +1200,15 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           for (int q = 0; q < PW / 8; ++q) {
             float v[8];
             if (!PERSTEP && full) {
-              // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e
+              // gamma^(i-j) = gamma^(i-j0-8q-7) * gamma^(7-e) for j = j0 + 8q + e (pairs)
               const float rf = T[i - j0 - q * 8 - 7];
+              const uint64_t rf2 = f2_make(rf, rf);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] = sv[q * 8 + e] * (rf * T[7 - e]);
+              for (int e = 0; e < 8; e += 2) {
+                const uint64_t d2 = f2_mul(rf2, f2_make(T[7 - e], T[6 - e]));
+                pk[q * 4 + e / 2] = f2_to_bf2(f2_mul(f2_make(sv[q * 8 + e], sv[q * 8 + e + 1]), d2));
+              }
+              continue;
             } else {
 #pragma unroll
               for (int e = 0; e < 8; ++e) {
@@ -1233,7 +1255,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       {
         const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
         float u[EPW];
-        tmem_ld16(tL + (e0 < 32 ? UCOL0 + e0 : UCOL1 + e0 - 32), u);
+        tmem_ld16(tL + UCOL + e0, u);
 #pragma unroll
         for (int e = 0; e < EPW; ++e) Rr[e] = fmaf(Rr[e], gC, u[e]);
         if (f_valid) {
@@ -1265,18 +1287,27 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         const float mean = S1 * (1.f / 64.f);
         const float var = fmaxf(S2 - S1 * mean, 0.f) * (1.f / 64.f);
         const float inv = rsqrtf(var + 1e-5f);
+        const uint64_t mean2 = f2_make(mean, mean), inv2 = f2_make(inv, inv), half2 = f2_make(0.5f, 0.5f);
 #pragma unroll
         for (int c = 0; c < EPW / 8; ++c) {
           uint4* gs = reinterpret_cast<uint4*>(sG + sw128_chunk(row, (e0 >> 3) + c));
-          float g[8], r[8];
-          unpack16<__nv_bfloat16>(*gs, g);
+          uint4 gv = *gs;
+          uint32_t* w = reinterpret_cast<uint32_t*>(&gv);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
+          for (int e = 0; e < 8; e += 2) {
             const int d = e0 + c * 8 + e;
-            const float ygn = ((o[rb][c * 8 + e] - mean) * inv) * sGn[d] + sGn[64 + d];
-            r[e] = ygn * fast_sigmoid(g[e]);
+            // ((y - mean) * inv) * w + b, then * sigmoid(g) = * (0.5 tanh(g / 2) + 0.5)
+            const float2 gw = *reinterpret_cast<const float2*>(&sGn[d]);
+            const float2 gb = *reinterpret_cast<const float2*>(&sGn[64 + d]);
+            const uint64_t ygn = f2_fma(f2_mul(f2_sub(f2_make(o[rb][c * 8 + e], o[rb][c * 8 + e + 1]), mean2), inv2),
+                                        f2_make(gw.x, gw.y), f2_make(gb.x, gb.y));
+            float tl, th;
+            f2_split(f2_mul(bf2_to_f2(w[e / 2]), half2), tl, th);
+            asm("tanh.approx.f32 %0, %0;" : "+f"(tl));
+            asm("tanh.approx.f32 %0, %0;" : "+f"(th));
+            w[e / 2] = f2_to_bf2(f2_mul(ygn, f2_fma(half2, f2_make(tl, th), half2)));
           }
-          *gs = pack16<__nv_bfloat16>(r);
+          *gs = gv;
         }
       }
       fence_proxy_async_smem();
@@ -1442,11 +1473,19 @@ __global__ void __launch_bounds__(256) slot_fold_kernel(SlotTcParams p) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) R[e] = 0.f;
   float D = 1.f;
+  // (unrolled so that the loads of several segments are in flight together)
+#pragma unroll 4
   for (int s = 0; s < p.nseg; ++s) {
     const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
-    const float* src = p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + threadIdx.x * 16;
+    const float4* src = reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + threadIdx.x * 16);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) R[e] = Ds * R[e] + src[e];
+    for (int e = 0; e < 4; ++e) {
+      const float4 v = src[e];
+      R[4 * e] = Ds * R[4 * e] + v.x;
+      R[4 * e + 1] = Ds * R[4 * e + 1] + v.y;
+      R[4 * e + 2] = Ds * R[4 * e + 2] + v.z;
+      R[4 * e + 3] = Ds * R[4 * e + 3] + v.w;
+    }
     D *= Ds;
   }
   float* dst = p.state_out + (size_t)bh * 4096 + threadIdx.x * 16;

@@ -348,7 +348,67 @@ __device__ __forceinline__ float fast_exp(float x) {
   return y;
 }
 
-// ---------------------------------------------------------------- UMMA
+// ---------------------------------------------------------------- packed pairs
+// sm_100 executes add / sub / mul / fma on two fp32 lanes held in a 64-bit register pair
+// with one instruction; each lane rounds exactly as the scalar instruction (to nearest).
+__device__ __forceinline__ uint64_t f2_make(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2_split(uint64_t d, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// two bf16 (low half first) <-> an fp32 pair; the narrowing rounds to nearest
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t x) {
+  return f2_make(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+}
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t d) {
+  float lo, hi;
+  f2_split(d, lo, hi);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// bf16(phi(z)) for two bf16 lanes, phi(z) = z > 0 ? z + 1 : exp(z) computed as
+// max(z, 0) + bf16(exp(min(z, 0))) with bf16x2 min / max / add: exp(0) = 1, so z > 0 gives
+// the single rounding of z + 1, and z <= 0 adds 0 to the rounded exp(z) exactly -- the same
+// bits as rounding the fp32 max(z, 0) + exp(min(z, 0)) once.
+__device__ __forceinline__ uint32_t phi_bf2(uint32_t z) {
+  uint32_t mn, mx;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(mn) : "r"(z), "r"(0u));
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(mx) : "r"(z), "r"(0u));
+  float lo, hi;
+  f2_split(f2_mul(bf2_to_f2(mn), f2_make(1.4426950408889634f, 1.4426950408889634f)), lo, hi);
+  asm("ex2.approx.ftz.f32 %0, %0;" : "+f"(lo));
+  asm("ex2.approx.ftz.f32 %0, %0;" : "+f"(hi));
+  uint32_t e, r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(e) : "f"(hi), "f"(lo));
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(mx), "r"(e));
+  return r;
+}
+
+// ---------------------------------------------------------------- UMMA// ---------------------------------------------------------------- UMMA
 // kind::f16 MMA, D (fp32, TMEM) (+)= A (smem desc) * B (smem desc); issued by one thread.
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accumulate) {
