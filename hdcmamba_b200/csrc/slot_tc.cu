@@ -344,10 +344,11 @@ __global__ void __launch_bounds__(spipe::NT, 1)
         if (!mbar_wait(&bars[B_PREP + st], (uint32_t)((i / NS) & 1), 71)) break;
         if (i >= 2 && !mbar_wait(&bars[B_UFREE + ub], (uint32_t)(((i >> 1) - 1) & 1), 72)) break;
         tc_fence_after();
+        const uint64_t dK = sdesc_sw128(smem_u32(sK(st)), 0, 1024), dV = sdesc_sw128(smem_u32(sV(st)), 0, 1024);
 #pragma unroll
         for (int kk = 0; kk < CT / 16; ++kk)
-          umma_bf16(tU + ub * 64, sdesc_sw128(smem_u32(sK(st)) + kk * 2048, 0, 1024),
-                    sdesc_sw128(smem_u32(sV(st)) + kk * 2048, 0, 1024), idU, kk > 0 ? 1u : 0u);
+          umma_bf16(tU + ub * 64, dK + (uint64_t)((kk * 2048) >> 4), dV + (uint64_t)((kk * 2048) >> 4), idU,
+                    kk > 0 ? 1u : 0u);
         umma_commit(&bars[B_UFULL + ub]);
         if (n + NS < n1) {  // this stage's product is done: refill it
           if (!mbar_wait(&bars[B_UFULL + ub], (uint32_t)((i >> 1) & 1), 73)) break;
@@ -937,7 +938,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
   uint8_t* sR = base + 6 * TILE;                           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [2][TABN] (per-step: one per stage)
   float* sGn = sTab + 2 * TABN;                            // [128] gn weight | bias of this head
-  float2* sRed = reinterpret_cast<float2*>(sGn + 128);     // [CT][NWG] GroupNorm (sum, sum of squares)
+  float2* sRed = reinterpret_cast<float2*>(sGn + 128);     // [NWG][CT] GroupNorm (sum, sum of squares)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * NWG);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + NBAR);
 
@@ -1011,15 +1012,16 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         if (!mbar_wait(&bars[B_READY], rph, 51)) break;
         rph ^= 1;
         tc_fence_after();
+        // descriptors of the stage's tiles; an MMA's operand is the base plus offset / 16
+        const uint64_t dK = sdesc_sw128(smem_u32(sK(cur)), 16, 1024), dQ = sdesc_sw128(smem_u32(sQ(cur)), 16, 1024);
+        // the two row blocks' accumulations interleaved (independent chains overlap in the
+        // tensor pipe)
 #pragma unroll
-        for (int rb = 0; rb < 2; ++rb) {
-          const uint32_t aq = smem_u32(sQ(cur)) + rb * RB * 128;
-          const uint32_t idS = idesc_bf16_f32(RB, RB * (rb + 1), false, false);
+        for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(tmem + rb * RB, sdesc_sw128(aq + k * 32, 16, 1024),
-                      sdesc_sw128(smem_u32(sK(cur)) + k * 32, 16, 1024), idS, k > 0 ? 1u : 0u);
-        }
+          for (int rb = 0; rb < 2; ++rb)
+            umma_bf16(tmem + rb * RB, dQ + (uint64_t)((rb * RB * 128 + k * 32) >> 4), dK + (uint64_t)((k * 32) >> 4),
+                      idesc_bf16_f32(RB, RB * (rb + 1), false, false), k > 0 ? 1u : 0u);
         umma_commit(&bars[B_S]);
         // outputs of chunk n-1 out, gate of chunk n in
         if (n > n0) {
@@ -1035,25 +1037,27 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         pph ^= 1;
         if (!mbar_wait(&bars[B_V], (uint32_t)((n - n0) & 1), 54)) break;
         tc_fence_after();
-#pragma unroll
-        for (int rb = 0; rb < 2; ++rb) {
+        const uint64_t dR = sdesc_sw128(smem_u32(sR), 0, 1024), dV = sdesc_sw128(smem_u32(sV), 0, 1024);
+        const uint64_t dKm = sdesc_sw128(smem_u32(sK(cur)), 0, 1024);
+        // three independent accumulations, interleaved: Y_0 (4 + 8 steps), Y_1 (4 + 16), U (16)
+        auto y_step = [&](int rb, int t) {  // step t of Y_rb: Qs_rb bf16(R) first, then P_rb V
           const uint32_t dY = tmem + YCOL + 64 * rb;
-          const uint32_t aq = smem_u32(sQ(cur)) + rb * RB * 128;
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(dY, sdesc_sw128(aq + k * 32, 16, 1024), sdesc_sw128(smem_u32(sR) + k * 2048, 0, 1024), idPV,
-                      k > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < (rb + 1) * RB / 16; ++kk) {
-            const int c = rb * (RB / PW) + (kk >> 1);
-            umma_bf16_ts(dY, tmem + pcol(c) + (kk & 1) * 8, sdesc_sw128(smem_u32(sV) + kk * 16 * 128, 0, 1024),
-                         idPV, 1u);
+          if (t < 4) {
+            umma_bf16(dY, dQ + (uint64_t)((rb * RB * 128 + t * 32) >> 4), dR + (uint64_t)((t * 2048) >> 4), idPV,
+                      t > 0 ? 1u : 0u);
+          } else {
+            const int kk = t - 4, c = rb * (RB / PW) + (kk >> 1);
+            umma_bf16_ts(dY, tmem + pcol(c) + (kk & 1) * 8, dV + (uint64_t)((kk * 16 * 128) >> 4), idPV, 1u);
           }
-        }
+        };
 #pragma unroll
-        for (int kk = 0; kk < CT / 16; ++kk)
-          umma_bf16(tmem + UCOL, sdesc_sw128(smem_u32(sK(cur)) + kk * 2048, 0, 1024),
-                    sdesc_sw128(smem_u32(sV) + kk * 2048, 0, 1024), idU, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < 4 + 2 * RB / 16; ++t) {
+          y_step(1, t);
+          if (t < CT / 16)
+            umma_bf16(tmem + UCOL, dKm + (uint64_t)((t * 2048) >> 4), dV + (uint64_t)((t * 2048) >> 4), idU,
+                      t > 0 ? 1u : 0u);
+          if (t < 4 + RB / 16) y_step(0, t);
+        }
         umma_commit(&bars[B_Y]);
         // every product reading stage cur and V is done: next loads
         if (!mbar_wait(&bars[B_Y], yph, 55)) break;
@@ -1249,7 +1253,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           s1 += o[rb][e];
           s2 += o[rb][e] * o[rb][e];
         }
-        sRed[(rb * RB + my_row) * NWG + wg] = make_float2(s1, s2);
+        sRed[wg * CT + rb * RB + my_row] = make_float2(s1, s2);
       }
       // R <- gC R + U (fp32) -> sR (bf16) for the next chunk
       {
@@ -1280,7 +1284,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         float S1 = 0.f, S2 = 0.f;
 #pragma unroll
         for (int w = 0; w < NWG; ++w) {
-          const float2 v = sRed[row * NWG + w];
+          const float2 v = sRed[w * CT + row];
           S1 += v.x;
           S2 += v.y;
         }
