@@ -896,7 +896,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 //                                                   || issue warp: S(n+1), TMA store of
 //                                                      chunk n's outputs, gate of n+1
 // TMEM (512 columns): S of row block 0 in [0,128), of row block 1 in [128,384), cut in
-// 32-column pieces.  A row-block-0 piece keeps its P (16 packed columns) in its own first
+// 16-column pieces.  A row-block-0 piece keeps its P (8 packed columns) in its own first
 // half; row block 1's P goes to [384,512).  Y and U are written only by the second round of
 // products, which starts after every warp has read its S pieces, so they take row block
 // 1's S columns: Y_rb in [128 + 64 rb, +64), U in [256,320).
@@ -904,8 +904,8 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 // (bounded wait), never through bar.sync inside the loop.
 // ---------------------------------------------------------------------------------
 namespace pipe {
-constexpr int CT = 256, RB = 128, NWG = 4, NCW = NWG * 4, NTC = NCW * 32, NT = NTC + 32, EPW = 16, PW = 32;
-constexpr int NPIECE = 3 * RB / PW;  // 12 pieces of S (4 of row block 0, 8 of row block 1)
+constexpr int CT = 256, RB = 128, NWG = 4, NCW = NWG * 4, NTC = NCW * 32, NT = NTC + 32, EPW = 16, PW = 16;
+constexpr int NPIECE = 3 * RB / PW;  // 24 pieces of S (8 of row block 0, 16 of row block 1)
 constexpr int CPW = NPIECE / NWG;    // per warpgroup
 constexpr int YCOL = RB, UCOL = 2 * RB, P1COL = 3 * RB;
 constexpr int TILE = CT * 128;       // one [CT x 64] bf16 tile
@@ -1046,8 +1046,9 @@ __global__ void __launch_bounds__(pipe::NT, 1)
             umma_bf16(dY, dQ + (uint64_t)((rb * RB * 128 + t * 32) >> 4), dR + (uint64_t)((t * 2048) >> 4), idPV,
                       t > 0 ? 1u : 0u);
           } else {
-            const int kk = t - 4, c = rb * (RB / PW) + (kk >> 1);
-            umma_bf16_ts(dY, tmem + pcol(c) + (kk & 1) * 8, dV + (uint64_t)((kk * 16 * 128) >> 4), idPV, 1u);
+            constexpr int KPP = PW / 16;  // 16-column K steps per piece
+            const int kk = t - 4, c = rb * (RB / PW) + kk / KPP;
+            umma_bf16_ts(dY, tmem + pcol(c) + (kk % KPP) * 8, dV + (uint64_t)((kk * 16 * 128) >> 4), idPV, 1u);
           }
         };
 #pragma unroll
@@ -1196,7 +1197,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           for (int q = 0; q < PW / 2; ++q) pk[q] = 0u;
         } else {
           float sv[PW];
-          tmem_ld32(tL + c * PW, sv);
+          tmem_ldn<PW>(tL + c * PW, sv);
           const int i = ib + my_row;
           const bool full = j0 + PW - 1 <= ib + row_lo;  // no masking for any row of this warp
           const float ci = PERSTEP ? T[i] : 0.f;
@@ -1229,7 +1230,8 @@ __global__ void __launch_bounds__(pipe::NT, 1)
             }
           }
         }
-        tmem_st16_async(tL + pcol(c), pk);
+        if constexpr (PW == 32) tmem_st16_async(tL + pcol(c), pk);
+        else tmem_st8_async(tL + pcol(c), pk);
       }
       tmem_wait_st();
       fence_proxy_async_smem();
