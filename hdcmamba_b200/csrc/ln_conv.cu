@@ -1,23 +1,30 @@
 // Fused LayerNorm + causal depthwise conv1d (width 4) (+ optional SiLU), sm_100a.
 //
 // Same math as the reference _fused_norm_conv_fwd_kernel (hdcmamba/model.py:22-72):
-//   n[t]   = (x[t] - mean_t) * rstd_t * norm_w + norm_b          (fp32, two-pass variance)
+//   n[t]   = (x[t] - mean_t) * rstd_t * norm_w + norm_b          (fp32)
 //   out[t] = n[t-3]*cw0 + n[t-2]*cw1 + n[t-1]*cw2 + n[t]*cw3 + cb
-// with rows t < 0 equal to zeros (LayerNorm(0) = norm_b) or to a supplied halo.
+// with rows t < 0 equal to zeros (LayerNorm(0) = norm_b) or to a supplied halo.  The kernel
+// carries the pre-affine rows z[t] = (x[t] - mean_t) * rstd_t through the conv window and
+// applies the affine once: out = norm_w * sum_k cw_k z[t-3+k] + (norm_b * sum_k cw_k + cb)
+// (the same value in fp32 up to reassociation; a zero row has z = 0).
 //
 // Layout and schedule (HBM-bound; every x byte is read from DRAM once, every out byte
 // written once):
-//   * one CTA walks a contiguous L-segment of one batch row; thread g owns the 16-byte
-//     channel vector g (and g + blockDim when D needs two vectors per thread).
-//   * rows arrive through a ring of NST shared-memory stages filled by one-dimensional
-//     bulk TMA copies (cp.async.bulk, mbarrier completion): a stage is TILE consecutive
-//     rows, which are contiguous in memory.  The copy of tile k+NST is issued as soon
-//     as tile k has been consumed.
-//   * per-row mean / rstd: one warp per row reads the row from shared memory (the whole
-//     row is in the stage), two-pass variance with warp shuffles only.  The statistics of
-//     tile k+1 are computed in the same phase as the conv of tile k (one barrier per tile).
-//   * the conv walks the tile's rows with the three previous normalised rows held in
-//     registers, so each thread's window carries from tile to tile.
+//   * one CTA walks a contiguous L-segment of one batch row with one thread per 16-byte
+//     channel vector (blockDim = D / vector, rounded up to a warp), so thread c owns the
+//     same channels in every row and keeps their conv window in registers.
+//   * rows arrive through a ring of NST shared-memory stages of 8 rows, each filled by one
+//     one-dimensional bulk copy (cp.async.bulk, mbarrier completion): the rows of one batch
+//     are contiguous.  Tile k + NST - 1 is issued as soon as tile k - 1 has been consumed.
+//   * row statistics come from the same threads: each sums its 8 channels of the 8 rows,
+//     shifted by the row's first element (sum d, sum d^2 with d = x - x[row, 0]; one pass),
+//     the 16 sums reduce over the warp in one xor butterfly, over the warps through shared
+//     memory (one barrier per tile), and every warp finalises mean / rstd for itself.  The
+//     summation order of a row does not depend on where the row sits in a tile, so a
+//     segment that starts with a halo reproduces the unsplit run bit for bit.
+//   * the arithmetic runs on packed fp32 pairs (add / mul / fma .f32x2).
+#include <type_traits>
+
 #include "tc.cuh"
 
 namespace hdc {
@@ -25,235 +32,351 @@ namespace hdc {
 struct LnConvParams {
   const void* x; const void* nw; const void* nb; const void* cw; const void* cb;
   const void* halo; void* out; __nv_bfloat16* mean; __nv_bfloat16* rstd;
-  int L, D, seg_len, segs_per_b, total_segs, tile, nst;
+  int L, D, seg_len, segs_per_b, total_segs, nst;
   float eps; int act;
 };
 
+constexpr int LNC_ROWS = 8;  // rows per stage (a multiple of 4: the conv window rotates mod 4)
 
-template <typename T, int VPT, bool SILU>
+// 16-byte vector of T <-> fp32 pairs (NP = elements / 2)
+template <typename T>
+__device__ __forceinline__ void vec_to_f2(const uint4& u, uint64_t* p) {
+  if constexpr (sizeof(T) == 4) {
+    p[0] = f2_make(__uint_as_float(u.x), __uint_as_float(u.y));
+    p[1] = f2_make(__uint_as_float(u.z), __uint_as_float(u.w));
+  } else {
+    p[0] = bf2_to_f2(u.x); p[1] = bf2_to_f2(u.y); p[2] = bf2_to_f2(u.z); p[3] = bf2_to_f2(u.w);
+  }
+}
+template <typename T>
+__device__ __forceinline__ uint4 f2_to_vec(const uint64_t* p) {
+  if constexpr (sizeof(T) == 4) {
+    float a, b, c, d;
+    f2_split(p[0], a, b);
+    f2_split(p[1], c, d);
+    return make_uint4(__float_as_uint(a), __float_as_uint(b), __float_as_uint(c), __float_as_uint(d));
+  } else {
+    return make_uint4(f2_to_bf2(p[0]), f2_to_bf2(p[1]), f2_to_bf2(p[2]), f2_to_bf2(p[3]));
+  }
+}
+
+// 16-byte / one-element shared-memory loads at 32-bit shared addresses
+__device__ __forceinline__ uint4 lds16(uint32_t a) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a) : "memory");
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ float lds_elem(uint32_t a) {
+  if constexpr (sizeof(T) == 4) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+  } else {
+    uint16_t h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a) : "memory");
+    return __uint_as_float((uint32_t)h << 16);
+  }
+}
+// 16-byte global store when `pred` (one predicated instruction, no branch)
+__device__ __forceinline__ void stg16_if(void* p, const uint4& v, bool pred) {
+  asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t"
+               "@q st.global.v4.u32 [%0], {%1,%2,%3,%4};\n\t}"
+               :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"((int)pred) : "memory");
+}
+
+// This thread's shifted sums over the rows of a stage (vector at `va` in row 0, rows
+// `row_bytes` apart; all R rows when FULL, else the first `nv`):
+// v[r] = sum (x - K_r), v[8 + r] = sum (x - K_r)^2, K_r = element 0 of row r (at `ka` + r *
+// row_bytes); zeros for the other rows.
+template <typename T, bool FULL>
+__device__ __forceinline__ void row_partials(uint32_t va, uint32_t ka, int row_bytes, int nv, float* v) {
+  constexpr int NP = Vec<T>::N / 2;
+#pragma unroll
+  for (int r = 0; r < LNC_ROWS; ++r) {
+    v[r] = 0.f;
+    v[LNC_ROWS + r] = 0.f;
+    if (FULL || r < nv) {
+      const float K = lds_elem<T>(ka + r * row_bytes);
+      const uint64_t K2 = f2_make(K, K);
+      uint64_t xp[NP];
+      vec_to_f2<T>(lds16(va + r * row_bytes), xp);
+      uint64_t d = f2_sub(xp[0], K2);
+      uint64_t s1 = d, s2 = f2_mul(d, d);
+#pragma unroll
+      for (int j = 1; j < NP; ++j) {
+        d = f2_sub(xp[j], K2);
+        s1 = f2_add(s1, d);
+        s2 = f2_fma(d, d, s2);
+      }
+      float x0, x1;
+      f2_split(s1, x0, x1);
+      v[r] = x0 + x1;
+      f2_split(s2, x0, x1);
+      v[LNC_ROWS + r] = x0 + x1;
+    }
+  }
+}
+
+// Sum each of the 16 values v[0..15] over the warp.  Each xor level keeps half of the
+// values and sends the other half to the partner, so lanes 2i and 2i + 1 end with the sum
+// of value i (15 exchanges instead of 80).  Every value goes through the same xor tree
+// (16, 8, 4, 2, 1), so its sum does not depend on its index.
+__device__ __forceinline__ float warp_sum16(float* v, int lane) {
+#pragma unroll
+  for (int lvl = 0; lvl < 4; ++lvl) {
+    const int half = 8 >> lvl;
+    const bool up = (lane >> (4 - lvl)) & 1;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float keep = up ? v[half + i] : v[i];
+      const float send = up ? v[i] : v[half + i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16 >> lvl);
+    }
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+template <typename T, bool SILU>
 __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
-  constexpr int VEC = Vec<T>::N;
+  constexpr int VEC = Vec<T>::N, NP = VEC / 2, R = LNC_ROWS;
   extern __shared__ uint8_t smem_raw[];
   const int row_bytes = p.D * (int)sizeof(T);
+  const int stage_bytes = R * row_bytes;
   const int G = p.D / VEC;
-  // smem: [nst][tile] rows | 3 pre rows | stats [nst][tile][2] + pre-row stats [3][2] |
-  // mbarriers [nst + 1]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, NW = blockDim.x >> 5;
+  // smem: ring [nst][R rows] | partial sums [2][16][NW] fp32 | mbarriers [nst + 1]
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-  uint8_t* pre = ring + (size_t)p.nst * p.tile * row_bytes;
-  float* stats = reinterpret_cast<float*>(pre + 3 * row_bytes);
-  float* pstats = stats + 2 * p.nst * p.tile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pstats + 6);
+  float* red = reinterpret_cast<float*>(ring + (size_t)p.nst * stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * 16 * NW);
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int seg = blockIdx.x;
   const int b = seg / p.segs_per_b;
   const int l0 = (seg - b * p.segs_per_b) * p.seg_len;
   const int l1 = min(l0 + p.seg_len, p.L);
-  const int ntiles = (l1 - l0 + p.tile - 1) / p.tile;
+  const int ntiles = (l1 - l0 + R - 1) / R;
   const T* __restrict__ x = static_cast<const T*>(p.x) + (size_t)b * p.L * p.D;
   T* __restrict__ out = static_cast<T*>(p.out) + (size_t)b * p.L * p.D;
   const float invD = 1.0f / (float)p.D;
+  const int c = tid;
+  const bool active = c < G;
 
   if (tid == 0) {
     for (int i = 0; i <= p.nst; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  int issued = 0;  // tiles issued (thread 0)
   auto issue = [&](int k) {
-    const int t0 = l0 + k * p.tile;
-    const int nv = min(p.tile, l1 - t0);
+    const int t0 = l0 + k * R;
+    const int nv = min(R, l1 - t0);
     uint64_t* bar = &bars[k % p.nst];
     mbar_expect_tx(bar, (uint32_t)(nv * row_bytes));
-    bulk_g2s(ring + (size_t)(k % p.nst) * p.tile * row_bytes, x + (size_t)t0 * p.D, (uint32_t)(nv * row_bytes), bar);
+    bulk_g2s(ring + (size_t)(k % p.nst) * stage_bytes, x + (size_t)t0 * p.D, (uint32_t)(nv * row_bytes), bar);
+    issued = k + 1;
   };
-  // the three rows before the segment: x rows, the halo, or zeros
+  // the three rows before the segment (x rows or the halo) go to the last stage, whose first
+  // tile (nst - 1) is issued only once they have been consumed; zero rows need no copy
   const bool pre_zero = (l0 == 0 && p.halo == nullptr);
+  uint8_t* pre = ring + (size_t)(p.nst - 1) * stage_bytes;
   if (tid == 0) {
-    for (int k = 0; k < p.nst && k < ntiles; ++k) issue(k);
     if (!pre_zero) {
       const T* src = l0 > 0 ? x + (size_t)(l0 - 3) * p.D : static_cast<const T*>(p.halo) + (size_t)b * 3 * p.D;
       mbar_expect_tx(&bars[p.nst], (uint32_t)(3 * row_bytes));
       bulk_g2s(pre, src, (uint32_t)(3 * row_bytes), &bars[p.nst]);
     }
-  }
-  if (pre_zero) {
-    for (int i = tid; i < 3 * row_bytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(pre)[i] = make_uint4(0, 0, 0, 0);
-    __syncthreads();  // the zero rows are read by every warp below
-  } else {
-    mbar_wait(&bars[p.nst], 0, 31);
+    for (int k = 0; k < p.nst - 1 && k < ntiles; ++k) issue(k);
   }
 
-  // per-row statistics of `nrows` rows at `rows`, one warp per row -> st[2*r], st[2*r+1]
-  // (two passes over the row in shared memory: mean, then the centred sum of squares)
-  auto row_stats = [&](const uint8_t* rows, int nrows, float* st) {
-    for (int r = warp; r < nrows; r += nwarps) {
-      const uint4* rp = reinterpret_cast<const uint4*>(rows + (size_t)r * row_bytes);
-      float s = 0.f;
-      for (int c = lane; c < G; c += 32) {
-        float f[VEC];
-        unpack16<T>(rp[c], f);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) s += f[e];
-      }
-      const float mean = warp_sum(s) * invD;
-      float q = 0.f;
-      for (int c = lane; c < G; c += 32) {
-        float f[VEC];
-        unpack16<T>(rp[c], f);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const float d = f[e] - mean;
-          q = fmaf(d, d, q);
-        }
-      }
-      const float rstd = rsqrtf(warp_sum(q) * invD + p.eps);
-      if (lane == 0) {
-        st[2 * r] = mean;
-        st[2 * r + 1] = rstd;
-      }
-    }
-  };
-
-  // parameters of this thread's channels
-  float nw[VPT][VEC], nb[VPT][VEC], c0[VPT][VEC], c1[VPT][VEC], c2[VPT][VEC], c3[VPT][VEC], cb[VPT][VEC];
-  bool active[VPT];
-#pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int c = tid + k * blockDim.x;
-    active[k] = c < G;
-    const int cc = active[k] ? c : 0;
-    unpack16<T>(ldg16(static_cast<const T*>(p.nw) + cc * VEC), nw[k]);
-    unpack16<T>(ldg16(static_cast<const T*>(p.nb) + cc * VEC), nb[k]);
-    unpack16<T>(ldg16(static_cast<const T*>(p.cb) + cc * VEC), cb[k]);
+  // parameters of this thread's channels, as fp32 pairs: z-space taps c0..c3, norm_w and
+  // the folded bias norm_b * (c0 + c1 + c2 + c3) + cb
+  uint64_t w2[NP], bb2[NP], c0[NP], c1[NP], c2[NP], c3[NP];
+  {
+    const int cc = active ? c : G - 1;
+    float nw[VEC], nb[VEC], cb[VEC], cw[4][VEC];
+    unpack16<T>(ldg16(static_cast<const T*>(p.nw) + cc * VEC), nw);
+    unpack16<T>(ldg16(static_cast<const T*>(p.nb) + cc * VEC), nb);
+    unpack16<T>(ldg16(static_cast<const T*>(p.cb) + cc * VEC), cb);
     const T* cwp = static_cast<const T*>(p.cw) + (size_t)cc * VEC * 4;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       float f[VEC];
       unpack16<T>(ldg16(cwp + q * VEC), f);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const int flat = q * VEC + e, ch = flat >> 2, tap = flat & 3;
-        if (tap == 0) c0[k][ch] = f[e];
-        else if (tap == 1) c1[k][ch] = f[e];
-        else if (tap == 2) c2[k][ch] = f[e];
-        else c3[k][ch] = f[e];
-      }
+      for (int e = 0; e < VEC; ++e) cw[(q * VEC + e) & 3][(q * VEC + e) >> 2] = f[e];
+    }
+#pragma unroll
+    for (int j = 0; j < NP; ++j) {
+      const int e0 = 2 * j, e1 = 2 * j + 1;
+      w2[j] = f2_make(nw[e0], nw[e1]);
+      bb2[j] = f2_make(fmaf(nb[e0], (cw[0][e0] + cw[1][e0]) + (cw[2][e0] + cw[3][e0]), cb[e0]),
+                       fmaf(nb[e1], (cw[0][e1] + cw[1][e1]) + (cw[2][e1] + cw[3][e1]), cb[e1]));
+      c0[j] = f2_make(cw[0][e0], cw[0][e1]);
+      c1[j] = f2_make(cw[1][e0], cw[1][e1]);
+      c2[j] = f2_make(cw[2][e0], cw[2][e1]);
+      c3[j] = f2_make(cw[3][e0], cw[3][e1]);
     }
   }
 
-  // conv window: W[k][rho & 3] holds the normalised row rho (relative to the segment start,
-  // rows -3..-1 from the preceding rows), so with tiles of a multiple of 4 rows and the row
-  // loop unrolled by 4 every index is a compile-time constant (no register moves)
-  float W[VPT][4][VEC];
-  row_stats(pre, 3, pstats);
-  bool ok = true;
-  if (ntiles > 0) {  // statistics of tile 0 (those of tile k+1 are computed next to tile k's conv)
-    ok = mbar_wait(&bars[0], 0, 32);
-    if (ok) row_stats(ring, min(p.tile, l1 - l0), stats);
-  }
-  __syncthreads();
+  // shared addresses: stage s, row r, this thread's vector at ring_a + s * stage_bytes +
+  // r * row_bytes + cc * 16; a lane past the last vector (D / VEC not a multiple of 32)
+  // reads the last vector and stores nothing
+  const uint32_t ring_a = smem_u32(ring);
+  const int cc = active ? c : G - 1;
+
+  // Reduce this thread's partial sums of a stage (`nv` valid rows) over the CTA through
+  // `rb`, then finalise: lane r < 8 of every warp returns row r's mean, rstd and
+  // -mean * rstd.  Contains one __syncthreads; returns the AND of every thread's `got`.
+  auto tile_stats = [&](uint32_t rows_a, int nv, float* rb, bool got, float& mean, float& rs,
+                        float& mrs) -> bool {
+    float v[16];
+    if (nv == R) row_partials<T, true>(rows_a + cc * 16, rows_a, row_bytes, R, v);
+    else row_partials<T, false>(rows_a + cc * 16, rows_a, row_bytes, nv, v);
+    if (!active) {
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int c = active[k] ? tid + k * blockDim.x : 0;
+      for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    }
+    const float s = warp_sum16(v, lane);
+    if ((lane & 1) == 0) rb[(lane >> 1) * NW + warp] = s;
+    const bool all_ok = __syncthreads_and(got) != 0;
+    float S = 0.f;
+    if (lane < 16) {
+      S = rb[lane * NW];
+      for (int w = 1; w < NW; ++w) S += rb[lane * NW + w];
+    }
+    const float Sq = __shfl_down_sync(0xffffffffu, S, 8);
+    mean = 0.f;
+    rs = 0.f;
+    mrs = 0.f;
+    if (lane < R) {
+      const float K = lds_elem<T>(rows_a + lane * row_bytes);
+      const float m1 = S * invD;
+      const float var = fmaxf(fmaf(-m1, m1, Sq * invD), 0.f);
+      mean = K + m1;
+      rs = rsqrtf(var + p.eps);
+      mrs = -mean * rs;
+    }
+    return all_ok;
+  };
+
+  // conv window: W[rho & 3] holds z of row rho (relative to the segment start; rows -3..-1
+  // are the preceding rows), so with 8-row tiles and the row loop unrolled every index is
+  // a compile-time constant
+  uint64_t W[4][NP];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < NP; ++j) W[i][j] = 0ull;  // z of a zero row is 0
+
+  // z, conv, affine (and SiLU) of the rows of a stage; stores row r at orow + r * D
+  auto conv_rows = [&](auto full, uint32_t va, T* orow, int nv, float rs, float mrs) {
+    constexpr bool FULL = decltype(full)::value;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float rsr = __shfl_sync(0xffffffffu, rs, r), mrsr = __shfl_sync(0xffffffffu, mrs, r);
+      if (FULL || r < nv) {
+        const uint64_t rs2 = f2_make(rsr, rsr), mrs2 = f2_make(mrsr, mrsr);
+        uint64_t xp[NP], o[NP];
+        vec_to_f2<T>(lds16(va + r * row_bytes), xp);
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+          const uint64_t z = f2_fma(xp[j], rs2, mrs2);  // (x - mean) * rstd
+          uint64_t a = f2_mul(z, c3[j]);
+          a = f2_fma(W[(r + 3) & 3][j], c2[j], a);  // row t-1
+          a = f2_fma(W[(r + 2) & 3][j], c1[j], a);  // row t-2
+          a = f2_fma(W[(r + 1) & 3][j], c0[j], a);  // row t-3
+          uint64_t v = f2_fma(a, w2[j], bb2[j]);
+          if (SILU) {  // v * sigmoid(v) = h + h * tanh(h), h = v / 2
+            const uint64_t h = f2_mul(v, f2_make(0.5f, 0.5f));
+            float h0, h1, t0f, t1f;
+            f2_split(h, h0, h1);
+            asm("tanh.approx.f32 %0, %1;" : "=f"(t0f) : "f"(h0));
+            asm("tanh.approx.f32 %0, %1;" : "=f"(t1f) : "f"(h1));
+            v = f2_fma(h, f2_make(t0f, t1f), h);
+          }
+          o[j] = v;
+          W[r & 3][j] = z;
+        }
+        stg16_if(orow + (size_t)r * p.D, f2_to_vec<T>(o), active);
+      }
+    }
+  };
+
+  bool ok = true;
+  if (!pre_zero) {
+    const bool got = mbar_wait(&bars[p.nst], 0, 31);
+    const uint32_t pre_a = ring_a + (uint32_t)((p.nst - 1) * stage_bytes);
+    float mean, rs, mrs;
+    ok = tile_stats(pre_a, 3, red + 16 * NW, got, mean, rs, mrs);
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
-      float f[VEC];
-      unpack16<T>(reinterpret_cast<const uint4*>(pre + (size_t)r * row_bytes)[c], f);
-      // the same expression as the row loop, so a halo row normalises to the same bits
-      const float rs = pstats[2 * r + 1], mrs = -pstats[2 * r] * rs;
+      // the same expression as the row loop, so a halo row gives the same bits
+      const float rsr = __shfl_sync(0xffffffffu, rs, r), mrsr = __shfl_sync(0xffffffffu, mrs, r);
+      const uint64_t rs2 = f2_make(rsr, rsr), mrs2 = f2_make(mrsr, mrsr);
+      uint64_t xp[NP];
+      vec_to_f2<T>(lds16(pre_a + r * row_bytes + cc * 16), xp);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) W[k][r + 1][e] = fmaf(fmaf(f[e], rs, mrs), nw[k][e], nb[k][e]);
+      for (int j = 0; j < NP; ++j) W[r + 1][j] = f2_fma(xp[j], rs2, mrs2);
     }
   }
 
-  for (int k = 0; k < ntiles && ok; ++k) {
+  int k = 0;
+  for (; k < ntiles && ok; ++k) {
     const int st = k % p.nst;
-    const int t0 = l0 + k * p.tile;
-    const int nv = min(p.tile, l1 - t0);
-    const uint8_t* tile = ring + (size_t)st * p.tile * row_bytes;
-    const float* tstat = stats + 2 * st * p.tile;
-    if (k + 1 < ntiles) {  // the next tile's row statistics, in the same phase as this conv
-      const int st1 = (k + 1) % p.nst;
-      if (!mbar_wait(&bars[st1], (uint32_t)(((k + 1) / p.nst) & 1), 32)) { ok = false; break; }
-      row_stats(ring + (size_t)st1 * p.tile * row_bytes, min(p.tile, l1 - (t0 + p.tile)), stats + 2 * st1 * p.tile);
+    const uint32_t tile_a = ring_a + (uint32_t)(st * stage_bytes);
+    const int t0 = l0 + k * R;
+    const int nv = min(R, l1 - t0);
+    const bool got = mbar_wait(&bars[st], (uint32_t)((k / p.nst) & 1), 32);
+    float mean, rs, mrs;
+    if (!tile_stats(tile_a, nv, red + (k & 1) * 16 * NW, got, mean, rs, mrs)) { ok = false; break; }
+    // every thread has finished tile k - 1 (its conv came before the barrier above): refill
+    // its stage with tile k + nst - 1
+    if (tid == 0 && k + p.nst - 1 < ntiles) {
+      fence_proxy_async_smem();  // order the generic reads of that stage before the async refill
+      issue(k + p.nst - 1);
     }
-    if (p.mean && tid < nv) {
-      p.mean[(size_t)b * p.L + t0 + tid] = __float2bfloat16_rn(tstat[2 * tid]);
-      p.rstd[(size_t)b * p.L + t0 + tid] = __float2bfloat16_rn(tstat[2 * tid + 1]);
+    if (p.mean && warp == 0 && lane < nv) {
+      p.mean[(size_t)b * p.L + t0 + lane] = __float2bfloat16_rn(mean);
+      p.rstd[(size_t)b * p.L + t0 + lane] = __float2bfloat16_rn(rs);
     }
-#pragma unroll
-    for (int kk = 0; kk < VPT; ++kk) {
-      if (!active[kk]) continue;
-      const int c = tid + kk * blockDim.x;
-      for (int r4 = 0; r4 < nv; r4 += 4) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int r = r4 + u;
-          if (r < nv) {
-            float f[VEC], o[VEC];
-            unpack16<T>(reinterpret_cast<const uint4*>(tile + (size_t)r * row_bytes)[c], f);
-            const float rs = tstat[2 * r + 1], mrs = -tstat[2 * r] * rs;
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) {
-              const float n0 = fmaf(fmaf(f[e], rs, mrs), nw[kk][e], nb[kk][e]);  // (x - mean) rstd w + b
-              float v = fmaf(W[kk][(u + 1) & 3][e], c0[kk][e],
-                             fmaf(W[kk][(u + 2) & 3][e], c1[kk][e],
-                                  fmaf(W[kk][(u + 3) & 3][e], c2[kk][e], fmaf(n0, c3[kk][e], cb[kk][e]))));
-              if (SILU) v *= fast_sigmoid(v);
-              o[e] = v;
-              W[kk][u][e] = n0;
-            }
-            stg16(out + (size_t)(t0 + r) * p.D + c * VEC, pack16<T>(o));
-          }
-        }
-      }
-    }
-    __syncthreads();
-    if (tid == 0 && k + p.nst < ntiles) {
-      fence_proxy_async_smem();  // order this stage's generic reads before the async refill
-      issue(k + p.nst);
-    }
+    T* orow = out + (size_t)t0 * p.D + cc * VEC;
+    if (nv == R) conv_rows(std::true_type{}, tile_a + cc * 16, orow, R, rs, mrs);
+    else conv_rows(std::false_type{}, tile_a + cc * 16, orow, nv, rs, mrs);
   }
   // after a timed-out wait: let this CTA's own copies in flight land (bounded) before exit
   if (!ok && tid == 0) {
-    for (int k = 0; k < ntiles && k < p.nst; ++k) mbar_wait(&bars[k], 0, 33);
+    if (!pre_zero) mbar_wait(&bars[p.nst], 0, 33);
+    for (int j = k; j < issued; ++j) mbar_wait(&bars[j % p.nst], (uint32_t)((j / p.nst) & 1), 33);
   }
 }
 
-template <typename T, int VPT, bool SILU>
+template <typename T, bool SILU>
 static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   const int G = p.D / Vec<T>::N;
-  int threads = ((G + VPT - 1) / VPT + 31) / 32 * 32;
-  if (threads < 128) threads = 128;
+  const int threads = (G + 31) / 32 * 32;
   const int row_bytes = p.D * (int)sizeof(T);
-  // stages of 32 KB for rows of 4 KB and more (8 rows: one per warp for the statistics),
-  // 16 KB otherwise (shorter segments keep more CTAs busy at narrow rows); a multiple of 4
-  // rows (the conv window unroll)
-  int tile = ((row_bytes >= 4096 ? 32768 : 16384) / row_bytes) & ~3;
-  tile = tile < 4 ? 4 : (tile > 16 ? 16 : tile);
-  int nst = 3;
-  auto smem_of = [&](int t, int s) {
-    return (size_t)128 + (size_t)s * t * row_bytes + 3 * (size_t)row_bytes + (2 * s * t + 6) * 4 + (s + 1) * 8 + 16;
+  auto smem_of = [&](int s) {
+    return (size_t)128 + (size_t)s * LNC_ROWS * row_bytes + 2 * 16 * (threads / 32) * 4 + (s + 1) * 8 + 16;
   };
-  while (smem_of(tile, nst) > 110 * 1024 && nst > 2) --nst;
-  while (smem_of(tile, nst) > 200 * 1024 && tile > 4) tile -= 4;
-  const size_t smem = smem_of(tile, nst);
-  cudaFuncSetAttribute(ln_conv_kernel<T, VPT, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int nst = 3;
+  while (smem_of(nst) > 227 * 1024 && nst > 2) --nst;
+  const size_t smem = smem_of(nst);
+  if (smem > 227 * 1024) return fail(HDC_E_SHAPE, "ln_conv: D=%d needs %zu bytes of shared memory", p.D, smem);
+  cudaFuncSetAttribute(ln_conv_kernel<T, SILU>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   int occ = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ln_conv_kernel<T, VPT, SILU>, threads, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ln_conv_kernel<T, SILU>, threads, smem);
   if (occ < 1) occ = 1;
   const int64_t target = (int64_t)num_sms() * occ;
   int64_t segs_per_b = (target + B - 1) / B;
   int64_t seg_len = (p.L + segs_per_b - 1) / segs_per_b;
-  seg_len = ((seg_len + tile - 1) / tile) * tile;
-  if (seg_len < 8) seg_len = 8;
+  seg_len = ((seg_len + LNC_ROWS - 1) / LNC_ROWS) * LNC_ROWS;
   segs_per_b = (p.L + seg_len - 1) / seg_len;
   p.seg_len = (int)seg_len;
   p.segs_per_b = (int)segs_per_b;
   p.total_segs = (int)(B * segs_per_b);
-  p.tile = tile;
   p.nst = nst;
-  ln_conv_kernel<T, VPT, SILU><<<p.total_segs, threads, smem, stream>>>(p);
+  ln_conv_kernel<T, SILU><<<p.total_segs, threads, smem, stream>>>(p);
   return launch_status("ln_conv_kernel");
 }
 
@@ -261,7 +384,7 @@ template <typename T>
 static int ln_conv_dispatch(LnConvParams p, int64_t B, cudaStream_t stream) {
   const int G = p.D / Vec<T>::N;
   if (G <= 512)
-    return p.act == HDC_ACT_SILU ? launch_ln_conv<T, 1, true>(p, B, stream) : launch_ln_conv<T, 1, false>(p, B, stream);
+    return p.act == HDC_ACT_SILU ? launch_ln_conv<T, true>(p, B, stream) : launch_ln_conv<T, false>(p, B, stream);
   return fail(HDC_E_SHAPE, "ln_conv: D=%d too large", p.D);
 }
 
