@@ -56,6 +56,7 @@ SIGNATURES = {
     "hdc_gate_cat_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
                                  c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_row_layernorm": (c_int, [c_int, c_vp, c_vp, c_i64, c_i64, c_float, c_vp]),
+    "hdc_row_layernorm_affine": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_float, c_vp]),
     "hdc_ln_conv_step": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_float, c_vp]),
     "hdc_ssm_step": (c_int, [c_int, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "hdc_ssm_carry_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),

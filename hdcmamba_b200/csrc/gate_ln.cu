@@ -10,7 +10,8 @@
 // corrected index maps run through the same kernel.
 //
 // row_layernorm_kernel: one warp per row, fp32 statistics (two-pass variance),
-// no affine, result in the activation dtype.
+// result in the activation dtype; optional elementwise affine (weight, bias in the
+// activation dtype, as nn.LayerNorm's (x - mean) * rstd * weight + bias in fp32).
 #include "common.cuh"
 
 namespace hdc {
@@ -71,7 +72,8 @@ __global__ void gate_cat_kernel(GateParams p) {
 }
 
 template <typename T>
-__global__ void row_layernorm_kernel(const T* in, T* out, int64_t rows, int width, float eps) {
+__global__ void row_layernorm_kernel(const T* in, const T* w, const T* bb, T* out, int64_t rows, int width,
+                                     float eps) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
@@ -86,15 +88,19 @@ __global__ void row_layernorm_kernel(const T* in, T* out, int64_t rows, int widt
     q += d * d;
   }
   const float rstd = rsqrtf(warp_sum(q) / (float)width + eps);
-  for (int c = lane; c < width; c += 32) o[c] = from_f<T>((to_f(r[c]) - mean) * rstd);
+  for (int c = lane; c < width; c += 32) {
+    float v = (to_f(r[c]) - mean) * rstd;
+    if (w) v = v * to_f(w[c]) + to_f(bb[c]);
+    o[c] = from_f<T>(v);
+  }
 }
 
 // Vectorized variant: one warp per row, the row held in registers as 16-byte vectors
 // (lane l holds vectors l, l+32, ...), so the row is read once and written once.
 // Needs width % 8 == 0 (bf16), 16-byte aligned rows and width <= 8 * 32 * MAXV.
 template <int MAXV>
-__global__ void row_layernorm_vec_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, int64_t rows, int width,
-                                         float eps) {
+__global__ void row_layernorm_vec_kernel(const __nv_bfloat16* in, const __nv_bfloat16* w, const __nv_bfloat16* bb,
+                                         __nv_bfloat16* out, int64_t rows, int width, float eps) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
   const int lane = threadIdx.x & 31;
@@ -134,6 +140,13 @@ __global__ void row_layernorm_vec_kernel(const __nv_bfloat16* in, __nv_bfloat16*
       unpack16<__nv_bfloat16>(raw[i], f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] = (f[e] - mean) * rstd;
+      if (w) {
+        float fw[8], fb[8];
+        unpack16<__nv_bfloat16>(ldg16(w + (lane + 32 * i) * 8), fw);
+        unpack16<__nv_bfloat16>(ldg16(bb + (lane + 32 * i) * 8), fb);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = f[e] * fw[e] + fb[e];
+      }
       stg16(o + (lane + 32 * i) * 8, pack16<__nv_bfloat16>(f));
     }
   }
@@ -165,25 +178,42 @@ extern "C" int hdc_gate_cat_fwd(int dtype, const void* y_slot, int64_t slot_s_bh
   return launch_status("gate_cat_kernel");
 }
 
-extern "C" int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t rows, int64_t width, float eps,
-                                 hdc_stream_t stream) {
+static int row_layernorm_launch(int dtype, const void* in, const void* w, const void* b, void* out, int64_t rows,
+                                int64_t width, float eps, hdc_stream_t stream) {
   if (dtype != HDC_F32 && dtype != HDC_BF16) return fail(HDC_E_DTYPE, "row_layernorm: dtype %d", dtype);
   if (!in || !out) return fail(HDC_E_NULL, "row_layernorm: null pointer");
   if (rows < 1 || width < 1 || width > (1 << 20)) return fail(HDC_E_SHAPE, "row_layernorm: rows/width");
   const int wpb = 8;
   const unsigned grid = (unsigned)((rows + wpb - 1) / wpb);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_BF16 && width % 8 == 0 && width <= 8 * 32 * 8 && aligned16(in) && aligned16(out)) {
+  if (dtype == HDC_BF16 && width % 8 == 0 && width <= 8 * 32 * 8 && aligned16(in) && aligned16(out) &&
+      (!w || (aligned16(w) && aligned16(b)))) {
     auto i = static_cast<const __nv_bfloat16*>(in);
     auto o = static_cast<__nv_bfloat16*>(out);
-    if (width <= 8 * 32 * 4) row_layernorm_vec_kernel<4><<<grid, 32 * wpb, 0, s>>>(i, o, rows, (int)width, eps);
-    else row_layernorm_vec_kernel<8><<<grid, 32 * wpb, 0, s>>>(i, o, rows, (int)width, eps);
+    auto wp = static_cast<const __nv_bfloat16*>(w);
+    auto bp = static_cast<const __nv_bfloat16*>(b);
+    if (width <= 8 * 32 * 4) row_layernorm_vec_kernel<4><<<grid, 32 * wpb, 0, s>>>(i, wp, bp, o, rows, (int)width, eps);
+    else row_layernorm_vec_kernel<8><<<grid, 32 * wpb, 0, s>>>(i, wp, bp, o, rows, (int)width, eps);
     return launch_status("row_layernorm_vec_kernel");
   }
   if (dtype == HDC_F32)
-    row_layernorm_kernel<float><<<grid, 32 * wpb, 0, s>>>(static_cast<const float*>(in), static_cast<float*>(out), rows, (int)width, eps);
+    row_layernorm_kernel<float><<<grid, 32 * wpb, 0, s>>>(static_cast<const float*>(in), static_cast<const float*>(w),
+                                                         static_cast<const float*>(b), static_cast<float*>(out), rows,
+                                                         (int)width, eps);
   else
-    row_layernorm_kernel<__nv_bfloat16><<<grid, 32 * wpb, 0, s>>>(static_cast<const __nv_bfloat16*>(in),
-                                                                 static_cast<__nv_bfloat16*>(out), rows, (int)width, eps);
+    row_layernorm_kernel<__nv_bfloat16><<<grid, 32 * wpb, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(in), static_cast<const __nv_bfloat16*>(w),
+        static_cast<const __nv_bfloat16*>(b), static_cast<__nv_bfloat16*>(out), rows, (int)width, eps);
   return launch_status("row_layernorm_kernel");
+}
+
+extern "C" int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t rows, int64_t width, float eps,
+                                 hdc_stream_t stream) {
+  return row_layernorm_launch(dtype, in, nullptr, nullptr, out, rows, width, eps, stream);
+}
+
+extern "C" int hdc_row_layernorm_affine(int dtype, const void* in, const void* weight, const void* bias, void* out,
+                                        int64_t rows, int64_t width, float eps, hdc_stream_t stream) {
+  if (!weight || !bias) return fail(HDC_E_NULL, "row_layernorm_affine: null weight / bias");
+  return row_layernorm_launch(dtype, in, weight, bias, out, rows, width, eps, stream);
 }

@@ -17,7 +17,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .model import HdcMamba9v3Block, HdcMamba9v3Model
+from .model import HdcMamba9v3Block, HdcMamba9v3Model, final_layer_norm
 
 
 class HdcMambaLM(nn.Module):
@@ -46,7 +46,7 @@ class HdcMambaLM(nn.Module):
         return h
 
     def forward(self, ids):
-        return F.linear(self.norm(self.hidden(ids)), self.embedding.weight)
+        return F.linear(final_layer_norm(self.norm, self.hidden(ids)), self.embedding.weight)
 
 
 @dataclass(frozen=True)

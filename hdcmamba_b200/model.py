@@ -67,6 +67,16 @@ class FusedNormConv1dFunction(torch.autograd.Function):
         return dx, dnw.to(nw.dtype), dnb.to(nw.dtype), dcw.reshape(cw.shape).to(cw.dtype), dcb.to(nw.dtype), None
 
 
+def final_layer_norm(norm, x):
+    """``norm(x)`` for an ``nn.LayerNorm`` over the last dim: through
+    hdc_row_layernorm_affine when no autograd graph is needed, else the module itself
+    (gradients for its weight and bias)."""
+    if torch.is_grad_enabled() and (x.requires_grad or norm.weight.requires_grad):
+        return norm(x)
+    _require_cuda(x)
+    return ops.layer_norm(x.contiguous(), norm.weight, norm.bias, norm.eps)
+
+
 def fused_norm_conv1d_trainable(x, norm_layer, conv_layer):
     """hdcmamba/model.py:168-172."""
     return FusedNormConv1dFunction.apply(
@@ -204,4 +214,4 @@ class HdcMamba9v3Model(nn.Module):
     def forward(self, x):
         for layer in self.layers:
             x, _ = layer(x)
-        return self.norm_final(x)
+        return final_layer_norm(self.norm_final, x)

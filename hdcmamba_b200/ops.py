@@ -379,6 +379,22 @@ def row_layernorm(x, eps=1e-5, out=None):
     return out
 
 
+def layer_norm(x, weight, bias, eps=1e-5, out=None):
+    """nn.LayerNorm over the last dim with its elementwise affine: fp32 statistics and
+    affine, result in x.dtype (hdc_row_layernorm_affine; replaces the final norms,
+    hdcmamba/model.py:400, 404 and train.py:121, 135)."""
+    _cuda(x, weight, bias, out)
+    if not x.is_contiguous():
+        raise ValueError("layer_norm needs a contiguous input")
+    if out is None:
+        out = torch.empty_like(x)
+    width = x.shape[-1]
+    w, b = weight.to(x.dtype).contiguous(), bias.to(x.dtype).contiguous()
+    _lib.call("hdc_row_layernorm_affine", _code(x), _p(x), _p(w), _p(b), _p(out), x.numel() // width, width,
+              float(eps), _stream(x))
+    return out
+
+
 # ------------------------------------------------------------------ single-token decode
 def ln_conv_step(x, norm_w, norm_b, conv_w, conv_b, window, eps=1e-5, out=None):
     """LN + conv of one new row per sequence, x [B, D]; ``window`` fp32 [B, 3, D] (the

@@ -274,6 +274,16 @@ int hdc_row_layernorm(int dtype, const void* in, void* out, int64_t rows, int64_
                       float eps, hdc_stream_t stream);
 
 /*
+ * Row LayerNorm with the elementwise affine of nn.LayerNorm: (x - mean) * rstd * weight +
+ * bias in fp32, result in dtype (in place allowed).  Replaces HdcMamba9v3Model.norm_final
+ * (hdcmamba/model.py:400, 404) and the LM wrapper's final LayerNorm (train.py:121, 135).
+ *   in/out : [rows, width] contiguous;  weight, bias : [width] in dtype.
+ */
+int hdc_row_layernorm_affine(int dtype, const void* in, const void* weight, const void* bias,
+                             void* out, int64_t rows, int64_t width, float eps,
+                             hdc_stream_t stream);
+
+/*
  * Recurrent single-token decode (no reference counterpart: the reference's generation
  * re-runs the whole prefix).  The state continues the chunked prefill one row at a time
  * with the prefill's formulas and rounding points (bf16 activations: the tcgen05 path's;

@@ -199,3 +199,18 @@ def test_row_layernorm(rows, width, dtype):
     xi = x.to(DEV)
     ops.row_layernorm(xi, out=xi)  # in place, as the Block runs it
     assert torch.equal(xi, y)
+
+
+@pytest.mark.parametrize("rows,width,dtype", [(1000, 768, torch.bfloat16), (77, 320, torch.float32),
+                                              (300, 100, torch.bfloat16), (64, 2048, torch.bfloat16)])
+def test_layer_norm_affine_matches_nn_layernorm(rows, width, dtype):
+    """The final norms (HdcMamba9v3Model.norm_final, the LM wrapper's norm) against
+    nn.LayerNorm on the same device, dtype and parameters."""
+    x = (3 * torch.randn(rows, width, generator=gen(41)) + 1).to(dtype).to(DEV)
+    ln = torch.nn.LayerNorm(width).to(DEV).to(dtype)
+    with torch.no_grad():
+        ln.weight.copy_(1 + 0.1 * torch.randn(width, generator=gen(42)))
+        ln.bias.copy_(0.1 * torch.randn(width, generator=gen(43)))
+        ref = ln(x)
+    y = ops.layer_norm(x, ln.weight, ln.bias, ln.eps)
+    assert rel(y, ref) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
