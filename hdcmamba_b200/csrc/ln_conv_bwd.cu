@@ -19,6 +19,9 @@
 //   * parameter gradients accumulate in registers per thread and are written per CTA to a
 //     workspace, which a second kernel sums over the CTAs in a fixed order (deterministic;
 //     the reference adds with fp32 atomics).
+#include <algorithm>
+#include <type_traits>
+
 #include "tc.cuh"
 
 namespace hdc {
@@ -188,11 +191,70 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_kernel(LnConvBwdParams p) {
 
 // The same computation with the rows staged through shared memory: tile k of a CTA holds the
 // x rows of its steps [l0 + k TR, +TR) and the grad rows three ahead, brought in by bulk TMA
-// copies (rows are contiguous) into a two-stage ring; a stage is refilled after the CTA
-// barrier that ends the last 4-row group of its tile.  Rows of a multiple of 16 bytes.
+// copies (rows are contiguous) into a ring of NST stages; a stage is refilled after the CTA
+// barrier of the first 4-row group of the next tile.  Rows of a multiple of 16 bytes.
+// The group's eight row sums (sum dn nw and sum dn nw xhat of 4 rows) reduce over the warp in
+// one xor butterfly, over the warps through shared memory (one barrier per group); lane i of
+// every warp fetches row i's mean / rstd once per tile (the rows take them by shuffle), and
+// the arithmetic runs on packed fp32 pairs.
+
+// Sum each of v[0..7] over the warp: lanes 4i..4i+3 end with the sum of value i (each xor
+// level keeps half of the values and sends the other half to the partner).
+__device__ __forceinline__ float warp_sum8(float* v, int lane) {
+#pragma unroll
+  for (int lvl = 0; lvl < 3; ++lvl) {
+    const int half = 4 >> lvl;
+    const bool up = (lane >> (4 - lvl)) & 1;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float keep = up ? v[half + i] : v[i];
+      const float send = up ? v[i] : v[half + i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16 >> lvl);
+    }
+  }
+  const float s = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 2);
+  return s + __shfl_xor_sync(0xffffffffu, s, 1);
+}
+
+// four channels at a 32-bit shared address / in global memory <-> two fp32 pairs
 template <typename T>
+__device__ __forceinline__ void lds4(uint32_t a, uint64_t* f) {
+  if constexpr (sizeof(T) == 4) {
+    uint32_t x, y, z, w;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(x), "=r"(y), "=r"(z), "=r"(w) : "r"(a) : "memory");
+    f[0] = f2_make(__uint_as_float(x), __uint_as_float(y));
+    f[1] = f2_make(__uint_as_float(z), __uint_as_float(w));
+  } else {
+    uint32_t x, y;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(x), "=r"(y) : "r"(a) : "memory");
+    f[0] = bf2_to_f2(x);
+    f[1] = bf2_to_f2(y);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void ldg4(const T* p, uint64_t* f) {
+  float v[4];
+  ld4<T>(p, v);
+  f[0] = f2_make(v[0], v[1]);
+  f[1] = f2_make(v[2], v[3]);
+}
+template <typename T>
+__device__ __forceinline__ void stg4_if(T* p, const uint64_t* f, bool pred) {
+  if constexpr (sizeof(T) == 4) {
+    float a, b, c, d;
+    f2_split(f[0], a, b);
+    f2_split(f[1], c, d);
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %5, 0;\n\t@q st.global.v4.f32 [%0], {%1,%2,%3,%4};\n\t}"
+                 :: "l"(p), "f"(a), "f"(b), "f"(c), "f"(d), "r"((int)pred) : "memory");
+  } else {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t@q st.global.v2.u32 [%0], {%1,%2};\n\t}"
+                 :: "l"(p), "r"(f2_to_bf2(f[0])), "r"(f2_to_bf2(f[1])), "r"((int)pred) : "memory");
+  }
+}
+
+template <typename T, int NST>
 __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams p, int TR) {
-  __shared__ float red[2][4][2][16];
+  __shared__ __align__(16) float red[2][8][16];  // [half][value: 4 x sum dn nw, 4 x sum dn nw xhat][warp]
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
@@ -202,15 +264,14 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams
   const int l1 = min(l0 + p.seg_len, p.L);
   const int c0 = tid * 4;
   const bool act = c0 < p.D;
-  const int cc = act ? c0 : 0;
+  const int cc = act ? c0 : p.D - 4;  // a thread past the row reads the last channels, stores nothing
   const size_t rowD = (size_t)p.D;
   const uint32_t row_bytes = (uint32_t)(p.D * sizeof(T));
   const uint32_t tile_bytes = (uint32_t)TR * row_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + 4 * (size_t)tile_bytes);  // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + 2 * (size_t)NST * tile_bytes);  // [NST]
+  const uint32_t ring_a = smem_u32(ring);
   const T* gob = static_cast<const T*>(p.go) + (size_t)b * p.L * rowD;
   const T* xb = static_cast<const T*>(p.x) + (size_t)b * p.L * rowD;
-  const T* go = gob + cc;
-  const T* x = xb + cc;
   T* dx = static_cast<T*>(p.dx) + (size_t)b * p.L * rowD + cc;
   const __nv_bfloat16* mean = p.mean + (size_t)b * p.L;
   const __nv_bfloat16* rstd = p.rstd + (size_t)b * p.L;
@@ -218,13 +279,13 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams
   const int ntiles = (l1 - l0 + TR - 1) / TR;
 
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    for (int i = 0; i < NST; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
+  int issued = 0;  // tiles issued (thread 0)
   auto issue = [&](int k) {  // tile k: x rows t0.., grad rows t0+3.. (clipped to the sequence)
-    const int st = k & 1;
+    const int st = k % NST;
     const int t0 = l0 + k * TR;
     const int nx = min(TR, l1 - t0);
     const int ng = max(0, min(TR, p.L - (t0 + 3)));
@@ -232,137 +293,172 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams
     mbar_expect_tx(&bars[st], (uint32_t)(nx + ng) * row_bytes);
     bulk_g2s(sx, xb + (size_t)t0 * rowD, (uint32_t)nx * row_bytes, &bars[st]);
     if (ng > 0) bulk_g2s(sx + tile_bytes, gob + (size_t)(t0 + 3) * rowD, (uint32_t)ng * row_bytes, &bars[st]);
+    issued = k + 1;
   };
-  if (tid == 0) {
-    if (ntiles > 0) issue(0);
-    if (ntiles > 1) issue(1);
+  if (tid == 0)
+    for (int k = 0; k < NST && k < ntiles; ++k) issue(k);  // stage of tile k - 1 refilled at tile k
+
+  // parameters as fp32 pairs: nw, and the taps c0..c3 of the channels (cw[e][k] of channel e)
+  uint64_t nw2[2], c_0[2], c_1[2], c_2[2], c_3[2];
+  {
+    float nw[4], cw[4][4];
+    ld4<T>(static_cast<const T*>(p.nw) + cc, nw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ld4<T>(static_cast<const T*>(p.cw) + (size_t)(cc + e) * 4, cw[e]);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      nw2[j] = f2_make(nw[2 * j], nw[2 * j + 1]);
+      c_0[j] = f2_make(cw[2 * j][0], cw[2 * j + 1][0]);
+      c_1[j] = f2_make(cw[2 * j][1], cw[2 * j + 1][1]);
+      c_2[j] = f2_make(cw[2 * j][2], cw[2 * j + 1][2]);
+      c_3[j] = f2_make(cw[2 * j][3], cw[2 * j + 1][3]);
+    }
+  }
+  // rings: G[rho & 3] = go row l0 + rho, X[rho & 3] = xhat * nw of row l0 + rho (rows before
+  // the sequence: zero)
+  uint64_t G[4][2], X[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) G[i][0] = G[i][1] = X[i][0] = X[i][1] = 0ull;
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    if (l0 + r < p.L) ldg4<T>(gob + (size_t)(l0 + r) * rowD + cc, G[r]);
+    const int t = l0 - 3 + r;
+    if (t >= 0) {
+      uint64_t v[2];
+      ldg4<T>(xb + (size_t)t * rowD + cc, v);
+      const float m = __bfloat162float(mean[t]), rr = __bfloat162float(rstd[t]);
+      const uint64_t r2 = f2_make(rr, rr), mr2 = f2_make(-m * rr, -m * rr);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) X[r + 1][j] = f2_mul(f2_fma(v[j], r2, mr2), nw2[j]);
+    }
   }
 
-  float nw[4], cw[4][4];
-  ld4<T>(static_cast<const T*>(p.nw) + cc, nw);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) ld4<T>(static_cast<const T*>(p.cw) + (size_t)(cc + e) * 4, cw[e]);
-  auto load_go = [&](int t, float* f) {
-    if (act && t < p.L) ld4<T>(go + (size_t)t * rowD, f);
-    else f[0] = f[1] = f[2] = f[3] = 0.f;
-  };
-  auto xhat_nw = [&](int t, float* f) {
-    if (act && t >= 0) {
-      float v[4];
-      ld4<T>(x + (size_t)t * rowD, v);
-      const float m = __bfloat162float(mean[t]), r = __bfloat162float(rstd[t]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) f[e] = (v[e] - m) * r * nw[e];
-    } else {
-      f[0] = f[1] = f[2] = f[3] = 0.f;
-    }
-  };
-  float G[4][4], X[4][4];
-  load_go(l0, G[0]);
-  load_go(l0 + 1, G[1]);
-  load_go(l0 + 2, G[2]);
-  xhat_nw(l0 - 3, X[1]);
-  xhat_nw(l0 - 2, X[2]);
-  xhat_nw(l0 - 1, X[3]);
-
-  float a_nw[4] = {0.f, 0.f, 0.f, 0.f}, a_nb[4] = {0.f, 0.f, 0.f, 0.f}, a_cb[4] = {0.f, 0.f, 0.f, 0.f};
-  float a_cw[4][4] = {};
+  uint64_t a_nw[2] = {0ull, 0ull}, a_nb[2] = {0ull, 0ull}, a_cb[2] = {0ull, 0ull};
+  uint64_t a_cw[4][2] = {};  // [k][pair]
   int half = 0;
-  uint32_t ph0 = 0, ph1 = 0;
   bool ok = true;
-  for (int r4 = 0; r4 < l1 - l0 && ok; r4 += 4) {
-    const int k = r4 / TR, rk = r4 - k * TR, st = k & 1;
-    if (rk == 0) {  // first group of tile k: its rows have landed
-      if (!mbar_wait_warp(&bars[st], st ? ph1 : ph0, 34)) { ok = false; break; }
-      if (st) ph1 ^= 1; else ph0 ^= 1;
+  int k = 0;
+  for (; k < ntiles && ok; ++k) {
+    const int st = k % NST;
+    const int t0 = l0 + k * TR;
+    const int nrows = min(TR, l1 - t0);
+    // row statistics of the tile: lane i holds row i's (TR <= 32)
+    float mt = 0.f, rt = 0.f;
+    if (lane < nrows) {
+      mt = __bfloat162float(mean[t0 + lane]);
+      rt = __bfloat162float(rstd[t0 + lane]);
     }
-    const uint8_t* sx = ring + (size_t)st * 2 * tile_bytes;
-    float xh[4][4], dxh[4][4], s1[4], s2[4], rs[4];
+    // a timed-out wait ends the loop for every warp together at the group barrier below
+    const bool got = mbar_wait_warp(&bars[st], (uint32_t)((k / NST) & 1), 34);
+    const uint32_t sx = ring_a + (uint32_t)st * 2 * tile_bytes + (uint32_t)cc * sizeof(T);
+    const uint32_t sg = sx + tile_bytes;
+    for (int rk = 0; rk < nrows; rk += 4) {
+      const int tg = t0 + rk;  // first row of the group
+      uint64_t dxh[4][2];
+      float v[8];
+      // phase 1: dn, xhat, the row sums' partials, the parameter gradients
+      auto row = [&](auto full, int u) {
+        constexpr bool FULL = decltype(full)::value;
+        const int t = tg + u, r = rk + u;
+        const float m = __shfl_sync(0xffffffffu, mt, r & 31), rr = __shfl_sync(0xffffffffu, rt, r & 31);
+        v[u] = v[4 + u] = 0.f;
+        if (!FULL && t >= l1) return;
+        if (FULL || t + 3 < p.L) lds4<T>(sg + (uint32_t)r * row_bytes, G[(u + 3) & 3]);
+        else G[(u + 3) & 3][0] = G[(u + 3) & 3][1] = 0ull;
+        uint64_t xv[2];
+        lds4<T>(sx + (uint32_t)r * row_bytes, xv);
+        const uint64_t r2 = f2_make(rr, rr), mr2 = f2_make(-m * rr, -m * rr);
+        uint64_t s1 = 0ull, s2 = 0ull;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = l0 + r4 + u;
-      s1[u] = s2[u] = 0.f;
-      rs[u] = 0.f;
-      if (t < l1) {
-        const int r = rk + u;
-        if (act && t + 3 < p.L) ld4<T>(reinterpret_cast<const T*>(sx + tile_bytes + (size_t)r * row_bytes) + cc,
-                                       G[(u + 3) & 3]);
-        else G[(u + 3) & 3][0] = G[(u + 3) & 3][1] = G[(u + 3) & 3][2] = G[(u + 3) & 3][3] = 0.f;
-        float v[4];
-        const float m = __bfloat162float(mean[t]), rr = __bfloat162float(rstd[t]);
-        rs[u] = rr;
-        if (act) ld4<T>(reinterpret_cast<const T*>(sx + (size_t)r * row_bytes) + cc, v);
-        else v[0] = v[1] = v[2] = v[3] = 0.f;
+        for (int j = 0; j < 2; ++j) {
+          const uint64_t g0 = G[u][j];
+          const uint64_t dn = f2_fma(G[(u + 3) & 3][j], c_0[j],
+                                     f2_fma(G[(u + 2) & 3][j], c_1[j], f2_fma(G[(u + 1) & 3][j], c_2[j], f2_mul(g0, c_3[j]))));
+          const uint64_t xhat = f2_fma(xv[j], r2, mr2);  // (x - mean) rstd
+          const uint64_t xw = f2_mul(xhat, nw2[j]);
+          const uint64_t d = f2_mul(dn, nw2[j]);
+          dxh[u][j] = d;
+          s1 = j ? f2_add(s1, d) : d;
+          s2 = j ? f2_fma(d, xhat, s2) : f2_mul(d, xhat);
+          a_nw[j] = f2_fma(dn, xhat, a_nw[j]);
+          a_nb[j] = f2_add(a_nb[j], dn);
+          a_cb[j] = f2_add(a_cb[j], g0);
+          a_cw[3][j] = f2_fma(g0, xw, a_cw[3][j]);
+          a_cw[2][j] = f2_fma(g0, X[(u + 3) & 3][j], a_cw[2][j]);
+          a_cw[1][j] = f2_fma(g0, X[(u + 2) & 3][j], a_cw[1][j]);
+          a_cw[0][j] = f2_fma(g0, X[(u + 1) & 3][j], a_cw[0][j]);
+          X[u][j] = xw;
+        }
+        float lo, hi;
+        f2_split(s1, lo, hi);
+        v[u] = lo + hi;
+        f2_split(s2, lo, hi);
+        v[4 + u] = lo + hi;
+      };
+      const bool full = tg + 4 <= l1 && tg + 7 < p.L;
+      if (full) {
+        row(std::true_type{}, 0); row(std::true_type{}, 1); row(std::true_type{}, 2); row(std::true_type{}, 3);
+      } else {
+        row(std::false_type{}, 0); row(std::false_type{}, 1); row(std::false_type{}, 2); row(std::false_type{}, 3);
+      }
+      if (!act) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float g0 = G[u][e];
-          const float dn = g0 * cw[e][3] + G[(u + 1) & 3][e] * cw[e][2] + G[(u + 2) & 3][e] * cw[e][1] +
-                           G[(u + 3) & 3][e] * cw[e][0];
-          const float xhat = act ? (v[e] - m) * rr : 0.f;
-          const float xw = xhat * nw[e];
-          xh[u][e] = xhat;
-          dxh[u][e] = dn * nw[e];
-          s1[u] += dxh[u][e];
-          s2[u] += dxh[u][e] * xhat;
-          a_nw[e] += dn * xhat;
-          a_nb[e] += dn;
-          a_cb[e] += g0;
-          a_cw[3][e] += g0 * xw;
-          a_cw[2][e] += g0 * X[(u + 3) & 3][e];
-          a_cw[1][e] += g0 * X[(u + 2) & 3][e];
-          a_cw[0][e] += g0 * X[(u + 1) & 3][e];
-          X[u][e] = xw;
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+      }
+      const float s = warp_sum8(v, lane);
+      if ((lane & 3) == 0) red[half][lane >> 2][warp] = s;
+      if (!__syncthreads_and(got)) { ok = false; break; }
+      // every thread has finished tile k - 1 (its last group's phase 2 came before the barrier
+      // above): refill that stage
+      if (tid == 0 && rk == 0 && k >= 1 && k - 1 + NST < ntiles) {
+        fence_proxy_async_smem();
+        issue(k - 1 + NST);
+      }
+      // phase 2: every warp finishes the sums itself (lane i < 8: value i over the warps);
+      // xhat is recomputed from the staged row
+      float S = 0.f;
+      if (lane < 8) {
+        S = red[half][lane][0];
+        for (int w = 1; w < nwarps; ++w) S += red[half][lane][w];
+        S *= invD;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float S1 = __shfl_sync(0xffffffffu, S, u), S2 = __shfl_sync(0xffffffffu, S, 4 + u);
+        const float m = __shfl_sync(0xffffffffu, mt, (rk + u) & 31), rr = __shfl_sync(0xffffffffu, rt, (rk + u) & 31);
+        const int t = tg + u;
+        if (t < l1) {
+          const uint64_t r2 = f2_make(rr, rr), mr2 = f2_make(-m * rr, -m * rr);
+          const uint64_t S1_2 = f2_make(S1, S1), mS2_2 = f2_make(-S2, -S2);
+          uint64_t xv[2], o[2];
+          lds4<T>(sx + (uint32_t)(rk + u) * row_bytes, xv);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            o[j] = f2_mul(r2, f2_fma(f2_fma(xv[j], r2, mr2), mS2_2, f2_sub(dxh[u][j], S1_2)));
+          stg4_if<T>(dx + (size_t)t * rowD, o, act);
         }
       }
+      half ^= 1;
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float a = warp_sum(s1[u]), c = warp_sum(s2[u]);
-      if (lane == 0) {
-        red[half][u][0][warp] = a;
-        red[half][u][1][warp] = c;
-      }
-    }
-    __syncthreads();
-    // tile k fully read by every thread after its last group: refill its stage
-    if (tid == 0 && (rk + 4 >= TR || r4 + 4 >= l1 - l0) && k + 2 < ntiles) {
-      fence_proxy_async_smem();
-      issue(k + 2);
-    }
-    // every warp reduces the warps' partials itself: one shared load per lane, then shuffles
-    float S1v[4], S2v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      S1v[u] = warp_sum(lane < nwarps ? red[half][u][0][lane] : 0.f) * invD;
-      S2v[u] = warp_sum(lane < nwarps ? red[half][u][1][lane] : 0.f) * invD;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = l0 + r4 + u;
-      if (t >= l1 || !act) continue;
-      const float S1 = S1v[u], S2 = S2v[u];
-      float o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[e] = rs[u] * (dxh[u][e] - S1 - xh[u][e] * S2);
-      st4<T>(dx + (size_t)t * rowD, o);
-    }
-    half ^= 1;
+    if (!ok) break;  // keep k at the tile whose copy timed out (waited for below)
   }
   if (act) {
     float* part = p.part + (size_t)seg * 7 * rowD + c0;
+    auto put = [&](int row, const uint64_t* f) {
+      float a, b2, c, d;
+      f2_split(f[0], a, b2);
+      f2_split(f[1], c, d);
+      *reinterpret_cast<float4*>(part + (size_t)row * rowD) = make_float4(a, b2, c, d);
+    };
+    put(0, a_nw);
+    put(1, a_nb);
+    put(2, a_cb);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      part[e] = a_nw[e];
-      part[rowD + e] = a_nb[e];
-      part[2 * rowD + e] = a_cb[e];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) part[(3 + k) * rowD + e] = a_cw[k][e];
-    }
+    for (int kk = 0; kk < 4; ++kk) put(3 + kk, a_cw[kk]);
   }
   // after a timed-out wait: let this CTA's own copies land (bounded) before exit
   if (!ok && tid == 0) {
-    mbar_wait(&bars[0], ph0, 35);
-    mbar_wait(&bars[1], ph1, 35);
+    for (int j = k; j < issued; ++j) mbar_wait(&bars[j % NST], (uint32_t)((j / NST) & 1), 35);
   }
 }
 
@@ -384,8 +480,10 @@ __global__ void ln_conv_bwd_reduce_kernel(const float* part, int nseg, int D, T*
 
 constexpr int kBwdMaxD = 2048;  // 512 threads x 4 channels
 
-static void bwd_plan(int64_t B, int64_t L, int* seg_len, int* segs_per_b) {
-  const int64_t target = (int64_t)num_sms() * 4;
+// one wave: a 512-thread CTA (D = 2048) per SM, more CTAs per SM for narrower rows
+static void bwd_plan(int64_t B, int64_t L, int64_t D, int* seg_len, int* segs_per_b) {
+  const int64_t threads = std::max<int64_t>(32, (D / 4 + 31) / 32 * 32);
+  const int64_t target = (int64_t)num_sms() * std::max<int64_t>(1, std::min<int64_t>(4, 512 / threads));
   int64_t spb = (target + B - 1) / B;
   int64_t len = (L + spb - 1) / spb;
   len = (len + 3) / 4 * 4;
@@ -401,7 +499,7 @@ using namespace hdc;
 extern "C" size_t hdc_ln_conv_bwd_workspace_bytes(int64_t B, int64_t L, int64_t D) {
   if (B < 1 || L < 1 || D < 1) return 0;
   int len, spb;
-  bwd_plan(B, L, &len, &spb);
+  bwd_plan(B, L, D, &len, &spb);
   return (size_t)B * spb * 7 * D * sizeof(float);
 }
 
@@ -425,7 +523,7 @@ extern "C" int hdc_ln_conv_bwd(int dtype, const void* grad_out, const void* x, c
   p.go = grad_out; p.x = x; p.mean = static_cast<const __nv_bfloat16*>(mean);
   p.rstd = static_cast<const __nv_bfloat16*>(rstd); p.nw = norm_w; p.cw = conv_w; p.dx = dx;
   p.part = static_cast<float*>(workspace); p.L = (int)L; p.D = (int)D;
-  bwd_plan(B, L, &p.seg_len, &p.segs_per_b);
+  bwd_plan(B, L, D, &p.seg_len, &p.segs_per_b);
   const int nseg = (int)(B * p.segs_per_b);
   int threads = ((int)(D / 4) + 31) / 32 * 32;
   if (threads < 64) threads = 64;
@@ -434,29 +532,34 @@ extern "C" int hdc_ln_conv_bwd(int dtype, const void* grad_out, const void* x, c
   const size_t es = dtype == HDC_F32 ? 4 : 2;
   const size_t row_bytes = (size_t)D * es;
   const bool staged = row_bytes % 16 == 0;
-  int TR = 8;
-  while (TR > 4 && 4 * (size_t)TR * row_bytes > 160 * 1024) TR -= 4;
-  const size_t smem = 128 + 4 * (size_t)TR * row_bytes + 16;
-  if (dtype == HDC_F32) {
+  // 8-row tiles and 3 stages where they fit, else 4-row tiles, else 2 stages
+  int TR = 8, nst = 3;
+  auto smem_of = [&](int tr, int ns) { return 128 + 2 * (size_t)ns * tr * row_bytes + ns * 8 + 16; };
+  if (smem_of(TR, nst) > 200 * 1024) TR = 4;
+  if (smem_of(TR, nst) > 200 * 1024) nst = 2;
+  const size_t smem = smem_of(TR, nst);
+  auto launch_main = [&](auto tag) -> int {
+    using T = decltype(tag);
     if (staged) {
-      cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      ln_conv_bwd_staged_kernel<float><<<nseg, threads, smem, s>>>(p, TR);
+      if (nst == 3) {
+        cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<T, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ln_conv_bwd_staged_kernel<T, 3><<<nseg, threads, smem, s>>>(p, TR);
+      } else {
+        cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ln_conv_bwd_staged_kernel<T, 2><<<nseg, threads, smem, s>>>(p, TR);
+      }
     } else {
-      ln_conv_bwd_kernel<float><<<nseg, threads, 0, s>>>(p);
+      ln_conv_bwd_kernel<T><<<nseg, threads, 0, s>>>(p);
     }
-    if (int e = launch_status("ln_conv_bwd_kernel")) return e;
+    return launch_status("ln_conv_bwd_kernel");
+  };
+  if (dtype == HDC_F32) {
+    if (int e = launch_main(float{})) return e;
     ln_conv_bwd_reduce_kernel<float><<<rgrid, 256, 0, s>>>(p.part, nseg, (int)D, static_cast<float*>(dnorm_w),
                                                            static_cast<float*>(dnorm_b), static_cast<float*>(dconv_w),
                                                            static_cast<float*>(dconv_b));
   } else {
-    if (staged) {
-      cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      ln_conv_bwd_staged_kernel<__nv_bfloat16><<<nseg, threads, smem, s>>>(p, TR);
-    } else {
-      ln_conv_bwd_kernel<__nv_bfloat16><<<nseg, threads, 0, s>>>(p);
-    }
-    if (int e = launch_status("ln_conv_bwd_kernel")) return e;
+    if (int e = launch_main(__nv_bfloat16{})) return e;
     ln_conv_bwd_reduce_kernel<__nv_bfloat16><<<rgrid, 256, 0, s>>>(
         p.part, nseg, (int)D, static_cast<__nv_bfloat16*>(dnorm_w), static_cast<__nv_bfloat16*>(dnorm_b),
         static_cast<__nv_bfloat16*>(dconv_w), static_cast<__nv_bfloat16*>(dconv_b));
