@@ -53,8 +53,11 @@ struct SlotTcParams {
   int nprev;
 };
 
+// Advance the dynamic shared-memory base to a 1024-byte boundary of its shared-space address
+// (the swizzled TMA / UMMA tiles need it).  Pointer arithmetic on the shared array keeps the
+// address space known to the compiler, so accesses through the result are ld/st.shared.
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+  return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
 }
 
 // phi(z) = elu(z) + 1 = (z > 0 ? z + 1 : exp(z)), branch-free: max(z, 0) + exp(min(z, 0))
