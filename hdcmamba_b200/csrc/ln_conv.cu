@@ -147,7 +147,8 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   const int G = p.D / VEC;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, NW = blockDim.x >> 5;
   // smem: ring [nst][R rows] | partial sums [2][16][NW] fp32 | mbarriers [nst + 1]
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  // 128-byte aligned by shared-space offset (pointer arithmetic on the array keeps accesses ld/st.shared)
+  uint8_t* ring = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   float* red = reinterpret_cast<float*>(ring + (size_t)p.nst * stage_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * 16 * NW);
 

@@ -256,7 +256,8 @@ template <typename T, int NST>
 __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams p, int TR) {
   __shared__ __align__(16) float red[2][8][16];  // [half][value: 4 x sum dn nw, 4 x sum dn nw xhat][warp]
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  // 128-byte aligned by shared-space offset (pointer arithmetic on the array keeps accesses ld/st.shared)
+  uint8_t* ring = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int seg = blockIdx.x;
   const int b = seg / p.segs_per_b;
