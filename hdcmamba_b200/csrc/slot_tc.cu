@@ -1247,10 +1247,11 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       tc_fence_after();
       // y = bf16(Y) (y_slot is bf16); GroupNorm partial sums
       float o[2][EPW];
+      float yv2[2][EPW];
+      tmem_ld16x2(tL + YCOL + e0, tL + YCOL + 64 + e0, yv2[0], yv2[1]);  // both row blocks, one wait
 #pragma unroll
       for (int rb = 0; rb < 2; ++rb) {
-        float yv[EPW];
-        tmem_ld16(tL + YCOL + 64 * rb + e0, yv);
+        const float* yv = yv2[rb];
         float s1 = 0.f, s2 = 0.f;
 #pragma unroll
         for (int e = 0; e < EPW; ++e) {

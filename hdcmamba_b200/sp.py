@@ -118,6 +118,13 @@ class SequenceParallel:
             self._mb = None
             self._mb_key = None
 
+    def _final_norm(self, norm, h):
+        """A final nn.LayerNorm: the affine row kernel for CUDA kernels, the module otherwise."""
+        if h.is_cuda and isinstance(self.k, CudaKernels):
+            from .model import final_layer_norm
+            return final_layer_norm(norm, h)
+        return norm(h)
+
     def _side(self, h):
         """The side stream for the SSM kernels (CUDA kernels only; None for CPU stand-ins)."""
         if not h.is_cuda or not isinstance(self.k, CudaKernels):
@@ -226,7 +233,7 @@ class SequenceParallel:
         for i, blk in enumerate(model.layers):
             h = self.block(blk, h, layer=i)
         self._end()
-        return model.norm_final(h)
+        return self._final_norm(model.norm_final, h)
 
     def lm(self, lm, ids_local):
         """HdcMambaLM.forward (embedding -> backbone -> LayerNorm -> tied head) on the local
@@ -240,4 +247,4 @@ class SequenceParallel:
                 for i, blk in enumerate(lm.layers):
                     h = self.block(blk, h, layer=i)
                 self._end()
-            return F.linear(lm.norm(h), lm.embedding.weight)
+            return F.linear(self._final_norm(lm.norm, h), lm.embedding.weight)
