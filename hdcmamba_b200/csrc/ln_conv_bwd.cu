@@ -252,8 +252,9 @@ __device__ __forceinline__ void stg4_if(T* p, const uint64_t* f, bool pred) {
   }
 }
 
-template <typename T, int NST>
-__global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams p, int TR) {
+template <typename T, int NST, int TR>
+__global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams p) {
+  static_assert(TR % 4 == 0 && TR <= 32, "tiles of whole 4-row groups, one row per lane");
   __shared__ __align__(16) float red[2][8][16];  // [half][value: 4 x sum dn nw, 4 x sum dn nw xhat][warp]
   extern __shared__ uint8_t smem_raw[];
   // 128-byte aligned by shared-space offset (pointer arithmetic on the array keeps accesses ld/st.shared)
@@ -353,7 +354,9 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams
     const bool got = mbar_wait_warp(&bars[st], (uint32_t)((k / NST) & 1), 34);
     const uint32_t sx = ring_a + (uint32_t)st * 2 * tile_bytes + (uint32_t)cc * sizeof(T);
     const uint32_t sg = sx + tile_bytes;
-    for (int rk = 0; rk < nrows; rk += 4) {
+#pragma unroll
+    for (int rk = 0; rk < TR; rk += 4) {  // the tile's groups, unrolled (TR is a compile-time constant)
+      if (rk >= nrows) break;
       const int tg = t0 + rk;  // first row of the group
       uint64_t dxh[4][2];
       float v[8];
@@ -541,17 +544,14 @@ extern "C" int hdc_ln_conv_bwd(int dtype, const void* grad_out, const void* x, c
   const size_t smem = smem_of(TR, nst);
   auto launch_main = [&](auto tag) -> int {
     using T = decltype(tag);
-    if (staged) {
-      if (nst == 3) {
-        cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<T, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ln_conv_bwd_staged_kernel<T, 3><<<nseg, threads, smem, s>>>(p, TR);
-      } else {
-        cudaFuncSetAttribute(ln_conv_bwd_staged_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        ln_conv_bwd_staged_kernel<T, 2><<<nseg, threads, smem, s>>>(p, TR);
-      }
-    } else {
-      ln_conv_bwd_kernel<T><<<nseg, threads, 0, s>>>(p);
-    }
+    auto go = [&](auto kernel) {
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      kernel<<<nseg, threads, smem, s>>>(p);
+    };
+    if (!staged) ln_conv_bwd_kernel<T><<<nseg, threads, 0, s>>>(p);
+    else if (nst == 3 && TR == 8) go(ln_conv_bwd_staged_kernel<T, 3, 8>);
+    else if (nst == 3) go(ln_conv_bwd_staged_kernel<T, 3, 4>);
+    else go(ln_conv_bwd_staged_kernel<T, 2, 4>);
     return launch_status("ln_conv_bwd_kernel");
   };
   if (dtype == HDC_F32) {
