@@ -468,6 +468,7 @@ struct OutCfg {
   static constexpr int PW = NWG == 8 ? 16 : 32;          // columns of one S / P piece
   static constexpr int SRED = 2 * NWG;                   // GroupNorm partials per row
   static constexpr int MINB = CT == 64 ? 2 : 1;          // resident CTAs per SM
+  static constexpr int NST = CT == 64 ? 2 : 1;           // K / V / Q stages
   static constexpr bool INPLACE = RB == 128;             // Yi / Yx inside the S columns
   static constexpr int ncol(int rb) { return (rb + 1) * RB; }      // S columns of block rb
   static constexpr int scol(int rb) { return rb == 0 ? 0 : ncol(0); }
@@ -491,19 +492,23 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   constexpr int AG = Cfg::AG, PW = Cfg::PW, SRED = Cfg::SRED;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
-  uint8_t* sK = base;                       // phi(K), then k~ = bf16(phi(K) * kdec) in place
-  uint8_t* sV = sK + CT * 128;
-  uint8_t* sQ = sV + CT * 128;
-  uint8_t* sP = sQ + CT * 128;              // per row block: [ncol/64 atoms][RB rows][128 B]
+  // [NST] stages of K | V | Q (chunk 64: two, so the next chunk's loads fly during this one);
+  // K holds phi(K), then k~ = bf16(phi(K) * kdec) in place
+  constexpr int NST = Cfg::NST;
+  uint8_t* const stage0 = base;
+  uint8_t* sP = base + NST * 3 * CT * 128;  // per row block: [ncol/64 atoms][RB rows][128 B]
   uint8_t* sR = sP + Cfg::PBYTES;           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [CT + 4]
   float* sGn = sTab + CT + 4;                              // [128] gn weight | bias of this head
   float* sRed = sGn + 128;                                 // [CT][SRED] GroupNorm partial sums
-  // mbarriers: [0] K + V loads, [1] S products, [2] P.V / Yx / state products, [3] Q loads.
-  // Each commit follows a CTA barrier, so no thread can fall two phases behind on a
-  // barrier (which would alias the parity).
+  // mbarriers: [0] K + V loads of stage 0, [1] S products, [2] P.V / Yx / state products,
+  // [3] Q load of stage 0, [4] K + V and [5] Q of stage 1.  Each commit follows a CTA
+  // barrier, so no thread can fall two phases behind on a barrier (which would alias the
+  // parity).
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * SRED);
-  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 4);
+  uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 6);
+  auto kv_bar = [&](int st) { return &bars[st ? 4 : 0]; };
+  auto q_bar = [&](int st) { return &bars[st ? 5 : 3]; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, wg = warp >> 2;
@@ -523,7 +528,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     tma_prefetch_map(&mapQ);
     tma_prefetch_map(&mapK);
@@ -604,24 +609,34 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
   constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
 
-  uint32_t kph = 0, qph = 0, sph = 0, pph = 0;
-  int pending = 0;  // thread 0: bit 0 K/V loads, bit 1 Q load in flight
+  uint32_t kph = 0, qph = 0, sph = 0, pph = 0;  // kph / qph: parity bit per stage
+  int pending = 0;  // thread 0: bit st set while stage st has loads in flight
   bool ok = true;
-  auto issue = [&](int n) {
-    mbar_expect_tx(&bars[0], 2 * CT * 128);
-    tma_load_3d(sK, &mapK, h * p.hd, n * CT, b, &bars[0]);
-    tma_load_3d(sV, &mapV, h * p.hd, n * CT, b, &bars[0]);
-    mbar_expect_tx(&bars[3], CT * 128);
-    tma_load_3d(sQ, &mapQ, h * p.hd, n * CT, b, &bars[3]);
-    pending = 3;
+  auto issue = [&](int n, int st) {
+    uint8_t* k_ = stage0 + st * 3 * CT * 128;
+    mbar_expect_tx(kv_bar(st), 2 * CT * 128);
+    tma_load_3d(k_, &mapK, h * p.hd, n * CT, b, kv_bar(st));
+    tma_load_3d(k_ + CT * 128, &mapV, h * p.hd, n * CT, b, kv_bar(st));
+    mbar_expect_tx(q_bar(st), CT * 128);
+    tma_load_3d(k_ + 2 * CT * 128, &mapQ, h * p.hd, n * CT, b, q_bar(st));
+    pending |= 1 << st;
   };
-  if (tid == 0 && n0 < n1) issue(n0);
+  if (tid == 0) {
+    for (int i = 0; i < NST && n0 + i < n1; ++i) issue(n0 + i, i);
+  }
 
   for (int n = n0; n < n1 && ok; ++n) {
-    if (!mbar_wait_warp(&bars[0], kph, 21) || !mbar_wait_warp(&bars[3], qph, 22)) { ok = false; break; }
-    kph ^= 1;
-    qph ^= 1;
-    if (tid == 0) pending = 0;
+    const int st = NST == 2 ? ((n - n0) & 1) : 0;
+    uint8_t* const sK = stage0 + st * 3 * CT * 128;
+    uint8_t* const sV = sK + CT * 128;
+    uint8_t* const sQ = sV + CT * 128;
+    if (!mbar_wait_warp(kv_bar(st), (kph >> st) & 1u, 21) || !mbar_wait_warp(q_bar(st), (qph >> st) & 1u, 22)) {
+      ok = false;
+      break;
+    }
+    kph ^= 1u << st;
+    qph ^= 1u << st;
+    if (tid == 0) pending &= ~(1 << st);
     if (PERSTEP) {
       if (warp == 0) chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)n * CT) * p.H + h, p.H, sTab);
       __syncthreads();
@@ -752,7 +767,7 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
     if (!mbar_wait_warp(&bars[2], pph, 24)) { ok = false; break; }
     pph ^= 1;
     tc_fence_after();
-    if (tid == 0 && n + 1 < n1) issue(n + 1);  // every buffer of this chunk is free
+    if (tid == 0 && n + NST < n1) issue(n + NST, st);  // every buffer of this chunk's stage is free
     // ---- epilogue: y = bf16(Y), plain or GroupNorm * sigmoid(gate)
     float o[NRB][EPW];
 #pragma unroll
@@ -861,8 +876,12 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
   }
   // after a timed-out wait: let this CTA's own loads in flight land (bounded) before exit
   if (!ok && tid == 0) {
-    if (pending & 1) mbar_wait(&bars[0], kph, 26);
-    if (pending & 2) mbar_wait(&bars[3], qph, 27);
+    for (int st = 0; st < NST; ++st) {
+      if (pending & (1 << st)) {
+        mbar_wait(kv_bar(st), (kph >> st) & 1u, 26);
+        mbar_wait(q_bar(st), (qph >> st) & 1u, 27);
+      }
+    }
   }
   if (ok && seg == p.nseg - 1 && p.state_out) {
 #pragma unroll
@@ -1373,7 +1392,8 @@ static int make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, 
 
 template <int CT>
 static size_t smem_out_bytes() {
-  return 1024 + 3 * CT * 128 + OutCfg<CT>::PBYTES + 64 * 128 + (CT + 4 + 128 + CT * OutCfg<CT>::SRED) * 4 + 64;
+  return 1024 + OutCfg<CT>::NST * 3 * CT * 128 + OutCfg<CT>::PBYTES + 64 * 128 +
+         (CT + 4 + 128 + CT * OutCfg<CT>::SRED) * 4 + 6 * 8 + 16;
 }
 static size_t smem_state_bytes(int CT) { return 1024 + 4 * CT * 128 + (CT + 4) * 4 + 64; }
 
