@@ -35,7 +35,7 @@ MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "prefill tokens/sec at L=32768"
 # DRAM bytes (read + write) of one config-5 slot op (slot_tc_state + slot_tc_out) from an ncu
-# --set full capture of `bench.py --workload c5slot` (profiles/slot_scan_c5.md)
+# --set full capture of `bench.py --workload c5slot`
 SLOT_TRAFFIC_BYTES = 97.17e6 + 3.53e6 + 203.58e6 + 33.12e6
 
 
@@ -366,7 +366,7 @@ def main():
     ap.add_argument("--parallel", default="auto", choices=["auto", "sp", "batch"],
                     help="N > 1: batch = split the global batch over the ranks (no collective, config 4); "
                          "sp = split the sequence (config 5); auto = batch when the batch divides evenly")
-    ap.add_argument("--ref-tokens", type=int, default=512)
+    ap.add_argument("--ref-tokens", type=int, default=4096)
     ap.add_argument("--cpu-tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
@@ -585,7 +585,10 @@ def main():
                          "ms_per_launch": slot_ms, "launches_per_step": slot_per_step},
             "e2e": {"value": world * tokens_per_rank / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": world * ids_host.numel() * ids_host.element_size(),
-                    "d2h_bytes_per_step": world * out_host.numel() * out_host.element_size()},
+                    "d2h_bytes_per_step": world * out_host.numel() * out_host.element_size(),
+                    "result": "ids copied host->device from pinned memory each step; the full logits "
+                              "[B, L, vocab] are computed and stay on the device, and the last position's "
+                              "logits [B, vocab] are copied device->host each step"},
             "gpu_launches": launches,
             "clocks": clocks,
         }

@@ -50,8 +50,9 @@ SIGNATURES = {
     "hdc_slot_gate_carry_fwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp,
                                         c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_size,
                                         c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
-    "hdc_slot_set_path": (c_int, [c_int]),
-    "hdc_slot_last_path": (c_int, []),
+    "hdc_slot_scan_fwd_path": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,
+                                       c_i64, c_vp, c_vp, c_vp, c_size, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                       c_int, ctypes.POINTER(c_int), c_vp]),
     "hdc_device_error": (c_int, [c_int]),
     "hdc_gate_cat_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_i64,
                                  c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
@@ -71,6 +72,7 @@ SIGNATURES = {
     "hdc_peer_put": (c_int, [c_vp, c_size, c_vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32, c_int, c_vp,
                              c_vp]),
     "hdc_peer_wait": (c_int, [c_vp, ctypes.c_uint32, c_vp, c_vp]),
+    "hdc_peer_wait_for": (c_int, [c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint64, c_vp]),
     "hdc_peer_gen_bump": (c_int, [c_vp, c_vp]),
     "hdc_peer_barrier": (c_int, [c_vp, ctypes.c_uint64, c_int, c_int, c_vp, c_vp, c_vp]),
 }

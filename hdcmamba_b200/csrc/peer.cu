@@ -40,12 +40,16 @@ __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_re
 // generation g has been reached (wrap-safe): a fast rank may already have written g + 1
 __device__ __forceinline__ bool reached(uint32_t v, uint32_t g) { return (int32_t)(v - g) >= 0; }
 
-// bounded spin until *flag has reached generation want; false (and the error code) on timeout
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, int code) {
+constexpr uint64_t kPeerWaitNs = 2000000000ull;  // default limit of every flag wait (2 s)
+
+// bounded spin until *flag has reached generation want; false (and the error code) after
+// limit_ns nanoseconds of %globaltimer
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, int code,
+                                          uint64_t limit_ns = kPeerWaitNs) {
   if (reached(ld_acquire_sys(flag), want)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (!reached(ld_acquire_sys(flag), want)) {
-    if (globaltimer_ns() - t0 > 2000000000ull) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicCAS(&g_dev_error, 0, code);
       return false;
     }
@@ -83,10 +87,11 @@ __global__ void __launch_bounds__(512) peer_put_kernel(const uint4* src, size_t 
   }
 }
 
-// lane s waits for flags[s] == *gen for every bit s of mask (s < 32)
-__global__ void peer_wait_kernel(const uint32_t* flags, uint32_t mask, const uint32_t* gen) {
+// lane s waits for flags[s] == *gen for every bit s of mask (s < 32), each wait bounded by
+// limit_ns
+__global__ void peer_wait_kernel(const uint32_t* flags, uint32_t mask, const uint32_t* gen, uint64_t limit_ns) {
   const int s = threadIdx.x;
-  if (s < 32 && ((mask >> s) & 1u)) wait_flag(flags + s, *gen, 41);
+  if (s < 32 && ((mask >> s) & 1u)) wait_flag(flags + s, *gen, 41, limit_ns);
 }
 
 __global__ void peer_gen_bump_kernel(uint32_t* gen) { *gen += 1; }
@@ -166,11 +171,18 @@ extern "C" int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_b
   return launch_status("peer_put_kernel");
 }
 
-extern "C" int hdc_peer_wait(const uint32_t* flags, uint32_t mask, const uint32_t* gen, hdc_stream_t stream) {
+extern "C" int hdc_peer_wait_for(const uint32_t* flags, uint32_t mask, const uint32_t* gen, uint64_t timeout_ns,
+                                 hdc_stream_t stream) {
   if (!flags || !gen) return fail(HDC_E_NULL, "peer_wait: null pointer");
+  if (timeout_ns == 0 || timeout_ns > kPeerWaitNs)
+    return fail(HDC_E_SHAPE, "peer_wait: timeout %llu ns (1 .. 2e9)", (unsigned long long)timeout_ns);
   if (mask == 0) return 0;
-  peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, mask, gen);
+  peer_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(flags, mask, gen, timeout_ns);
   return launch_status("peer_wait_kernel");
+}
+
+extern "C" int hdc_peer_wait(const uint32_t* flags, uint32_t mask, const uint32_t* gen, hdc_stream_t stream) {
+  return hdc_peer_wait_for(flags, mask, gen, kPeerWaitNs, stream);
 }
 
 extern "C" int hdc_peer_gen_bump(uint32_t* gen, hdc_stream_t stream) {

@@ -4,28 +4,22 @@
 
 using namespace hdc;
 
-static int g_path_mode = 0;                // 0 auto, 1 force CUDA-core, 2 require tcgen05
-static thread_local int g_last_path = -1;  // 1 tcgen05, 0 CUDA-core
-
-extern "C" int hdc_slot_set_path(int mode) {
-  if (mode < 0 || mode > 2) return fail(HDC_E_SHAPE, "slot: path mode %d", mode);
-  g_path_mode = mode;
-  return 0;
-}
-
-extern "C" int hdc_slot_last_path(void) { return g_last_path; }
-
 extern "C" size_t hdc_slot_workspace_bytes(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C) {
   if (B < 1 || H < 1 || hd < 1 || C < 1 || L < C) return 0;
   const size_t a = slot_simt_workspace(B, L, H, hd, C), b = slot_tc_workspace(B, L, H, hd, C);
   return a > b ? a : b;
 }
 
-extern "C" int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
-                                 int64_t in_st, const void* gamma, const float* log_a, void* y, int64_t y_sb,
-                                 int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
-                                 void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
-                                 int64_t hd, int64_t C, int64_t rows, hdc_stream_t stream) {
+// Shared body of hdc_slot_scan_fwd / hdc_slot_scan_fwd_path: `path` 0 automatic, 1 CUDA
+// cores, 2 tcgen05 required; *path_used (when non-NULL) receives 1 for tcgen05, 0 for CUDA
+// cores.  No state outlives the call.
+extern "C" int hdc_slot_scan_fwd_path(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                                      int64_t in_st, const void* gamma, const float* log_a, void* y, int64_t y_sb,
+                                      int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
+                                      void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                                      int64_t hd, int64_t C, int64_t rows, int path, int* path_used,
+                                      hdc_stream_t stream) {
+  if (path < 0 || path > 2) return fail(HDC_E_SHAPE, "slot: path %d (0 auto, 1 CUDA cores, 2 tcgen05)", path);
   if (dtype != HDC_F32 && dtype != HDC_BF16) return fail(HDC_E_DTYPE, "slot: dtype %d", dtype);
   if (!q || !k || !v || !y || !workspace || (!gamma && !log_a)) return fail(HDC_E_NULL, "slot: null pointer");
   if (B < 1 || H < 1 || hd < 1 || hd > 128 || C < 1 || C > 256 || L < C || L % C != 0)
@@ -41,10 +35,19 @@ extern "C" int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const 
   p.L = (int)L; p.H = (int)H; p.hd = (int)hd; p.C = (int)C; p.rows = (int)rows; p.N = (int)(L / C);
   p.bd = (int)feature_block(hd);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  const bool tc = dtype == HDC_BF16 && g_path_mode != 1 && slot_tc_supported(p, B, in_sb, in_st);
-  if (g_path_mode == 2 && !tc) return fail(HDC_E_SHAPE, "slot: tcgen05 path required but not applicable");
-  g_last_path = tc ? 1 : 0;
+  const bool tc = dtype == HDC_BF16 && path != 1 && slot_tc_supported(p, B, in_sb, in_st);
+  if (path == 2 && !tc) return fail(HDC_E_SHAPE, "slot: tcgen05 path required but not applicable");
+  if (path_used) *path_used = tc ? 1 : 0;
   return tc ? slot_tc_fwd(p, nullptr, nullptr, B, in_sb, in_st, workspace, s) : slot_simt_fwd(dtype, p, B, workspace, s);
+}
+
+extern "C" int hdc_slot_scan_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                                 int64_t in_st, const void* gamma, const float* log_a, void* y, int64_t y_sb,
+                                 int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
+                                 void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                                 int64_t hd, int64_t C, int64_t rows, hdc_stream_t stream) {
+  return hdc_slot_scan_fwd_path(dtype, q, k, v, in_sb, in_st, gamma, log_a, y, y_sb, y_sh, y_st, state_in,
+                                state_out, workspace, workspace_bytes, B, L, H, hd, C, rows, 0, nullptr, stream);
 }
 
 static int slot_gate_common(const char* who, const void* q, const void* k, const void* v, int64_t in_sb,
@@ -71,7 +74,6 @@ static int slot_gate_common(const char* who, const void* q, const void* k, const
   if (!slot_tc_supported(p, B, in_sb, in_st))
     return fail(HDC_E_SHAPE, "%s: the fused epilogue needs the tcgen05 path (head_dim %% 8 == 0, "
                 "chunk 64/128/256, aligned row-major q/k/v)", who);
-  g_last_path = 1;
   SlotGate g{gate, gate_sb, gate_st, gn_w, gn_b};
   return slot_tc_fwd(p, &g, carry, B, in_sb, in_st, workspace, stream);
 }

@@ -112,29 +112,31 @@ __device__ __forceinline__ void prep_tile_u(uint8_t* tile, int hd, float pad) {
 
 // chunk-local cumulative log decay (per-step mode) by one warp:
 //   tab[i] = c_i = sum_{t=1..i} log_a[c0+t], tab[C] = c_{C-1} + log_a[c0] (chunk decay exponent)
+// The lanes stage log_a in tab, then lane 0 sums in row order, one fp32 add per row (the
+// sequential order of the CUDA-core kernel and of the oracle), so the decayed keys
+// bf16(phi(k) exp(c_{C-1} - c_j)) see the same c_j bits.
 template <int CT>
 __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float* tab) {
   constexpr int E = CT / 32;
   const int lane = threadIdx.x & 31;
   float v[E];
-  float run = 0.f;
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const int i = lane * E + e;
-    run += (i == 0) ? 0.f : la[(size_t)i * H];
-    v[e] = run;
-  }
-  float incl = run;
+  for (int e = 0; e < E; ++e) v[e] = la[(size_t)(e * 32 + lane) * H];
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  const float off = incl - run;
-#pragma unroll
-  for (int e = 0; e < E; ++e) tab[lane * E + e] = off + v[e];
+  for (int e = 0; e < E; ++e) tab[e * 32 + lane] = v[e];
   __syncwarp();
-  if (lane == 0) tab[CT] = tab[CT - 1] + la[0];
+  if (lane == 0) {
+    const float a0 = tab[0];
+    float run = 0.f;
+    tab[0] = 0.f;
+#pragma unroll 8
+    for (int i = 1; i < CT; ++i) {
+      run += tab[i];
+      tab[i] = run;
+    }
+    tab[CT] = run + a0;
+  }
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------

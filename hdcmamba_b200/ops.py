@@ -192,16 +192,23 @@ def feature_block(hd):
     return max(64, b)
 
 
+_SLOT_PATHS = {"auto": 0, "simt": 1, "tc": 2}
+
+
 def slot_scan(q, k, v, num_heads, chunk, gamma=None, log_a=None, rows=None, y=None, y_strides=None,
-              state_in=None, return_state=False):
+              state_in=None, return_state=False, path="auto", path_used=None):
     """Slot memory scan (replaces ``_slot_all_fused``, hdcmamba/model.py:236-272).
 
     q, k, v: [B, L, H*hd] views sharing strides (unit last-dim stride), raw
     (before phi).  gamma: [H] (in the activation dtype) or log_a: fp32 [B, L, H].
     y: optional output tensor with element strides ``y_strides = (sb, sh, st)``
     (element (b, t, h, d) at b*sb + h*sh + t*st + d); default [B, L, H, hd].
+    path: "auto", "simt" (CUDA-core kernel) or "tc" (tcgen05 required, error otherwise);
+    ``path_used`` (a list) receives "tc" or "simt".
     Returns y (and the fp32 final state [B, H, bd, bd] if ``return_state``)."""
     _cuda(q, k, v, gamma, log_a, y, state_in)
+    if path not in _SLOT_PATHS:
+        raise ValueError(f"path must be one of {sorted(_SLOT_PATHS)}")
     _same_dtype(q, k, v)
     B, L, W = q.shape
     H = num_heads
@@ -231,9 +238,12 @@ def slot_scan(q, k, v, num_heads, chunk, gamma=None, log_a=None, rows=None, y=No
         state_in = state_in.float().contiguous()
     nbytes = slot_workspace_bytes(B, L, H, hd, chunk)
     ws = torch.empty(max(nbytes, 16), device=q.device, dtype=torch.uint8)
-    _lib.call("hdc_slot_scan_fwd", _code(q), _p(q), _p(k), _p(v), q.stride(0), q.stride(1), _p(gamma), _p(log_a),
-              _p(y), y_strides[0], y_strides[1], y_strides[2], _p(state_in), _p(state_out), _p(ws), ws.numel(),
-              B, L, H, hd, chunk, rows, _stream(q))
+    used = ctypes.c_int(-1)
+    _lib.call("hdc_slot_scan_fwd_path", _code(q), _p(q), _p(k), _p(v), q.stride(0), q.stride(1), _p(gamma),
+              _p(log_a), _p(y), y_strides[0], y_strides[1], y_strides[2], _p(state_in), _p(state_out), _p(ws),
+              ws.numel(), B, L, H, hd, chunk, rows, _SLOT_PATHS[path], ctypes.byref(used), _stream(q))
+    if path_used is not None:
+        path_used.append("tc" if used.value == 1 else "simt")
     return (y, state_out) if return_state else y
 
 

@@ -83,9 +83,14 @@ class _Mailboxes:
 class SequenceParallel:
     """Runs HdcMamba blocks / LMs on this rank's segment of the sequence."""
 
-    def __init__(self, group=None, kernels=None, transport="nccl"):
+    def __init__(self, group=None, kernels=None, transport="nccl", check_errors=False):
+        """``check_errors``: after every forward, synchronise and raise HdcError if a bounded
+        device wait (p2p halo / carry flags, the end-of-forward flag barrier, the kernels'
+        mbarrier waits) gave up.  Off by default because it synchronises the stream (and
+        cannot run inside CUDA-graph capture); ``check()`` does the same on demand."""
         if transport not in ("nccl", "p2p"):
             raise ValueError(f"transport {transport!r}: 'nccl' or 'p2p'")
+        self.check_errors = check_errors
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -110,6 +115,19 @@ class SequenceParallel:
             self._mb = PeerMailbox(self._lay.total, group=self.group, device=device)
             self._mb_key = key
         return self._mb, self._lay
+
+    def check(self):
+        """Synchronise this rank's device and raise HdcError if a bounded device wait timed
+        out since the last check (the error word is cleared).  A timed-out p2p wait means
+        the halo or carries of a peer never arrived, so the forward's output is invalid."""
+        if not isinstance(self.k, CudaKernels):
+            return
+        from . import _lib
+        torch.cuda.synchronize()
+        code = _lib.load().hdc_device_error(1)
+        if code != 0:
+            raise _lib.HdcError(f"rank {self.rank}: a bounded device wait timed out (code {code}); "
+                                "the sequence-parallel forward's output is invalid")
 
     def close(self):
         """Release the p2p mailbox (collective)."""
@@ -141,6 +159,10 @@ class SequenceParallel:
     def _end(self):
         if self.transport == "p2p":
             self._mb.barrier(self._lay.bar)
+
+    def _finish(self):
+        if self.check_errors:
+            self.check()
 
     def block(self, blk, h, layer=0):
         """One HdcMamba9v3Block on the local segment h [B, Ls, dm] (Ls a multiple of the
@@ -233,7 +255,9 @@ class SequenceParallel:
         for i, blk in enumerate(model.layers):
             h = self.block(blk, h, layer=i)
         self._end()
-        return self._final_norm(model.norm_final, h)
+        out = self._final_norm(model.norm_final, h)
+        self._finish()
+        return out
 
     def lm(self, lm, ids_local):
         """HdcMambaLM.forward (embedding -> backbone -> LayerNorm -> tied head) on the local
@@ -247,4 +271,5 @@ class SequenceParallel:
                 for i, blk in enumerate(lm.layers):
                     h = self.block(blk, h, layer=i)
                 self._end()
+                self._finish()
             return F.linear(self._final_norm(lm.norm, h), lm.embedding.weight)

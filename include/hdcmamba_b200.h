@@ -229,15 +229,19 @@ int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, const void*
                             hdc_stream_t stream);
 
 /*
- * Slot-scan path control (tests / cross-checks): mode 0 = automatic (tcgen05 for bf16
- * with feature width 64, chunk 64/128/256, 8-aligned head_dim and row-contiguous
- * inputs; CUDA cores otherwise), 1 = always the CUDA-core kernel, 2 = require
- * tcgen05 (calls that cannot use it fail with HDC_E_SHAPE).  Process-wide.
- * hdc_slot_last_path(): 1 if the calling thread's last hdc_slot_scan_fwd ran the
- * tcgen05 kernels, 0 for the CUDA-core kernels, -1 before any call.
+ * hdc_slot_scan_fwd with the kernel family chosen per call (tests / cross-checks): path 0 =
+ * automatic (tcgen05 for bf16 with feature width 64, chunk 64/128/256, 8-aligned head_dim
+ * and row-contiguous inputs; CUDA cores otherwise), 1 = always the CUDA-core kernel, 2 =
+ * require tcgen05 (HDC_E_SHAPE when it cannot be used).  *path_used (host int, may be NULL)
+ * receives 1 when the tcgen05 kernels ran, 0 for the CUDA-core kernels.  No state is kept
+ * between calls.  Same reference code as hdc_slot_scan_fwd (hdcmamba/model.py:236-272).
  */
-int hdc_slot_set_path(int mode);
-int hdc_slot_last_path(void);
+int hdc_slot_scan_fwd_path(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
+                           int64_t in_st, const void* gamma, const float* log_a, void* y, int64_t y_sb,
+                           int64_t y_sh, int64_t y_st, const float* state_in, float* state_out,
+                           void* workspace, size_t workspace_bytes, int64_t B, int64_t L, int64_t H,
+                           int64_t hd, int64_t C, int64_t rows, int path, int* path_used,
+                           hdc_stream_t stream);
 
 /*
  * Device-side error word of the tcgen05 kernels: 0, or the code of a bounded wait
@@ -334,6 +338,8 @@ int hdc_slot_step(int dtype, const void* q, const void* k, const void* v, const 
  *   dst_base is a device array of `world` mailbox base addresses as mapped in this process.
  * hdc_peer_wait: wait until flags[s] has reached *gen (wrap-safe >=) for every bit s of mask
  *   (acquire, system scope).
+ * hdc_peer_wait_for: hdc_peer_wait with the caller's limit per flag (1 ns .. 2 s; HDC_E_SHAPE
+ *   otherwise); on timeout the wait records code 41 in hdc_device_error() and returns.
  * hdc_peer_gen_bump: *gen += 1 (once per forward on every rank).
  * hdc_peer_barrier: store *gen into slot `rank` of the uint32 array at base[s] + bar_off of
  *   every rank s, then wait until all `world` slots of local_bar have reached *gen.
@@ -348,6 +354,8 @@ int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_base, uint64
                  uint64_t flag_off, uint32_t mask, int world, const uint32_t* gen,
                  hdc_stream_t stream);
 int hdc_peer_wait(const uint32_t* flags, uint32_t mask, const uint32_t* gen, hdc_stream_t stream);
+int hdc_peer_wait_for(const uint32_t* flags, uint32_t mask, const uint32_t* gen, uint64_t timeout_ns,
+                      hdc_stream_t stream);
 int hdc_peer_gen_bump(uint32_t* gen, hdc_stream_t stream);
 int hdc_peer_barrier(const uint64_t* base, uint64_t bar_off, int world, int rank,
                      const uint32_t* local_bar, const uint32_t* gen, hdc_stream_t stream);

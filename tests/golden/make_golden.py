@@ -318,10 +318,13 @@ def case_c1(M):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("HDCMAMBA_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("HDCMAMBA_REF"),
+                    help="checkout of the reference repository (or set HDCMAMBA_REF)")
     ap.add_argument("--skip-c1", action="store_true")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give --ref <reference checkout> or set HDCMAMBA_REF")
     torch.set_num_threads(8)
     M, triton = load_reference(a.ref)
     todo = {"lnconv": lambda: case_lnconv(M, triton), "lnconv_bwd": lambda: case_lnconv_bwd(M, triton),

@@ -38,18 +38,20 @@ def _worker(rank, world, port, q, transport="nccl"):
         L = 4096
         ids = torch.randint(0, 4096, (1, L), generator=torch.Generator().manual_seed(1)).to(dev)
         Ls = L // world
-        sp = SequenceParallel(transport=transport)
+        sp = SequenceParallel(transport=transport, check_errors=True)  # raises on a timed-out wait
         logits = sp.lm(lm, ids[:, rank * Ls:(rank + 1) * Ls].contiguous())
         logits = sp.lm(lm, ids[:, rank * Ls:(rank + 1) * Ls].contiguous())  # a second generation
         out = torch.empty((world,) + tuple(logits.shape), device=dev, dtype=logits.dtype)
         dist.all_gather_into_tensor(out.reshape(-1), logits.contiguous().reshape(-1))
         torch.cuda.synchronize()
+        # every rank reports its device error word: in p2p mode the higher ranks run the waits
+        q.put(("dev", rank, _lib.load().hdc_device_error(1)))
         if rank == 0:
             with torch.no_grad():
                 ref = lm(ids)
             got = out.permute(1, 0, 2, 3).reshape(1, L, -1)
             err = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
-            q.put((err, _lib.load().hdc_device_error(1)))
+            q.put(("err", err))
         dist.barrier()
         sp.close()
     except Exception as e:
@@ -71,13 +73,17 @@ def test_sequence_parallel_two_gpus_matches_one_gpu(transport):
     procs = [ctx.Process(target=_worker, args=(r, world, port, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
-    res = q.get(timeout=600)
+    msgs = []
+    for _ in range(world + 1):
+        m = q.get(timeout=600)
+        if isinstance(m, Exception):
+            raise m
+        msgs.append(m)
     for p in procs:
         p.join(timeout=120)
-    if isinstance(res, Exception):
-        raise res
-    err, dev_err = res
-    assert dev_err == 0
+    dev = {m[1]: m[2] for m in msgs if m[0] == "dev"}
+    assert dev == {r: 0 for r in range(world)}, dev
+    err = [m[1] for m in msgs if m[0] == "err"][0]
     assert err < BF16_TOL, err
     assert all(p.exitcode == 0 for p in procs)
 

@@ -6,12 +6,14 @@ call cudaMalloc at that point); its chunk statistics live in a fixed device arra
 the library reserves at load time.  The GPU test checks it against the regular entry
 points (hdc_ssm_chunk_stats + hdc_ssm_scan_out with a caller workspace) on two calls in
 a row, so the shared array's leftover contents from the first call cannot leak into the
-second.  This file is collected last on purpose."""
+second, and against the CPU oracle's restatement of the reference's three SSM kernels
+(oracle.ssm_chunk_fwd, hdcmamba/model.py:175-233).  This file is collected last on purpose."""
 import ctypes
 
 import pytest
 import torch
 
+import oracle as O
 from hdcmamba_b200 import _lib, ops
 
 BF16_TOL = 2e-2
@@ -58,3 +60,6 @@ def test_noalloc_matches_regular_entry_points_on_two_calls():
         err = float((y.float() - ref.float()).abs().max() / ref.float().abs().max())
         assert err < BF16_TOL, err
         assert torch.equal(y, ref)  # same kernels, same statistics: bit-identical
+        oracle = O.ssm_chunk_fwd(projs.cpu(), A_log.cpu(), ds, C)
+        err_o = float((y.float().cpu() - oracle).abs().max() / oracle.abs().max())
+        assert err_o < BF16_TOL, err_o
