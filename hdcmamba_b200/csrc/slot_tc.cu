@@ -935,7 +935,7 @@ constexpr int YCOL = RB, UCOL = 2 * RB, P1COL = 3 * RB;
 constexpr int TILE = CT * 128;       // one [CT x 64] bf16 tile
 constexpr int TABN = CT + 4;
 // mbarriers
-enum { B_L0, B_L1, B_V, B_G, B_S, B_Y, B_READY, B_P, B_OUT, B_SYNC, NBAR };
+enum { B_L0, B_L1, B_V, B_G, B_S, B_Y, B_READY, B_P, B_KQ, B_OUT, B_SYNC, NBAR };
 constexpr size_t SMEM = 1024 + 6 * TILE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + CT * NWG * 8 + NBAR * 8 + 16;
 // TMEM column of the packed P of piece c (row block 0: in place; row block 1: [384,512))
 __device__ __forceinline__ uint32_t pcol(int c) {
@@ -988,7 +988,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
   }
   if (tid == 0) {
     for (int i = 0; i < NBAR; ++i)
-      mbar_init(&bars[i], (i == B_READY || i == B_P || i == B_OUT || i == B_SYNC) ? NCW : 1);
+      mbar_init(&bars[i], (i == B_READY || i == B_P || i == B_KQ || i == B_OUT || i == B_SYNC) ? NCW : 1);
     fence_mbar_init();
   }
   if (!PERSTEP) {
@@ -1029,7 +1029,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       if (n0 + 1 < n1) load_kq(n0 + 1, 1);
       constexpr uint32_t idPV = idesc_bf16_f32(RB, 64, false, true);
       constexpr uint32_t idU = idesc_bf16_f32(64, 64, true, true);
-      uint32_t rph = 0, pph = 0, yph = 0, oph = 0;
+      uint32_t rph = 0, pph = 0, kqph = 0, yph = 0, oph = 0;
       for (int n = n0; n < n1; ++n) {
         const int cur = (n - n0) & 1;
         // S_rb = phi(Q_rb) phi(K[0 : 128 (rb + 1)])^T once phi(n) is in place and U(n-1) was read
@@ -1056,32 +1056,40 @@ __global__ void __launch_bounds__(pipe::NT, 1)
           bulk_wait_read0();
           load_g(n);
         }
-        // Y_rb = Qs_rb bf16(R) + P_rb V;  U = k~^T V
+        // Y_rb = P_rb V + Qs_rb bf16(R);  U = k~^T V.  The P V products go first: they need only
+        // P (TMEM) and V, so they run while the compute warps form k~ and Qs in place.
         if (!mbar_wait(&bars[B_P], pph, 53)) break;
         pph ^= 1;
         if (!mbar_wait(&bars[B_V], (uint32_t)((n - n0) & 1), 54)) break;
         tc_fence_after();
         const uint64_t dR = sdesc_sw128(smem_u32(sR), 0, 1024), dV = sdesc_sw128(smem_u32(sV), 0, 1024);
         const uint64_t dKm = sdesc_sw128(smem_u32(sK(cur)), 0, 1024);
-        // three independent accumulations, interleaved: Y_0 (4 + 8 steps), Y_1 (4 + 16), U (16)
-        auto y_step = [&](int rb, int t) {  // step t of Y_rb: Qs_rb bf16(R) first, then P_rb V
-          const uint32_t dY = tmem + YCOL + 64 * rb;
-          if (t < 4) {
-            umma_bf16(dY, dQ + (uint64_t)((rb * RB * 128 + t * 32) >> 4), dR + (uint64_t)((t * 2048) >> 4), idPV,
-                      t > 0 ? 1u : 0u);
-          } else {
-            constexpr int KPP = PW / 16;  // 16-column K steps per piece
-            const int kk = t - 4, c = rb * (RB / PW) + kk / KPP;
-            umma_bf16_ts(dY, tmem + pcol(c) + (kk % KPP) * 8, dV + (uint64_t)((kk * 16 * 128) >> 4), idPV, 1u);
-          }
+        constexpr int KPP = PW / 16;  // 16-column K steps per piece
+        auto pv_step = [&](int rb, int kk) {  // K step kk of P_rb V (the first one starts Y_rb)
+          const int c = rb * (RB / PW) + kk / KPP;
+          umma_bf16_ts(tmem + YCOL + 64 * rb, tmem + pcol(c) + (kk % KPP) * 8, dV + (uint64_t)((kk * 16 * 128) >> 4),
+                       idPV, kk > 0 ? 1u : 0u);
         };
+        // two independent accumulations, interleaved: Y_1 (16 steps), Y_0 (8)
 #pragma unroll
-        for (int t = 0; t < 4 + 2 * RB / 16; ++t) {
-          y_step(1, t);
-          if (t < CT / 16)
-            umma_bf16(tmem + UCOL, dKm + (uint64_t)((t * 2048) >> 4), dV + (uint64_t)((t * 2048) >> 4), idU,
-                      t > 0 ? 1u : 0u);
-          if (t < 4 + RB / 16) y_step(0, t);
+        for (int t = 0; t < 2 * RB / 16; ++t) {
+          pv_step(1, t);
+          if (t < RB / 16) pv_step(0, t);
+        }
+        if (!mbar_wait(&bars[B_KQ], kqph, 64)) break;
+        kqph ^= 1;
+        tc_fence_after();
+        // U (16 steps) interleaved with Qs_rb bf16(R) (4 steps per row block, accumulating)
+#pragma unroll
+        for (int t = 0; t < CT / 16; ++t) {
+          umma_bf16(tmem + UCOL, dKm + (uint64_t)((t * 2048) >> 4), dV + (uint64_t)((t * 2048) >> 4), idU,
+                    t > 0 ? 1u : 0u);
+          if (t < 4) {
+#pragma unroll
+            for (int rb = 0; rb < 2; ++rb)
+              umma_bf16(tmem + YCOL + 64 * rb, dQ + (uint64_t)((rb * RB * 128 + t * 32) >> 4),
+                        dR + (uint64_t)((t * 2048) >> 4), idPV, 1u);
+          }
         }
         umma_commit(&bars[B_Y]);
         // every product reading stage cur and V is done: next loads
@@ -1182,32 +1190,6 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       if (!mbar_wait_warp(&bars[B_S], sph, 58)) { ok = false; break; }
       sph ^= 1;
       tc_fence_after();
-      // k~ = bf16(phi(k) kdec_j) and Qs = bf16(phi(q) qdec_i) in place
-      {
-        constexpr int IT = CT * 8 / NTC;
-        uint4 kv[IT], qv[IT];
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-          kv[it] = reinterpret_cast<const uint4*>(K_)[tid + it * NTC];
-          qv[it] = reinterpret_cast<const uint4*>(Q_)[tid + it * NTC];
-        }
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-          const int idx = tid + it * NTC, row = idx >> 3;
-          const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
-          const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
-          const uint64_t kd2 = f2_make(kd, kd), qd2 = f2_make(qd, qd);
-          uint32_t* wk = reinterpret_cast<uint32_t*>(&kv[it]);
-          uint32_t* wq = reinterpret_cast<uint32_t*>(&qv[it]);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            wk[i] = f2_to_bf2(f2_mul(bf2_to_f2(wk[i]), kd2));
-            wq[i] = f2_to_bf2(f2_mul(bf2_to_f2(wq[i]), qd2));
-          }
-          reinterpret_cast<uint4*>(K_)[idx] = kv[it];
-          reinterpret_cast<uint4*>(Q_)[idx] = qv[it];
-        }
-      }
       // P = bf16(mask(S) decay) of this warpgroup's pieces -> TMEM (packed pairs)
 #pragma unroll
       for (int cc = 0; cc < CPW; ++cc) {
@@ -1258,9 +1240,37 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         else tmem_st8_async(tL + pcol(c), pk);
       }
       tmem_wait_st();
-      fence_proxy_async_smem();
       tc_fence_before();
       warp_arrive(B_P);
+      // the P V products run while k~ and Qs are formed
+      // k~ = bf16(phi(k) kdec_j) and Qs = bf16(phi(q) qdec_i) in place (S(n) has read them)
+      {
+        constexpr int IT = CT * 8 / NTC;
+        uint4 kv[IT], qv[IT];
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+          kv[it] = reinterpret_cast<const uint4*>(K_)[tid + it * NTC];
+          qv[it] = reinterpret_cast<const uint4*>(Q_)[tid + it * NTC];
+        }
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+          const int idx = tid + it * NTC, row = idx >> 3;
+          const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
+          const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
+          const uint64_t kd2 = f2_make(kd, kd), qd2 = f2_make(qd, qd);
+          uint32_t* wk = reinterpret_cast<uint32_t*>(&kv[it]);
+          uint32_t* wq = reinterpret_cast<uint32_t*>(&qv[it]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            wk[i] = f2_to_bf2(f2_mul(bf2_to_f2(wk[i]), kd2));
+            wq[i] = f2_to_bf2(f2_mul(bf2_to_f2(wq[i]), qd2));
+          }
+          reinterpret_cast<uint4*>(K_)[idx] = kv[it];
+          reinterpret_cast<uint4*>(Q_)[idx] = qv[it];
+        }
+      }
+      fence_proxy_async_smem();
+      warp_arrive(B_KQ);
       // meanwhile: the next chunk's phi
       if (n + 1 < n1 && !prep(n + 1, nxt)) { ok = false; break; }
       if (!mbar_wait_warp(&bars[B_Y], yph, 60)) { ok = false; break; }
