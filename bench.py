@@ -297,6 +297,90 @@ def kernel_c5slot(dev, iters, hbm):
             "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / ms / 1e6, "frac": nbytes / ms / 1e6 / hbm}
 
 
+class _AttnBlock(torch.nn.Module):
+    """Decoder block of the comparison Transformer in the reference benchmark harness
+    (benchmark.py:52-85): pre-LN causal self-attention through
+    F.scaled_dot_product_attention (flash / cuDNN backends), then a pre-LN 4x GELU MLP."""
+
+    def __init__(self, d, heads):
+        super().__init__()
+        nn = torch.nn
+        self.heads = heads
+        self.ln1, self.ln2 = nn.LayerNorm(d), nn.LayerNorm(d)
+        self.qkv, self.proj = nn.Linear(d, 3 * d), nn.Linear(d, d)
+        self.mlp = nn.Sequential(nn.Linear(d, 4 * d), nn.GELU(), nn.Linear(4 * d, d))
+
+    def forward(self, x):
+        B, L, d = x.shape
+        q, k, v = self.qkv(self.ln1(x)).view(B, L, 3, self.heads, d // self.heads).permute(2, 0, 3, 1, 4)
+        a = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True)
+        x = x + self.proj(a.transpose(1, 2).reshape(B, L, d))
+        return x + self.mlp(self.ln2(x))
+
+
+class _AttnModel(torch.nn.Module):
+    def __init__(self, d=512, heads=8, layers=6):
+        super().__init__()
+        self.blocks = torch.nn.ModuleList([_AttnBlock(d, heads) for _ in range(layers)])
+        self.ln = torch.nn.LayerNorm(d)
+
+    def forward(self, x):
+        for b in self.blocks:
+            x = b(x)
+        return self.ln(x)
+
+
+def harness(dev, runs=20, warmup=5):
+    """The reference's benchmark harness (benchmark.py:215-362), B200 edition: forward
+    throughput of HdcMamba9v3Model (6 x d768, d_state 128, 12 heads, the harness's shapes)
+    against a 6 x d512, 8-head Transformer on torch's scaled_dot_product_attention, bf16,
+    inputs x ~ N(0,1) of the models' widths.  Shapes (B, L) follow the harness: 4x1024, 4x4096,
+    the "8K" row (HdcMamba 2x4096 as the harness builds it, benchmark.py:330; Transformer
+    2x8192), 1x16384, 1x32768.  Each model is timed eagerly (CUDA events around ``runs``
+    forwards after ``warmup``); the HdcMamba model also as one CUDA-graph replay per forward."""
+    from hdcmamba_b200 import HdcMamba9v3Model
+    from hdcmamba_b200.graph import GraphedForward
+    torch.manual_seed(0)
+    hdc = HdcMamba9v3Model(d_model=768, n_layers=6, d_state=128, num_slots=32, num_heads=12).to(dev).bfloat16().eval()
+    tf = _AttnModel().to(dev).bfloat16().eval()
+    rows = [("1K", (4, 1024), (4, 1024)), ("4K", (4, 4096), (4, 4096)), ("8K", (2, 4096), (2, 8192)),
+            ("16K", (1, 16384), (1, 16384)), ("32K", (1, 32768), (1, 32768))]
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(runs):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / runs
+
+    out = []
+    with torch.no_grad():
+        for label, (hb, hl), (tb, tlen) in rows:
+            g = torch.Generator(device=dev).manual_seed(1)
+            xh = torch.randn(hb, hl, 768, device=dev, generator=g).bfloat16()
+            xt = torch.randn(tb, tlen, 512, device=dev, generator=g).bfloat16()
+            ms_h = timed(lambda: hdc(xh))
+            gf = GraphedForward(hdc, xh)
+            ms_hg = timed(gf.replay)
+            del gf
+            ms_t = timed(lambda: tf(xt))
+            r = {"row": label, "hdcmamba": {"B": hb, "L": hl, "ms": ms_h, "tok_s": hb * hl / ms_h * 1e3,
+                                             "ms_graph": ms_hg, "tok_s_graph": hb * hl / ms_hg * 1e3},
+                 "transformer_sdpa": {"B": tb, "L": tlen, "ms": ms_t, "tok_s": tb * tlen / ms_t * 1e3}}
+            r["speedup_tok_s"] = r["hdcmamba"]["tok_s"] / r["transformer_sdpa"]["tok_s"]
+            out.append(r)
+            del xh, xt
+            torch.cuda.empty_cache()
+    return {"workload": "harness: HdcMamba9v3Model 6x d768 ds128 H12 vs Transformer 6x d512 H8 (SDPA), "
+                        "forward, bf16, x ~ N(0,1)", "reference_claim": "3.37x tokens/s at L=32768 (README.md:12)",
+            "rows": out}
+
+
 def cpu_oracle_tokens_per_s(cfg, tokens, repeats=2):
     """CPU oracle port (oracle/restate.py, fp32 math with the bf16 rounding points) on
     the first ``tokens`` ids, all layers and the full vocab head."""
@@ -371,7 +455,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
     ap.add_argument("--eager", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--workload", default=None, choices=["c2", "c2bwd", "c3", "c5slot", "c5layer"],
+    ap.add_argument("--workload", default=None, choices=["c2", "c2bwd", "c3", "c5slot", "c5layer", "harness"],
                     help="time one kernel workload alone (for profiling) and print its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -387,6 +471,9 @@ def main():
     if args.workload:
         torch.cuda.set_device(local)
         dev = torch.device("cuda", local)
+        if args.workload == "harness":
+            print(json.dumps(harness(dev)), flush=True)
+            return
         if args.workload == "c5layer":
             for L in (4096, 32768):  # a sequence-parallel rank's length at 8 GPUs, and one GPU's
                 print(json.dumps(layer_c5(dev, peaks()[0], seq_len=L, iters=args.steps)), flush=True)

@@ -126,13 +126,27 @@ __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float*
   for (int e = 0; e < E; ++e) tab[e * 32 + lane] = v[e];
   __syncwarp();
   if (lane == 0) {
+    // blocks of 8 rows; the next block's loads are issued before this block's stores, so
+    // only the fp32 add chain is serial
     const float a0 = tab[0];
-    float run = 0.f;
-    tab[0] = 0.f;
-#pragma unroll 8
-    for (int i = 1; i < CT; ++i) {
-      run += tab[i];
-      tab[i] = run;
+    float run = 0.f, cur[8], nxt[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cur[e] = tab[e];
+#pragma unroll 1
+    for (int blk = 0; blk < CT / 8; ++blk) {
+      if (blk + 1 < CT / 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nxt[e] = tab[(blk + 1) * 8 + e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (blk > 0 || e > 0) run += cur[e];
+        cur[e] = run;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tab[blk * 8 + e] = cur[e];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cur[e] = nxt[e];
     }
     tab[CT] = run + a0;
   }
