@@ -950,7 +950,7 @@ constexpr int TILE = CT * 128;       // one [CT x 64] bf16 tile
 constexpr int TABN = CT + 4;
 // mbarriers
 enum { B_L0, B_L1, B_V, B_G, B_S, B_Y, B_READY, B_P, B_KQ, B_OUT, B_SYNC, NBAR };
-constexpr size_t SMEM = 1024 + 6 * TILE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + CT * NWG * 8 + NBAR * 8 + 16;
+constexpr size_t SMEM = 1024 + 6 * TILE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + 2 * CT * NWG * 8 + NBAR * 8 + 16;
 // TMEM column of the packed P of piece c (row block 0: in place; row block 1: [384,512))
 __device__ __forceinline__ uint32_t pcol(int c) {
   return c < RB / PW ? (uint32_t)(c * PW) : (uint32_t)(P1COL + (c - RB / PW) * (PW / 2));
@@ -976,8 +976,8 @@ __global__ void __launch_bounds__(pipe::NT, 1)
   uint8_t* sR = base + 6 * TILE;                           // [64 rows][128 B], MN-major bf16 R
   float* sTab = reinterpret_cast<float*>(sR + 64 * 128);  // [2][TABN] (per-step: one per stage)
   float* sGn = sTab + 2 * TABN;                            // [128] gn weight | bias of this head
-  float2* sRed = reinterpret_cast<float2*>(sGn + 128);     // [NWG][CT] GroupNorm (sum, sum of squares)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + CT * NWG);
+  float2* sRed = reinterpret_cast<float2*>(sGn + 128);     // [2][NWG][CT] GroupNorm (sum, sum of squares)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + 2 * CT * NWG);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + NBAR);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1046,7 +1046,8 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       uint32_t rph = 0, pph = 0, kqph = 0, yph = 0, oph = 0;
       for (int n = n0; n < n1; ++n) {
         const int cur = (n - n0) & 1;
-        // S_rb = phi(Q_rb) phi(K[0 : 128 (rb + 1)])^T once phi(n) is in place and U(n-1) was read
+        // S_rb = phi(Q_rb) phi(K[0 : 128 (rb + 1)])^T once phi(n) is in place and Y(n-1), U(n-1)
+        // were read out of TMEM
         if (!mbar_wait(&bars[B_READY], rph, 51)) break;
         rph ^= 1;
         tc_fence_after();
@@ -1061,15 +1062,6 @@ __global__ void __launch_bounds__(pipe::NT, 1)
             umma_bf16(tmem + rb * RB, dQ + (uint64_t)((rb * RB * 128 + k * 32) >> 4), dK + (uint64_t)((k * 32) >> 4),
                       idesc_bf16_f32(RB, RB * (rb + 1), false, false), k > 0 ? 1u : 0u);
         umma_commit(&bars[B_S]);
-        // outputs of chunk n-1 out, gate of chunk n in
-        if (n > n0) {
-          if (!mbar_wait(&bars[B_OUT], oph, 52)) break;
-          oph ^= 1;
-          tma_store_3d(&mg.out, sG, h * p.hd, (n - 1) * CT, b);
-          bulk_commit();
-          bulk_wait_read0();
-          load_g(n);
-        }
         // Y_rb = P_rb V + Qs_rb bf16(R);  U = k~^T V.  The P V products go first: they need only
         // P (TMEM) and V, so they run while the compute warps form k~ and Qs in place.
         if (!mbar_wait(&bars[B_P], pph, 53)) break;
@@ -1111,6 +1103,16 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         yph ^= 1;
         if (n + 1 < n1) load_v(n + 1);
         if (n + 2 < n1) load_kq(n + 2, cur);
+        // the gated outputs of chunk n-1 (formed during this chunk's products) out, the gate
+        // tile of chunk n in
+        if (n > n0) {
+          if (!mbar_wait(&bars[B_OUT], oph, 52)) break;
+          oph ^= 1;
+          tma_store_3d(&mg.out, sG, h * p.hd, (n - 1) * CT, b);
+          bulk_commit();
+          bulk_wait_read0();
+          load_g(n);
+        }
       }
       // outputs of the last chunk
       if (mbar_wait(&bars[B_OUT], oph, 56)) {
@@ -1185,22 +1187,75 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       fence_proxy_async_smem();
       return true;
     };
+    // y of the chunk whose GroupNorm * gate is pending, as bf16 pairs (it is stored as bf16)
+    uint32_t yp[2][EPW / 2];
+    // outputs of chunk m: GroupNorm(y) * sigmoid(gate) over the gate tile, with the
+    // GroupNorm partials every warp left in sRed[(m - n0) & 1]
+    auto gn_gate = [&](int m) -> bool {
+      if (!mbar_wait_warp(&bars[B_SYNC], (uint32_t)((m - n0) & 1), 61)) return false;
+      if (!mbar_wait_warp(&bars[B_G], gph, 62)) return false;
+      gph ^= 1;
+      const float2* red = sRed + (size_t)((m - n0) & 1) * (NWG * CT);
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        const int row = rb * RB + my_row;
+        float S1 = 0.f, S2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < NWG; ++w) {
+          const float2 v = red[w * CT + row];
+          S1 += v.x;
+          S2 += v.y;
+        }
+        const float mean = S1 * (1.f / 64.f);
+        const float var = fmaxf(S2 - S1 * mean, 0.f) * (1.f / 64.f);
+        const float inv = rsqrtf(var + 1e-5f);
+        const uint64_t mean2 = f2_make(mean, mean), inv2 = f2_make(inv, inv), half2 = f2_make(0.5f, 0.5f);
+#pragma unroll
+        for (int c = 0; c < EPW / 8; ++c) {
+          uint4* gs = reinterpret_cast<uint4*>(sG + sw128_chunk(row, (e0 >> 3) + c));
+          uint4 gv = *gs;
+          uint32_t* w = reinterpret_cast<uint32_t*>(&gv);
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const int d = e0 + c * 8 + e;
+            // ((y - mean) * inv) * w + b, then * sigmoid(g) = * (0.5 tanh(g / 2) + 0.5)
+            const float2 gw = *reinterpret_cast<const float2*>(&sGn[d]);
+            const float2 gb = *reinterpret_cast<const float2*>(&sGn[64 + d]);
+            const uint64_t ygn = f2_fma(f2_mul(f2_sub(bf2_to_f2(yp[rb][(c * 8 + e) / 2]), mean2), inv2),
+                                        f2_make(gw.x, gw.y), f2_make(gb.x, gb.y));
+            float tl, th;
+            f2_split(f2_mul(bf2_to_f2(w[e / 2]), half2), tl, th);
+            asm("tanh.approx.f32 %0, %0;" : "+f"(tl));
+            asm("tanh.approx.f32 %0, %0;" : "+f"(th));
+            w[e / 2] = f2_to_bf2(f2_mul(ygn, f2_fma(half2, f2_make(tl, th), half2)));
+          }
+          *gs = gv;
+        }
+      }
+      fence_proxy_async_smem();
+      warp_arrive(B_OUT);
+      return true;
+    };
 
     if (n0 < n1) {
       ok = prep(n0, 0);
-      fence_proxy_async_smem();
       tc_fence_before();
       warp_arrive(B_READY);
-      // warp 0's per-step table of chunk n0 is visible to every compute warp
-      warp_arrive(B_SYNC);
-      if (ok && !mbar_wait_warp(&bars[B_SYNC], 0, 63)) ok = false;
     }
-    uint32_t cph = 1;
+    // warp 0's per-step table of chunk n0 is visible to every compute warp (every compute
+    // warp passes this barrier exactly once)
+    if (PERSTEP) named_bar_sync(1, NTC);
     for (int n = n0; n < n1 && ok; ++n) {
       const int cur = (n - n0) & 1, nxt = cur ^ 1;
       uint8_t* K_ = sK(cur);
       uint8_t* Q_ = sQ(cur);
       const float* T = tab(cur);
+      // per-step: warp 0 wrote chunk n's table (in prep(n), before its arrival at the end of
+      // chunk n-1)
+      if (PERSTEP && n > n0 && !mbar_wait_warp(&bars[B_SYNC], (uint32_t)((n - 1 - n0) & 1), 63)) {
+        ok = false;
+        break;
+      }
       if (!mbar_wait_warp(&bars[B_S], sph, 58)) { ok = false; break; }
       sph ^= 1;
       tc_fence_after();
@@ -1285,32 +1340,35 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       }
       fence_proxy_async_smem();
       warp_arrive(B_KQ);
-      // meanwhile: the next chunk's phi
+      // during the products: the outputs of the previous chunk, then the next chunk's phi
+      if (n > n0 && !gn_gate(n - 1)) { ok = false; break; }
       if (n + 1 < n1 && !prep(n + 1, nxt)) { ok = false; break; }
       if (!mbar_wait_warp(&bars[B_Y], yph, 60)) { ok = false; break; }
       yph ^= 1;
       tc_fence_after();
-      // y = bf16(Y) (y_slot is bf16); GroupNorm partial sums
-      float o[2][EPW];
-      float yv2[2][EPW];
-      tmem_ld16x2(tL + YCOL + e0, tL + YCOL + 64 + e0, yv2[0], yv2[1]);  // both row blocks, one wait
+      // Y of both row blocks and U out of TMEM (one wait); then S(n+1) may overwrite them
+      float yv2[2][EPW], u[EPW];
+      tmem_ld16x3(tL + YCOL + e0, tL + YCOL + 64 + e0, tL + UCOL + e0, yv2[0], yv2[1], u);
+      tc_fence_before();
+      if (n + 1 < n1) warp_arrive(B_READY);
+      // y = bf16(Y) (y_slot is bf16), kept as bf16 pairs for the deferred GroupNorm; partials
+      float2* red = sRed + (size_t)cur * (NWG * CT);
 #pragma unroll
       for (int rb = 0; rb < 2; ++rb) {
-        const float* yv = yv2[rb];
         float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-        for (int e = 0; e < EPW; ++e) {
-          o[rb][e] = bf16_round(yv[e]);
-          s1 += o[rb][e];
-          s2 += o[rb][e] * o[rb][e];
+        for (int e = 0; e < EPW; e += 2) {
+          yp[rb][e / 2] = f2_to_bf2(f2_make(yv2[rb][e], yv2[rb][e + 1]));
+          float lo, hi;
+          f2_split(bf2_to_f2(yp[rb][e / 2]), lo, hi);
+          s1 += lo + hi;
+          s2 = fmaf(lo, lo, fmaf(hi, hi, s2));
         }
-        sRed[wg * CT + rb * RB + my_row] = make_float2(s1, s2);
+        red[wg * CT + rb * RB + my_row] = make_float2(s1, s2);
       }
-      // R <- gC R + U (fp32) -> sR (bf16) for the next chunk
+      // R <- gC R + U (fp32) -> sR (bf16) for the next chunk's Qs R (issued after KQ(n+1))
       {
         const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
-        float u[EPW];
-        tmem_ld16(tL + UCOL + e0, u);
 #pragma unroll
         for (int e = 0; e < EPW; ++e) Rr[e] = fmaf(Rr[e], gC, u[e]);
         if (f_valid) {
@@ -1320,54 +1378,10 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         }
       }
       fence_proxy_async_smem();
-      tc_fence_before();
-      if (n + 1 < n1) warp_arrive(B_READY);  // S(n+1) may overwrite U and P now
-      // the GroupNorm partials of every warp (and warp 0's per-step table) are in place
+      // this warp's GroupNorm partials of chunk n (and warp 0's table of chunk n+1) are in place
       warp_arrive(B_SYNC);
-      if (!mbar_wait_warp(&bars[B_SYNC], cph, 61)) { ok = false; break; }
-      cph ^= 1;
-      // outputs of chunk n: GroupNorm(y) * sigmoid(gate) over the gate tile
-      if (!mbar_wait_warp(&bars[B_G], gph, 62)) { ok = false; break; }
-      gph ^= 1;
-#pragma unroll
-      for (int rb = 0; rb < 2; ++rb) {
-        const int row = rb * RB + my_row;
-        float S1 = 0.f, S2 = 0.f;
-#pragma unroll
-        for (int w = 0; w < NWG; ++w) {
-          const float2 v = sRed[w * CT + row];
-          S1 += v.x;
-          S2 += v.y;
-        }
-        const float mean = S1 * (1.f / 64.f);
-        const float var = fmaxf(S2 - S1 * mean, 0.f) * (1.f / 64.f);
-        const float inv = rsqrtf(var + 1e-5f);
-        const uint64_t mean2 = f2_make(mean, mean), inv2 = f2_make(inv, inv), half2 = f2_make(0.5f, 0.5f);
-#pragma unroll
-        for (int c = 0; c < EPW / 8; ++c) {
-          uint4* gs = reinterpret_cast<uint4*>(sG + sw128_chunk(row, (e0 >> 3) + c));
-          uint4 gv = *gs;
-          uint32_t* w = reinterpret_cast<uint32_t*>(&gv);
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const int d = e0 + c * 8 + e;
-            // ((y - mean) * inv) * w + b, then * sigmoid(g) = * (0.5 tanh(g / 2) + 0.5)
-            const float2 gw = *reinterpret_cast<const float2*>(&sGn[d]);
-            const float2 gb = *reinterpret_cast<const float2*>(&sGn[64 + d]);
-            const uint64_t ygn = f2_fma(f2_mul(f2_sub(f2_make(o[rb][c * 8 + e], o[rb][c * 8 + e + 1]), mean2), inv2),
-                                        f2_make(gw.x, gw.y), f2_make(gb.x, gb.y));
-            float tl, th;
-            f2_split(f2_mul(bf2_to_f2(w[e / 2]), half2), tl, th);
-            asm("tanh.approx.f32 %0, %0;" : "+f"(tl));
-            asm("tanh.approx.f32 %0, %0;" : "+f"(th));
-            w[e / 2] = f2_to_bf2(f2_mul(ygn, f2_fma(half2, f2_make(tl, th), half2)));
-          }
-          *gs = gv;
-        }
-      }
-      fence_proxy_async_smem();
-      warp_arrive(B_OUT);
     }
+    if (ok && n0 < n1) ok = gn_gate(n1 - 1);
     if (ok && seg == p.nseg - 1 && p.state_out && f_valid) {
       float* dst = p.state_out + (size_t)bh * 4096 + f_row * 64 + e0;
 #pragma unroll

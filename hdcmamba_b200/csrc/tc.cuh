@@ -303,6 +303,32 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va,
     vb[i] = __uint_as_float(r[16 + i]);
   }
 }
+// Three 16-column TMEM loads (columns [a, a+16), [b, b+16), [c, c+16)) and one wait.
+__device__ __forceinline__ void tmem_ld16x3(uint32_t ta, uint32_t tb, uint32_t tc, float* va, float* vb, float* vc) {
+  uint32_t r[48];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%48];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%49];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47}, [%50];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
+      : "r"(ta), "r"(tb), "r"(tc)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(r[i]);
+    vb[i] = __uint_as_float(r[16 + i]);
+    vc[i] = __uint_as_float(r[32 + i]);
+  }
+}
 template <>
 __device__ __forceinline__ void tmem_ldn2<8>(uint32_t ta, uint32_t tb, float* va, float* vb) {
   tmem_ld8x2(ta, tb, va, vb);
