@@ -951,6 +951,11 @@ constexpr int TABN = CT + 4;
 // mbarriers
 enum { B_L0, B_L1, B_V, B_G, B_S, B_Y, B_READY, B_P, B_KQ, B_OUT, B_SYNC, NBAR };
 constexpr size_t SMEM = 1024 + 6 * TILE + 64 * 128 + 2 * TABN * 4 + 128 * 4 + 2 * CT * NWG * 8 + NBAR * 8 + 16;
+// Chunk row held by Q tile row r (and by TMEM lane r of row block 0's accumulators): row
+// block 0 arrives in 32-row blocks in reverse order, so every lane quarter holds one block of
+// row block 0 and one of row block 1 whose causal widths add up to the same total (P work
+// balanced over the warps).  Row block 1 is in order.
+__host__ __device__ constexpr int q_row(int r) { return r < RB ? (RB - 32) - (r & ~31) + (r & 31) : r; }
 // TMEM column of the packed P of piece c (row block 0: in place; row block 1: [384,512))
 __device__ __forceinline__ uint32_t pcol(int c) {
   return c < RB / PW ? (uint32_t)(c * PW) : (uint32_t)(P1COL + (c - RB / PW) * (PW / 2));
@@ -1027,7 +1032,10 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       auto load_kq = [&](int n, int st) {
         mbar_expect_tx(&bars[B_L0 + st], 2 * TILE);
         tma_load_3d(sK(st), &mapK, h * p.hd, n * CT, b, &bars[B_L0 + st]);
-        tma_load_3d(sQ(st), &mapQ, h * p.hd, n * CT, b, &bars[B_L0 + st]);
+        // Q in 32-row boxes; row block 0's blocks in reverse order (q_row)
+#pragma unroll
+        for (int j = 0; j < CT / 32; ++j)
+          tma_load_3d(sQ(st) + j * 32 * 128, &mapQ, h * p.hd, n * CT + q_row(j * 32), b, &bars[B_L0 + st]);
       };
       auto load_v = [&](int n) {
         mbar_expect_tx(&bars[B_V], TILE);
@@ -1125,50 +1133,9 @@ __global__ void __launch_bounds__(pipe::NT, 1)
   } else {
     // ------------------------------------------------------------ compute warps
     const uint32_t tL = tmem + ((uint32_t)(quarter * 32) << 16);  // this warp's TMEM lanes
-    // entering state: state_in, then earlier sequence parts, then the earlier segments'
-    // local states (lanes < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR
     float Rr[EPW];
 #pragma unroll
     for (int e = 0; e < EPW; ++e) Rr[e] = 0.f;
-    if (f_valid) {
-      if (p.state_in) {
-        const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + e0;
-#pragma unroll
-        for (int e = 0; e < EPW; ++e) Rr[e] = src[e];
-      }
-#pragma unroll 4
-      for (int s = 0; s < p.nprev; ++s) {
-        const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
-        const float4* src = reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride +
-                                                            (size_t)bh * 4096 + f_row * 64 + e0);
-#pragma unroll
-        for (int e = 0; e < EPW / 4; ++e) {
-          const float4 v = src[e];
-          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
-          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
-          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
-          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
-        }
-      }
-#pragma unroll 4
-      for (int s = 0; s < seg; ++s) {
-        const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
-        const float4* src =
-            reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
-#pragma unroll
-        for (int e = 0; e < EPW / 4; ++e) {
-          const float4 v = src[e];
-          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
-          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
-          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
-          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < EPW / 8; ++c)
-        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
-    }
-
     uint32_t lph0 = 0, lph1 = 0, sph = 0, yph = 0, gph = 0;
     bool ok = true;
     // one arrival per compute warp, after every lane's writes and fences
@@ -1212,7 +1179,7 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         const uint64_t mean2 = f2_make(mean, mean), inv2 = f2_make(inv, inv), half2 = f2_make(0.5f, 0.5f);
 #pragma unroll
         for (int c = 0; c < EPW / 8; ++c) {
-          uint4* gs = reinterpret_cast<uint4*>(sG + sw128_chunk(row, (e0 >> 3) + c));
+          uint4* gs = reinterpret_cast<uint4*>(sG + sw128_chunk(q_row(row), (e0 >> 3) + c));
           uint4 gv = *gs;
           uint32_t* w = reinterpret_cast<uint32_t*>(&gv);
 #pragma unroll
@@ -1242,6 +1209,50 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       tc_fence_before();
       warp_arrive(B_READY);
     }
+    // the entering state (read by the Qs R products of the first chunk, after its k~ / Qs)
+    // is folded while S(n0) runs
+    // state_in, then earlier sequence parts, then the earlier segments' local states (lanes
+    // < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR
+    if (f_valid) {
+      if (p.state_in) {
+        const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + e0;
+#pragma unroll
+        for (int e = 0; e < EPW; ++e) Rr[e] = src[e];
+      }
+#pragma unroll 4
+      for (int s = 0; s < p.nprev; ++s) {
+        const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
+        const float4* src = reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride +
+                                                            (size_t)bh * 4096 + f_row * 64 + e0);
+#pragma unroll
+        for (int e = 0; e < EPW / 4; ++e) {
+          const float4 v = src[e];
+          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+        }
+      }
+#pragma unroll 4
+      for (int s = 0; s < seg; ++s) {
+        const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+        const float4* src =
+            reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
+#pragma unroll
+        for (int e = 0; e < EPW / 4; ++e) {
+          const float4 v = src[e];
+          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < EPW / 8; ++c)
+        *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
+    }
+
+
     // warp 0's per-step table of chunk n0 is visible to every compute warp (every compute
     // warp passes this barrier exactly once)
     if (PERSTEP) named_bar_sync(1, NTC);
@@ -1262,19 +1273,19 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       // P = bf16(mask(S) decay) of this warpgroup's pieces -> TMEM (packed pairs)
 #pragma unroll
       for (int cc = 0; cc < CPW; ++cc) {
-        const int c = wg * CPW + cc;
+        const int c = cc * NWG + wg;      // pieces interleaved over the warpgroups
         const int rb = c * PW >= RB ? 1 : 0;
         const int j0 = c * PW - rb * RB;  // chunk position of the piece's first column
-        const int ib = rb * RB;           // chunk position of the block's first row
+        const int rlo = q_row(rb * RB + row_lo);  // chunk rows [rlo, rlo + 31] in this warp's lanes
         uint32_t pk[PW / 2];
-        if (j0 > ib + row_hi) {           // above the diagonal for every row of this warp
+        if (j0 > rlo + 31) {              // above the diagonal for every row of this warp
 #pragma unroll
           for (int q = 0; q < PW / 2; ++q) pk[q] = 0u;
         } else {
           float sv[PW];
           tmem_ldn<PW>(tL + c * PW, sv);
-          const int i = ib + my_row;
-          const bool full = j0 + PW - 1 <= ib + row_lo;  // no masking for any row of this warp
+          const int i = rlo + lane;
+          const bool full = j0 + PW - 1 <= rlo;  // no masking for any row of this warp
           const float ci = PERSTEP ? T[i] : 0.f;
 #pragma unroll
           for (int q = 0; q < PW / 8; ++q) {
@@ -1325,7 +1336,8 @@ __global__ void __launch_bounds__(pipe::NT, 1)
         for (int it = 0; it < IT; ++it) {
           const int idx = tid + it * NTC, row = idx >> 3;
           const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[row]) : T[CT - 1 - row];
-          const float qd = PERSTEP ? fast_exp(T[row]) : T[row];
+          const int qr = q_row(row);  // chunk row of Q tile row `row`
+          const float qd = PERSTEP ? fast_exp(T[qr]) : T[qr];
           const uint64_t kd2 = f2_make(kd, kd), qd2 = f2_make(qd, qd);
           uint32_t* wk = reinterpret_cast<uint32_t*>(&kv[it]);
           uint32_t* wq = reinterpret_cast<uint32_t*>(&qv[it]);
@@ -1523,9 +1535,11 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
         return e;
       if (int e = make_map(&mg.out, sp.y, W, sp.L, B, sp.y_st, B > 1 ? sp.y_sb : (int64_t)sp.L * sp.y_st, CT))
         return e;
+      CUtensorMap mq32;  // Q in 32-row boxes (row block 0 is loaded in permuted block order)
+      if (int e = make_map(&mq32, sp.q, W, sp.L, B, in_st, sb, 32)) return e;
       const size_t sm = pipe::SMEM;
       cudaFuncSetAttribute(slot_tc_pipe_kernel<PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      slot_tc_pipe_kernel<PS><<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq, mk, mv, mg, p);
+      slot_tc_pipe_kernel<PS><<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq32, mk, mv, mg, p);
       return launch_status("slot_tc_pipe_kernel");
     }
   }
