@@ -182,12 +182,19 @@ class SequenceParallel:
                 raise RuntimeError("the p2p transport runs whole models: use SequenceParallel.model / .lm")
             mb, lay = self._mb, self._lay
         # (1) halo: the last three input rows of rank r-1
+        side = self._side(h)
         if p2p:
             if self.rank < self.world - 1:
                 last3 = h[:, -3:, :]
                 if not last3.is_contiguous() or last3.data_ptr() % 16 or (last3.numel() * 2) % 16:
                     last3 = last3.contiguous()
-                mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])
+                if side is not None:  # off this rank's critical path: its LN + conv does not wait for it
+                    side.wait_stream(torch.cuda.current_stream(h.device))
+                    with torch.cuda.stream(side):
+                        mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])
+                    last3.record_stream(side)
+                else:
+                    mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])
             halo = None
             if self.rank > 0:
                 mb.wait(lay.halo_flag(layer), [0])
@@ -210,7 +217,6 @@ class SequenceParallel:
             flat = mb.view(lay.carries(layer, self.rank), (n,), torch.float32)
         else:
             flat = torch.empty(n, device=h.device, dtype=torch.float32)
-        side = self._side(h)
         if side is not None:  # the SSM kernels overlap the slot kernels on a second stream
             cur = torch.cuda.current_stream(h.device)
             side.wait_stream(cur)
