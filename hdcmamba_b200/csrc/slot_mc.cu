@@ -56,9 +56,11 @@ __global__ void __launch_bounds__(mc::NT, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cgrp = warp >> 2;
+  // piece `seg` of this (batch, head): chunks [seg * len, (seg + 1) * len), len = seg_len / a_split
   const int bh = blockIdx.x / p.nseg_a, seg = blockIdx.x - bh * p.nseg_a;
   const int b = bh / p.H, h = bh - b * p.H;
-  const int n0 = seg * p.seg_len, n1 = min(p.N, n0 + p.seg_len);
+  const int len = p.seg_len / p.a_split;
+  const int n0 = seg * len, n1 = min(p.N, n0 + len);
   const int ngroups = (n1 - n0) / G;
 
   if (warp == 0) {
@@ -166,11 +168,11 @@ __global__ void __launch_bounds__(mc::NT, 1)
   }
   if (ok && lane < 16) {
     const int f = quarter * 16 + lane;
-    float* dst = p.Rseg + ((size_t)bh * p.nseg + seg) * 4096 + f * 64 + cgrp * 16;
+    float* dst = p.Rseg + ((size_t)bh * p.nseg_a + seg) * 4096 + f * 64 + cgrp * 16;
 #pragma unroll
     for (int e = 0; e < 16; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(R[e], R[e + 1], R[e + 2], R[e + 3]);
   }
-  if (ok && tid == 0) p.Dseg[(size_t)bh * p.nseg + seg] = D;
+  if (ok && tid == 0) p.Dseg[(size_t)bh * p.nseg_a + seg] = D;
   // after a timed-out wait: let this CTA's own loads in flight land (bounded) before exit
   if (!ok && tid == 0) {
     if (pending & 1) mbar_wait(&bars[0], fph & 1u, 73);
@@ -256,8 +258,8 @@ __global__ void __launch_bounds__(mc::NT, 1)
     if (ngroups > 1) issue_kq(1, 1);
   }
 
-  // entering state: state_in, then the earlier segments' local states (fp32; lanes < 16 hold
-  // row f_row, columns [e0, e0 + 16))
+  // entering state: state_in, then the local states of pass A's pieces before this segment
+  // (fp32; lanes < 16 hold row f_row, columns [e0, e0 + 16))
   float Rr[16];
 #pragma unroll
   for (int e = 0; e < 16; ++e) Rr[e] = 0.f;
@@ -271,10 +273,10 @@ __global__ void __launch_bounds__(mc::NT, 1)
       }
     }
 #pragma unroll 4
-    for (int s = 0; s < seg; ++s) {
-      const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+    for (int s = 0; s < seg * p.a_split; ++s) {
+      const float Ds = p.Dseg[(size_t)bh * p.nseg_a + s];
       const float4* src =
-          reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
+          reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg_a + s) * 4096 + f_row * 64 + e0);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float4 v = src[e];
@@ -493,15 +495,25 @@ bool slot_mc_supported(const SlotParams& p) {
   return p.C == mc::CT && p.hd == 64 && p.rows == p.C && p.N % mc::G == 0;
 }
 
-// One CTA per SM (512 TMEM columns); segments of whole groups.
-void slot_mc_plan(int64_t BH, int N, int* nseg, int* seg_len) {
-  const int groups = N / mc::G;
-  int s = (int)(num_sms() / BH);
+// One CTA per SM (512 TMEM columns); segments of whole groups.  Pass A covers the segments
+// before the last one; when those are fewer than the SMs, each is split into a_split equal
+// pieces (a divisor of its group count) so that more CTAs share the state pass.
+void slot_mc_plan(int64_t BH, int N, int* nseg, int* seg_len, int* a_split) {
+  const int groups = N / mc::G, sms = num_sms();
+  int s = (int)(sms / BH);
   if (s < 1) s = 1;
   if (s > groups) s = groups;
   const int len = (groups + s - 1) / s;
   *seg_len = len * mc::G;
   *nseg = (groups + len - 1) / len;
+  int k = 1;
+  if (*nseg > 1) {
+    k = (int)(sms / (BH * (*nseg - 1)));
+    if (k < 1) k = 1;
+    if (k > len) k = len;
+    while (len % k != 0) --k;
+  }
+  *a_split = k;
 }
 
 int slot_mc_fwd(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s) {
@@ -510,9 +522,9 @@ int slot_mc_fwd(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, v
   p.gamma = sp.gamma; p.log_a = sp.log_a; p.y = sp.y; p.y_sb = sp.y_sb; p.y_sh = sp.y_sh; p.y_st = sp.y_st;
   p.state_in = sp.state_in; p.state_out = sp.state_out;
   p.L = sp.L; p.H = sp.H; p.hd = sp.hd; p.N = sp.N;
-  slot_mc_plan(BH, sp.N, &p.nseg, &p.seg_len);
+  slot_mc_plan(BH, sp.N, &p.nseg, &p.seg_len, &p.a_split);
   p.Rseg = static_cast<float*>(ws);
-  p.Dseg = p.Rseg + (size_t)BH * p.nseg * 4096;
+  p.Dseg = p.Rseg + (size_t)BH * (p.nseg - 1 > 0 ? (p.nseg - 1) * p.a_split : 1) * 4096;
   p.y_vec = (aligned16(sp.y) && sp.y_sb % 8 == 0 && sp.y_sh % 8 == 0 && sp.y_st % 8 == 0) ? 1 : 0;
   const int64_t W = (int64_t)sp.H * sp.hd;
   const int64_t sb = B > 1 ? in_sb : (int64_t)sp.L * in_st;
@@ -521,8 +533,8 @@ int slot_mc_fwd(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, v
   if (int e = slot_make_map(&mk, sp.k, W, sp.L, B, in_st, sb, mc::ROWS)) return e;
   if (int e = slot_make_map(&mv, sp.v, W, sp.L, B, in_st, sb, mc::ROWS)) return e;
   const bool ps = sp.log_a != nullptr;
+  p.nseg_a = (p.nseg - 1) * p.a_split;  // pass A's pieces per (batch, head)
   if (p.nseg > 1) {
-    p.nseg_a = p.nseg - 1;
     const unsigned grid = (unsigned)(BH * p.nseg_a);
     if (ps) {
       cudaFuncSetAttribute(slot_mc_state_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mc::SMEM_A);

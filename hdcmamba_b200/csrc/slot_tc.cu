@@ -1360,8 +1360,9 @@ size_t slot_tc_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C)
   int nseg, len;
   plan_segments(B * H, (int)(L / C), (int)C, &nseg, &len);
   if (C == 64 && (L / C) % 4 == 0) {  // the four-chunk kernels' plan (slot_mc.cu)
-    int nseg_mc, len_mc;
-    slot_mc_plan(B * H, (int)(L / C), &nseg_mc, &len_mc);
+    int nseg_mc, len_mc, split;
+    slot_mc_plan(B * H, (int)(L / C), &nseg_mc, &len_mc, &split);
+    nseg_mc *= split;  // pass A's pieces (the workspace holds one state per piece)
     nseg = nseg_mc > nseg ? nseg_mc : nseg;
   }
   return (size_t)(B * H) * nseg * (4096 + 1) * sizeof(float) + 256;

@@ -23,6 +23,9 @@ struct SlotTcParams {
   const void* gn_b;
   int L, H, hd, N, nseg, seg_len, y_vec;
   int nseg_a;  // segments computed by pass A (nseg - 1 before pass B; nseg for the state-only call)
+  // four-chunk kernels (slot_mc.cu): pass A splits each output segment but the last into
+  // a_split pieces of seg_len / a_split chunks, so that more CTAs share the state pass
+  int a_split;
   // states of earlier sequence parts (other ranks), folded first: part s has its state at
   // prev_R + s*prev_stride + bh*4096 and its decay product at prev_D + s*prev_stride + bh
   const float* prev_R;
@@ -139,7 +142,7 @@ int slot_make_map(CUtensorMap* m, const void* base, int64_t width, int64_t L, in
 // Chunk 64 with four chunks per CTA iteration (slot_mc.cu): plain outputs (no gate epilogue,
 // no earlier sequence parts), head_dim 64, a whole number of four-chunk groups.
 bool slot_mc_supported(const SlotParams& p);
-void slot_mc_plan(int64_t BH, int N, int* nseg, int* seg_len);
+void slot_mc_plan(int64_t BH, int N, int* nseg, int* seg_len, int* a_split);
 int slot_mc_fwd(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, void* ws, cudaStream_t s);
 
 }  // namespace hdc
