@@ -29,14 +29,22 @@ constexpr int CT = 64, G = 4, ROWS = CT * G, NT = 512;
 constexpr int TILE = ROWS * 128;  // one [256 x 64] bf16 tile, 128-byte swizzle
 constexpr int CHUNK = CT * 128;   // one chunk's rows inside a tile
 constexpr int TABN = CT + 4;      // one chunk's decay table (CT + 1 entries used)
-constexpr size_t SMEM_A = 1024 + 4 * TILE + G * TABN * 4 + 3 * 8 + 16;
-constexpr size_t SMEM_B = 1024 + 6 * TILE + G * TABN * 4 + 6 * 8 + 16;
+constexpr size_t SMEM_A = 1024 + 4 * TILE + 2 * G * TABN * 4 + 3 * 8 + 16;
+constexpr size_t SMEM_B = 1024 + 6 * TILE + 2 * G * TABN * 4 + 6 * 8 + 16;
 }  // namespace mc
 
-// Decay table of chunk n for this (b, h): per-step, c_i and the chunk decay exponent (warp
-// `x` of the first G warps fills table x); constant gamma, gamma^k for k <= CT (one table).
-__device__ __forceinline__ const float* mc_tab(const float* sTab, bool perstep, int x) {
-  return sTab + (perstep ? x * mc::TABN : 0);
+// Decay table of chunk x of group g for this (b, h): per-step, c_i and the chunk decay
+// exponent, in one of two buffers of G tables (warp x of the first G warps fills table x of
+// the next group while this one is processed); constant gamma, gamma^k for k <= CT (one table).
+__device__ __forceinline__ const float* mc_tab(const float* sTab, bool perstep, int g, int x) {
+  return sTab + (perstep ? ((g & 1) * mc::G + x) * mc::TABN : 0);
+}
+__device__ __forceinline__ float* mc_tab_w(float* sTab, int g, int x) {
+  return sTab + ((g & 1) * mc::G + x) * mc::TABN;
+}
+// log_a of chunk x of group g (rows n0 + G g + x), element (b, t, h) at (b L + t) H + h
+__device__ __forceinline__ const float* mc_log_a(const SlotTcParams& p, int b, int h, int n0, int g, int x) {
+  return p.log_a + ((size_t)b * p.L + (size_t)(n0 + g * mc::G + x) * mc::CT) * p.H + h;
 }
 
 // ---------------------------------------------------------------------------------
@@ -50,8 +58,8 @@ __global__ void __launch_bounds__(mc::NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   // stage st: K at base + 2 st TILE, V right after it
-  float* sTab = reinterpret_cast<float*>(base + 4 * TILE);   // [G][TABN]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + G * TABN);  // [0], [1] stage loads, [2] products
+  float* sTab = reinterpret_cast<float*>(base + 4 * TILE);          // [2][G][TABN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + 2 * G * TABN);  // [0], [1] stage loads, [2] products
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 3);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -102,19 +110,20 @@ __global__ void __launch_bounds__(mc::NT, 1)
     if (ngroups > 0) issue(0, 0);
     if (ngroups > 1) issue(1, 1);
   }
+  // per-step: tables of group 0 now; each later group's log_a is loaded a group ahead
+  float la_next[CT / 32];
+  if (PERSTEP) {
+    if (warp < G && ngroups > 0) chunk_cumlog_warp<CT>(mc_log_a(p, b, h, n0, 0, warp), p.H, mc_tab_w(sTab, 0, warp));
+    __syncthreads();
+  }
   for (int g = 0; g < ngroups; ++g) {
     const int st = g & 1;
     uint8_t* sK = base + st * 2 * TILE;
     uint8_t* sV = sK + TILE;
+    if (PERSTEP && warp < G && g + 1 < ngroups) chunk_cumlog_load<CT>(mc_log_a(p, b, h, n0, g + 1, warp), p.H, la_next);
     if (!mbar_wait_warp(&bars[st], (fph >> st) & 1u, 71)) { ok = false; break; }
     fph ^= 1u << st;
     if (tid == 0) pending &= ~(1 << st);
-    if (PERSTEP) {
-      if (warp < G)
-        chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)(n0 + g * G + warp) * CT) * p.H + h, p.H,
-                              sTab + warp * TABN);
-      __syncthreads();
-    }
     // k~ = bf16(bf16(phi(k)) kdec_j) in place, four 16-byte pieces per thread
     {
       uint4 kv[ROWS * 8 / NT];
@@ -123,7 +132,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
 #pragma unroll
       for (int it = 0; it < ROWS * 8 / NT; ++it) {
         const int idx = tid + it * NT, row = idx >> 3, x = row >> 6, i = row & (CT - 1);
-        const float* T = mc_tab(sTab, PERSTEP, x);
+        const float* T = mc_tab(sTab, PERSTEP, g, x);
         const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[i]) : T[CT - 1 - i];
         const uint64_t kd2 = f2_make(kd, kd);
         uint32_t* w = reinterpret_cast<uint32_t*>(&kv[it]);
@@ -155,12 +164,13 @@ __global__ void __launch_bounds__(mc::NT, 1)
     tmem_ld16x2(tU + 128 + cgrp * 16, tU + 192 + cgrp * 16, u[2], u[3]);
 #pragma unroll
     for (int x = 0; x < G; ++x) {
-      const float* T = mc_tab(sTab, PERSTEP, x);
+      const float* T = mc_tab(sTab, PERSTEP, g, x);
       const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
 #pragma unroll
       for (int e = 0; e < 16; ++e) R[e] = fmaf(R[e], gC, u[x][e]);
       D *= gC;
     }
+    if (PERSTEP && warp < G && g + 1 < ngroups) chunk_cumlog_regs<CT>(la_next, mc_tab_w(sTab, g + 1, warp));
     // every thread's TMEM and table reads are done before the next group's products / tables
     tc_fence_before();
     __syncthreads();
@@ -197,9 +207,9 @@ __global__ void __launch_bounds__(mc::NT, 1)
   // stage st: K at base + 2 st TILE, Q right after it; V at 4 TILE; P / R of the group at 5 TILE
   uint8_t* sV = base + 4 * TILE;
   uint8_t* sPR = base + 5 * TILE;
-  float* sTab = reinterpret_cast<float*>(base + 6 * TILE);       // [G][TABN]
+  float* sTab = reinterpret_cast<float*>(base + 6 * TILE);       // [2][G][TABN]
   // mbarriers: [0], [1] K + Q of a stage, [2] V, [3] S products, [4] U and P V, [5] Qs R
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + G * TABN);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sTab + 2 * G * TABN);
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + 6);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -290,16 +300,18 @@ __global__ void __launch_bounds__(mc::NT, 1)
 
   uint32_t kqph = 0, vph = 0, sph = 0, aph = 0, yph = 0;
   bool ok = true;
+  // per-step: tables of group 0 now (visible after the first barrier in the loop); each later
+  // group's log_a is loaded a group ahead
+  float la_next[CT / 32];
+  if (PERSTEP && warp < G && ngroups > 0) chunk_cumlog_warp<CT>(mc_log_a(p, b, h, n0, 0, warp), p.H, mc_tab_w(sTab, 0, warp));
   for (int g = 0; g < ngroups; ++g) {
     const int st = g & 1;
     uint8_t* sK = base + st * 2 * TILE;
     uint8_t* sQ = sK + TILE;
+    if (PERSTEP && warp < G && g + 1 < ngroups) chunk_cumlog_load<CT>(mc_log_a(p, b, h, n0, g + 1, warp), p.H, la_next);
     if (!mbar_wait_warp(&bars[st], (kqph >> st) & 1u, 74)) { ok = false; break; }
     kqph ^= 1u << st;
     if (tid == 0) pending &= ~(1 << st);
-    if (PERSTEP && warp < G)
-      chunk_cumlog_warp<CT>(p.log_a + ((size_t)b * p.L + (size_t)(n0 + g * G + warp) * CT) * p.H + h, p.H,
-                            sTab + warp * TABN);
     prep_tile_u<NT, ROWS, true>(sK, 64, 1.f);
     prep_tile_u<NT, ROWS, true>(sQ, 64, 1.f);
     fence_proxy_async_smem();
@@ -332,7 +344,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
 #pragma unroll
       for (int it = 0; it < IT; ++it) {
         const int idx = tid + it * NT, row = idx >> 3, x = row >> 6, i = row & (CT - 1);
-        const float* T = mc_tab(sTab, PERSTEP, x);
+        const float* T = mc_tab(sTab, PERSTEP, g, x);
         const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[i]) : T[CT - 1 - i];
         const float qd = PERSTEP ? fast_exp(T[i]) : T[i];
         const uint64_t kd2 = f2_make(kd, kd), qd2 = f2_make(qd, qd);
@@ -357,7 +369,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
         if (f_valid) {
 #pragma unroll
           for (int x = 0; x < G; ++x) {
-            const float* T = mc_tab(sTab, PERSTEP, x);
+            const float* T = mc_tab(sTab, PERSTEP, g, x);
             const float ci = PERSTEP ? T[i] : 0.f;
             float v[16];
 #pragma unroll
@@ -420,7 +432,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
           for (int c = 0; c < 2; ++c)
             *reinterpret_cast<uint4*>(sPR + x * CHUNK + sw128_chunk(f_row, (e0 >> 3) + c)) =
                 pack16<__nv_bfloat16>(&Rr[c * 8]);
-          const float* T = mc_tab(sTab, PERSTEP, x);
+          const float* T = mc_tab(sTab, PERSTEP, g, x);
           const float gC = PERSTEP ? fast_exp(T[CT]) : T[CT];
 #pragma unroll
           for (int e = 0; e < 16; ++e) Rr[e] = fmaf(Rr[e], gC, u[x][e]);
@@ -466,6 +478,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
         }
       }
     }
+    if (PERSTEP && warp < G && g + 1 < ngroups) chunk_cumlog_regs<CT>(la_next, mc_tab_w(sTab, g + 1, warp));
     // every thread's TMEM, table and tile reads are done before the next group's products
     tc_fence_before();
     __syncthreads();

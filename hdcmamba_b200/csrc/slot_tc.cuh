@@ -97,12 +97,24 @@ __device__ __forceinline__ void prep_tile_u(uint8_t* tile, int hd, float pad) {
 // sequential order of the CUDA-core kernel and of the oracle), so the decayed keys
 // bf16(phi(k) exp(c_{C-1} - c_j)) see the same c_j bits.
 template <int CT>
+__device__ __forceinline__ void chunk_cumlog_regs(const float* v, float* tab);
+template <int CT>
+__device__ __forceinline__ void chunk_cumlog_load(const float* la, int H, float* v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int e = 0; e < CT / 32; ++e) v[e] = la[(size_t)(e * 32 + lane) * H];
+}
+template <int CT>
 __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float* tab) {
+  float v[CT / 32];
+  chunk_cumlog_load<CT>(la, H, v);
+  chunk_cumlog_regs<CT>(v, tab);
+}
+// the same from log_a values already loaded by chunk_cumlog_load (row e * 32 + lane in v[e])
+template <int CT>
+__device__ __forceinline__ void chunk_cumlog_regs(const float* v, float* tab) {
   constexpr int E = CT / 32;
   const int lane = threadIdx.x & 31;
-  float v[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) v[e] = la[(size_t)(e * 32 + lane) * H];
 #pragma unroll
   for (int e = 0; e < E; ++e) tab[e * 32 + lane] = v[e];
   __syncwarp();
