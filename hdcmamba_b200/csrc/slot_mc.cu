@@ -300,20 +300,28 @@ __global__ void __launch_bounds__(mc::NT, 1)
 
   uint32_t kqph = 0, vph = 0, sph = 0, aph = 0, yph = 0;
   bool ok = true;
-  // per-step: tables of group 0 now (visible after the first barrier in the loop); each later
-  // group's log_a is loaded a group ahead
+  // phi of a stage's K and Q in place once its loads landed
+  auto prep_stage = [&](int st) -> bool {
+    if (!mbar_wait_warp(&bars[st], (kqph >> st) & 1u, 74)) return false;
+    kqph ^= 1u << st;
+    if (tid == 0) pending &= ~(1 << st);
+    prep_tile_u<NT, ROWS, true>(base + st * 2 * TILE, 64, 1.f);
+    prep_tile_u<NT, ROWS, true>(base + st * 2 * TILE + TILE, 64, 1.f);
+    return true;
+  };
+  // group 0: phi and (per-step) tables now; each later group's are formed while the previous
+  // group's U and P V products run, with its log_a loaded a group ahead
   float la_next[CT / 32];
-  if (PERSTEP && warp < G && ngroups > 0) chunk_cumlog_warp<CT>(mc_log_a(p, b, h, n0, 0, warp), p.H, mc_tab_w(sTab, 0, warp));
-  for (int g = 0; g < ngroups; ++g) {
+  if (ngroups > 0) {
+    if (PERSTEP && warp < G) chunk_cumlog_warp<CT>(mc_log_a(p, b, h, n0, 0, warp), p.H, mc_tab_w(sTab, 0, warp));
+    ok = prep_stage(0);
+  }
+  for (int g = 0; g < ngroups && ok; ++g) {
     const int st = g & 1;
     uint8_t* sK = base + st * 2 * TILE;
     uint8_t* sQ = sK + TILE;
     if (PERSTEP && warp < G && g + 1 < ngroups) chunk_cumlog_load<CT>(mc_log_a(p, b, h, n0, g + 1, warp), p.H, la_next);
-    if (!mbar_wait_warp(&bars[st], (kqph >> st) & 1u, 74)) { ok = false; break; }
-    kqph ^= 1u << st;
-    if (tid == 0) pending &= ~(1 << st);
-    prep_tile_u<NT, ROWS, true>(sK, 64, 1.f);
-    prep_tile_u<NT, ROWS, true>(sQ, 64, 1.f);
+    // phi(K), phi(Q) and the tables of this group are in place
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -415,6 +423,11 @@ __global__ void __launch_bounds__(mc::NT, 1)
       }
     }
     vph ^= 1;
+    // meanwhile: the next group's phi and tables (its stage's loads were issued a group ago)
+    if (g + 1 < ngroups) {
+      if (PERSTEP && warp < G) chunk_cumlog_regs<CT>(la_next, mc_tab_w(sTab, g + 1, warp));
+      if (!prep_stage(st ^ 1)) { ok = false; break; }
+    }
     if (!mbar_wait_warp(&bars[4], aph, 77)) { ok = false; break; }
     aph ^= 1;
     tc_fence_after();
@@ -457,28 +470,42 @@ __global__ void __launch_bounds__(mc::NT, 1)
     yph ^= 1;
     tc_fence_after();
     if (tid == 0 && g + 2 < ngroups) issue_kq(g + 2, st);  // this stage's K and Q are free
-    // ---- y = bf16(Y_x)
+    // ---- y = bf16(Y_x): staged in sPR (free after the Qs R products, 128-byte swizzled rows),
+    // then written out with 16-byte stores, eight threads per 128-byte row
     {
       float yv[G][16];
       tmem_ld16x2(tL + e0, tL + 128 + e0, yv[0], yv[1]);
       tmem_ld16x2(tL + 256 + e0, tL + 384 + e0, yv[2], yv[3]);
-      if (f_valid) {
+      if (p.y_vec) {
+        if (f_valid) {
+#pragma unroll
+          for (int x = 0; x < G; ++x)
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+              *reinterpret_cast<uint4*>(sPR + sw128_chunk(x * CT + f_row, (e0 >> 3) + c)) =
+                  pack16<__nv_bfloat16>(&yv[x][c * 8]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < ROWS * 8 / NT; ++it) {
+          const int idx = tid + it * NT, row = idx >> 3, c = idx & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(sPR + sw128_chunk(row, c));
+          const int t_row = (n0 + g * G) * CT + row;
+          stg16(static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh + (size_t)t_row * p.y_st +
+                    c * 8,
+                v);
+        }
+      } else if (f_valid) {
 #pragma unroll
         for (int x = 0; x < G; ++x) {
           const int t_row = (n0 + g * G + x) * CT + f_row;
           __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
                                 (size_t)t_row * p.y_st + e0;
-          if (p.y_vec) {
-            stg16(yrow, pack16<__nv_bfloat16>(&yv[x][0]));
-            stg16(yrow + 8, pack16<__nv_bfloat16>(&yv[x][8]));
-          } else {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) yrow[e] = __float2bfloat16_rn(yv[x][e]);
-          }
+          for (int e = 0; e < 16; ++e) yrow[e] = __float2bfloat16_rn(yv[x][e]);
         }
       }
     }
-    if (PERSTEP && warp < G && g + 1 < ngroups) chunk_cumlog_regs<CT>(la_next, mc_tab_w(sTab, g + 1, warp));
     // every thread's TMEM, table and tile reads are done before the next group's products
     tc_fence_before();
     __syncthreads();
