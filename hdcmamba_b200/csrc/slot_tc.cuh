@@ -93,57 +93,45 @@ __device__ __forceinline__ void prep_tile_u(uint8_t* tile, int hd, float pad) {
 
 // chunk-local cumulative log decay (per-step mode) by one warp:
 //   tab[i] = c_i = sum_{t=1..i} log_a[c0+t], tab[C] = c_{C-1} + log_a[c0] (chunk decay exponent)
-// The lanes stage log_a in tab, then lane 0 sums in row order, one fp32 add per row (the
-// sequential order of the CUDA-core kernel and of the oracle), so the decayed keys
-// bf16(phi(k) exp(c_{C-1} - c_j)) see the same c_j bits.
-template <int CT>
-__device__ __forceinline__ void chunk_cumlog_regs(const float* v, float* tab);
+// The sum runs in row order, one fp32 add per row (the sequential order of the CUDA-core kernel
+// and of the oracle), so the decayed keys bf16(phi(k) exp(c_{C-1} - c_j)) see the same c_j bits.
+// Every lane runs the same chain on values broadcast by shuffles (no shared-memory round trip
+// per row); lane 0 stores the results.
 template <int CT>
 __device__ __forceinline__ void chunk_cumlog_load(const float* la, int H, float* v) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int e = 0; e < CT / 32; ++e) v[e] = la[(size_t)(e * 32 + lane) * H];
 }
+// from log_a values loaded by chunk_cumlog_load (row e * 32 + lane in v[e] of each lane)
+template <int CT>
+__device__ __forceinline__ void chunk_cumlog_regs(const float* v, float* tab) {
+  const int lane = threadIdx.x & 31;
+  float run = 0.f;
+#pragma unroll
+  for (int blk = 0; blk < CT / 8; ++blk) {
+    float a[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) a[e] = __shfl_sync(0xffffffffu, v[(blk * 8 + e) / 32], (blk * 8 + e) % 32);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (blk > 0 || e > 0) run += a[e];
+      a[e] = run;
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tab[blk * 8 + e] = a[e];
+    }
+  }
+  const float a0 = __shfl_sync(0xffffffffu, v[0], 0);
+  if (lane == 0) tab[CT] = run + a0;
+  __syncwarp();
+}
 template <int CT>
 __device__ __forceinline__ void chunk_cumlog_warp(const float* la, int H, float* tab) {
   float v[CT / 32];
   chunk_cumlog_load<CT>(la, H, v);
   chunk_cumlog_regs<CT>(v, tab);
-}
-// the same from log_a values already loaded by chunk_cumlog_load (row e * 32 + lane in v[e])
-template <int CT>
-__device__ __forceinline__ void chunk_cumlog_regs(const float* v, float* tab) {
-  constexpr int E = CT / 32;
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int e = 0; e < E; ++e) tab[e * 32 + lane] = v[e];
-  __syncwarp();
-  if (lane == 0) {
-    // blocks of 8 rows; the next block's loads are issued before this block's stores, so
-    // only the fp32 add chain is serial
-    const float a0 = tab[0];
-    float run = 0.f, cur[8], nxt[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) cur[e] = tab[e];
-#pragma unroll 1
-    for (int blk = 0; blk < CT / 8; ++blk) {
-      if (blk + 1 < CT / 8) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) nxt[e] = tab[(blk + 1) * 8 + e];
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (blk > 0 || e > 0) run += cur[e];
-        cur[e] = run;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) tab[blk * 8 + e] = cur[e];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) cur[e] = nxt[e];
-    }
-    tab[CT] = run + a0;
-  }
-  __syncwarp();
 }
 
 // 3-D TMA map (columns, positions, batch) over bf16 rows: `width` columns, rows `row_stride`
