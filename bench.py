@@ -438,6 +438,57 @@ def run_reference(args, cfg, rank):
     }), flush=True)
 
 
+def run_timeline(args, cfg, world, rank, local):
+    """Per-op device timeline of the LM forward (hdcmamba_b200.trace), CUDA-graph replay.
+    One GPU: the config's model at L = 4096 (a sequence-parallel rank's length at 8 GPUs)
+    and at the config's length; under torchrun: the sequence-parallel forward, one line
+    per rank (rank 0 prints them all)."""
+    import dataclasses
+    from hdcmamba_b200.lm import build_lm, synthetic_ids
+    from hdcmamba_b200.trace import trace
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lm = build_lm(cfg).to(dev).bfloat16()
+    if world == 1:
+        for L in (4096, cfg.seq_len):
+            ids = synthetic_ids(dataclasses.replace(cfg, seq_len=L)).to(dev)
+
+            def fwd():
+                with torch.no_grad():
+                    return lm(ids)
+            for _ in range(args.warmup):
+                fwd()
+            torch.cuda.synchronize()
+            r = trace(fwd, dev, replays=args.steps)
+            print(json.dumps({"workload": f"timeline {cfg.name} B{cfg.batch} L{L}, 1 GPU", "rank": 0, **r}), flush=True)
+        return
+    import torch.distributed as dist
+    from datetime import timedelta
+    from hdcmamba_b200.sp import SequenceParallel
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    sp = SequenceParallel(transport=args.sp_transport)
+    Ls = cfg.seq_len // world
+    ids = synthetic_ids(cfg)[:, rank * Ls:(rank + 1) * Ls].contiguous().to(dev)
+
+    def fwd():
+        return sp.lm(lm, ids)
+    for _ in range(args.warmup):
+        fwd()
+    torch.cuda.synchronize()
+    dist.barrier()
+    r = trace(fwd, dev, replays=args.steps, before_replay=dist.barrier)
+    r = {"workload": f"timeline {cfg.name} B{cfg.batch} L{cfg.seq_len}, sp{world} ({args.sp_transport})",
+         "rank": rank, **r}
+    rows = [None] * world
+    dist.all_gather_object(rows, r)
+    if rank == 0:
+        for row in rows:
+            print(json.dumps(row), flush=True)
+    sp.close()
+    torch.cuda.synchronize()
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -455,8 +506,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernels", action="store_true", help="skip the config-2/3 kernel lines")
     ap.add_argument("--eager", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
-    ap.add_argument("--workload", default=None, choices=["c2", "c2bwd", "c3", "c5slot", "c5layer", "harness"],
-                    help="time one kernel workload alone (for profiling) and print its line")
+    ap.add_argument("--workload", default=None,
+                    choices=["c2", "c2bwd", "c3", "c5slot", "c5layer", "harness", "timeline"],
+                    help="time one kernel workload alone (for profiling) and print its line; timeline: "
+                         "per-op device times of the forward (hdcmamba_b200.trace), also under torchrun")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -468,6 +521,8 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, cfg, rank)
+    if args.workload == "timeline":
+        return run_timeline(args, cfg, world, rank, local)
     if args.workload:
         torch.cuda.set_device(local)
         dev = torch.device("cuda", local)

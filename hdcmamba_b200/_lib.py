@@ -75,6 +75,7 @@ SIGNATURES = {
     "hdc_peer_wait_for": (c_int, [c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint64, c_vp]),
     "hdc_peer_gen_bump": (c_int, [c_vp, c_vp]),
     "hdc_peer_barrier": (c_int, [c_vp, ctypes.c_uint64, c_int, c_int, c_vp, c_vp, c_vp]),
+    "hdc_trace_stamp": (c_int, [c_vp, ctypes.c_longlong, c_vp]),
 }
 
 _lib = None

@@ -420,10 +420,15 @@ __global__ void __launch_bounds__(512) ln_conv_bwd_staged_kernel(LnConvBwdParams
       }
       // phase 2: every warp finishes the sums itself (lane i < 8: value i over the warps);
       // xhat is recomputed from the staged row
+      // lane l adds value (l & 7) of warps 4 (l >> 3) .. +3; two xor levels join the four
+      // quarters, so lanes 0..7 (and their copies) hold the eight sums
       float S = 0.f;
-      if (lane < 8) {
-        S = red[half][lane][0];
-        for (int w = 1; w < nwarps; ++w) S += red[half][lane][w];
+      {
+        const int v = lane & 7, w0 = (lane >> 3) * 4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) S += (w0 + k < nwarps) ? red[half][v][w0 + k] : 0.f;
+        S += __shfl_xor_sync(0xffffffffu, S, 8);
+        S += __shfl_xor_sync(0xffffffffu, S, 16);
         S *= invD;
       }
 #pragma unroll

@@ -360,6 +360,15 @@ int hdc_peer_gen_bump(uint32_t* gen, hdc_stream_t stream);
 int hdc_peer_barrier(const uint64_t* base, uint64_t bar_off, int world, int rank,
                      const uint32_t* local_bar, const uint32_t* gen, hdc_stream_t stream);
 
+/*
+ * Tracing (no counterpart in the reference, which times whole forwards with
+ * time.perf_counter, benchmark.py:165-192): enqueue on `stream` a one-thread kernel that
+ * stores the device's %globaltimer (ns) into buf[index].  Stamps taken between the
+ * launches of a CUDA graph time each op on the device in stream order
+ * (hdcmamba_b200/trace.py).  buf: device array of at least index + 1 entries.
+ */
+int hdc_trace_stamp(unsigned long long* buf, long long index, hdc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
