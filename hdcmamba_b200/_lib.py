@@ -70,7 +70,7 @@ SIGNATURES = {
     "hdc_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
     "hdc_ipc_close": (c_int, [c_vp]),
     "hdc_peer_put": (c_int, [c_vp, c_size, c_vp, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32, c_int, c_vp,
-                             c_vp]),
+                             c_vp, c_vp]),
     "hdc_peer_wait": (c_int, [c_vp, ctypes.c_uint32, c_vp, c_vp]),
     "hdc_peer_wait_for": (c_int, [c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint64, c_vp]),
     "hdc_peer_gen_bump": (c_int, [c_vp, c_vp]),

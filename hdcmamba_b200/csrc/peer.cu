@@ -21,6 +21,7 @@
 //
 // Every wait gives up after ~2 s of %globaltimer, records an error code readable through
 // hdc_device_error() and returns, so a missing peer can not hang the GPU.
+#include <algorithm>
 #include <cstring>
 
 #include "tc.cuh"
@@ -58,32 +59,43 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, i
   return true;
 }
 
-// CTA t copies `bytes` from src to dst_base[t] + dst_off and then sets flag_base[t] +
-// flag_off to the generation; targets t with bit t of `mask` clear are skipped.
+// CTAs [kc t, kc t + kc) copy `bytes` from src to dst_base[t] + dst_off, one slice each;
+// the CTA that completes target t's last slice (counted in counters[t], zero between calls)
+// sets flag_base[t] + flag_off to the generation.  Targets t with bit t of `mask` clear are
+// skipped.  Ordering: every CTA's stores, its system-scope fence, then its count; the last
+// CTA's count, its fence, then the flag (fence - atomic / atomic - fence synchronisation),
+// so a consumer that acquires the flag sees every slice.
 __global__ void __launch_bounds__(512) peer_put_kernel(const uint4* src, size_t n16, const uint64_t* dst_base,
                                                        uint64_t dst_off, uint64_t flag_off, uint32_t mask,
-                                                       const uint32_t* gen) {
-  const int t = blockIdx.x;
+                                                       const uint32_t* gen, uint32_t* counters, int kc) {
+  const int t = blockIdx.x / kc, c = blockIdx.x - t * kc;
   if (!((mask >> t) & 1u)) return;
   uint4* dst = reinterpret_cast<uint4*>(dst_base[t] + dst_off);
+  const size_t lo = n16 * (size_t)c / kc, hi = n16 * (size_t)(c + 1) / kc;
   // eight loads in flight per thread before their stores
-  for (size_t i0 = 0; i0 < n16; i0 += 8 * (size_t)blockDim.x) {
+  for (size_t i0 = lo; i0 < hi; i0 += 8 * (size_t)blockDim.x) {
     uint4 v[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const size_t i = i0 + (size_t)k * blockDim.x + threadIdx.x;
-      if (i < n16) v[k] = src[i];
+      if (i < hi) v[k] = src[i];
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const size_t i = i0 + (size_t)k * blockDim.x + threadIdx.x;
-      if (i < n16) dst[i] = v[k];
+      if (i < hi) dst[i] = v[k];
     }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     fence_acq_rel_sys();
-    st_relaxed_sys(reinterpret_cast<uint32_t*>(dst_base[t] + flag_off), *gen);
+    if (kc == 1 || atomicAdd(&counters[t], 1u) == (uint32_t)(kc - 1)) {
+      if (kc > 1) {
+        counters[t] = 0;  // the next call on this counter array comes after this kernel
+        fence_acq_rel_sys();
+      }
+      st_relaxed_sys(reinterpret_cast<uint32_t*>(dst_base[t] + flag_off), *gen);
+    }
   }
 }
 
@@ -160,14 +172,17 @@ extern "C" int hdc_ipc_close(void* dev_ptr) {
 
 extern "C" int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_base, uint64_t dst_off,
                             uint64_t flag_off, uint32_t mask, int world, const uint32_t* gen,
-                            hdc_stream_t stream) {
-  if (!src || !dst_base || !gen) return fail(HDC_E_NULL, "peer_put: null pointer");
+                            uint32_t* counters, hdc_stream_t stream) {
+  if (!src || !dst_base || !gen || !counters) return fail(HDC_E_NULL, "peer_put: null pointer");
   if (world < 1 || world > 32) return fail(HDC_E_SHAPE, "peer_put: world %d (1..32)", world);
   if (bytes % 16 || !aligned16(src) || dst_off % 16 || flag_off % 4)
     return fail(HDC_E_ALIGN, "peer_put: src / dst must be 16-byte aligned and sizes multiples of 16");
   if (mask == 0) return 0;
-  peer_put_kernel<<<world, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(src), bytes / 16, dst_base, dst_off, flag_off, mask, gen);
+  // one CTA per 24 KB slice of a target's copy (at most 16): a single SM's peer stores do
+  // not fill an NVLink port
+  const int kc = (int)std::min<size_t>(16, std::max<size_t>(1, bytes / (24 * 1024)));
+  peer_put_kernel<<<world * kc, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), bytes / 16, dst_base, dst_off, flag_off, mask, gen, counters, kc);
   return launch_status("peer_put_kernel");
 }
 

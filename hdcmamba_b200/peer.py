@@ -67,6 +67,9 @@ class PeerMailbox:
                 bases.append(p.value)
             self.bases = torch.tensor(bases, dtype=torch.int64, device=self.device)
             self.gen = torch.zeros(1, dtype=torch.int32, device=self.device)
+            # per-target slice counters of hdc_peer_put, one array per put site that may run
+            # concurrently with another (``lane``)
+            self.counters = torch.zeros(4, self.world, dtype=torch.int32, device=self.device)
             self.buf = torch.as_tensor(_DeviceBytes(ptr.value, self.nbytes), device=self.device)
 
     def view(self, offset, shape, dtype):
@@ -77,9 +80,10 @@ class PeerMailbox:
         nb = n * torch.empty((), dtype=dtype).element_size()
         return self.buf[offset:offset + nb].view(dtype).view(*shape)
 
-    def put(self, src, dst_off, flag_off, targets):
+    def put(self, src, dst_off, flag_off, targets, lane=0):
         """Copy the contiguous tensor ``src`` to byte ``dst_off`` of the mailboxes of the
-        ranks in ``targets`` and raise their flag at byte ``flag_off``."""
+        ranks in ``targets`` and raise their flag at byte ``flag_off``.  Puts that can run at
+        the same time (on different streams) pass different ``lane`` s (0..3)."""
         mask = 0
         for t in targets:
             mask |= 1 << t
@@ -87,7 +91,8 @@ class PeerMailbox:
             return
         _lib.call("hdc_peer_put", ctypes.c_void_p(src.data_ptr()), src.numel() * src.element_size(),
                   ctypes.c_void_p(self.bases.data_ptr()), dst_off, flag_off, mask, self.world,
-                  ctypes.c_void_p(self.gen.data_ptr()), _stream(self.device))
+                  ctypes.c_void_p(self.gen.data_ptr()), ctypes.c_void_p(self.counters[lane].data_ptr()),
+                  _stream(self.device))
 
     def wait(self, flag_off, sources):
         """Wait until the uint32 flags at byte ``flag_off`` + 4*s (s in ``sources``) of the

@@ -191,7 +191,7 @@ class SequenceParallel:
                 if side is not None:  # off this rank's critical path: its LN + conv does not wait for it
                     side.wait_stream(torch.cuda.current_stream(h.device))
                     with torch.cuda.stream(side):
-                        mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])
+                        mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1], lane=1)
                     last3.record_stream(side)
                 else:
                     mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])

@@ -336,6 +336,10 @@ int hdc_slot_step(int dtype, const void* q, const void* k, const void* v, const 
  *   16-byte aligned) to dst_base[t] + dst_off, then store *gen (a device counter) as a
  *   uint32 flag at dst_base[t] + flag_off with release semantics at system scope.
  *   dst_base is a device array of `world` mailbox base addresses as mapped in this process.
+ *   The copy to each target is split over up to 16 CTAs (24 KB slices); `counters` is a
+ *   caller-owned device array of `world` uint32, zero before the call and left zero after it,
+ *   through which the CTA finishing a target's last slice raises its flag.  Puts that may
+ *   run concurrently (different streams) need separate counter arrays.
  * hdc_peer_wait: wait until flags[s] has reached *gen (wrap-safe >=) for every bit s of mask
  *   (acquire, system scope).
  * hdc_peer_wait_for: hdc_peer_wait with the caller's limit per flag (1 ns .. 2 s; HDC_E_SHAPE
@@ -352,7 +356,7 @@ int hdc_ipc_open(const void* handle, void** dev_ptr);
 int hdc_ipc_close(void* dev_ptr);
 int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_base, uint64_t dst_off,
                  uint64_t flag_off, uint32_t mask, int world, const uint32_t* gen,
-                 hdc_stream_t stream);
+                 uint32_t* counters, hdc_stream_t stream);
 int hdc_peer_wait(const uint32_t* flags, uint32_t mask, const uint32_t* gen, hdc_stream_t stream);
 int hdc_peer_wait_for(const uint32_t* flags, uint32_t mask, const uint32_t* gen, uint64_t timeout_ns,
                       hdc_stream_t stream);
