@@ -34,9 +34,9 @@ sys.path.insert(0, ROOT)
 MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "prefill tokens/sec at L=32768"
-# DRAM bytes (read + write) of one config-5 slot op (slot_tc_state + slot_tc_out) from an ncu
-# --set full capture of `bench.py --workload c5slot`
-SLOT_TRAFFIC_BYTES = 97.17e6 + 3.53e6 + 203.58e6 + 33.12e6
+# DRAM bytes (read + write) of one config-5 slot op (pass A + pass B) from an ncu --set full
+# capture of `bench.py --workload c5slot`
+SLOT_TRAFFIC_BYTES = 97.19e6 + 3.49e6 + 205.99e6 + 28.82e6
 
 
 def peaks():
@@ -715,8 +715,8 @@ def main():
                                        "batch": f"dp{world} (batch-sharded, no collective)"}[mode],
                        "launch": "eager" if args.eager else "cuda_graph",
                        "l2": "working set > L2 (projs 214 MB/layer, weights 153 MB): no explicit flush"},
-            "roofline": {"kernel": ("slot_state + slot_scan_gate_carry (slot_tc_state + slot_fold + slot_tc_out)"
-                                    if mode == "sp" else "slot_scan_gate (slot_tc_state + slot_tc_out)"), "bound": "hbm", "achieved": achieved, "peak": hbm,
+            "roofline": {"kernel": ("slot_state + slot_scan_gate_carry (slot_tc_state_pipe + slot_fold + slot_tc_pipe)"
+                                    if mode == "sp" else "slot_scan_gate (slot_tc_state_pipe + slot_tc_pipe)"), "bound": "hbm", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "peak_source": src,
                          "traffic": SLOT_TRAFFIC_BYTES * tokens_per_rank / (cfg.batch * cfg.seq_len),
                          "traffic_source": "ncu capture of the 1-GPU op" + (
