@@ -466,7 +466,7 @@ def run_timeline(args, cfg, world, rank, local):
     from datetime import timedelta
     from hdcmamba_b200.sp import SequenceParallel
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    sp = SequenceParallel(transport=args.sp_transport)
+    sp = SequenceParallel(transport=args.sp_transport, ssm_placement=args.sp_ssm)
     Ls = cfg.seq_len // world
     ids = synthetic_ids(cfg)[:, rank * Ls:(rank + 1) * Ls].contiguous().to(dev)
 
@@ -498,6 +498,9 @@ def main():
     ap.add_argument("--config", default="c5")
     ap.add_argument("--sp-transport", default="p2p", choices=["p2p", "nccl"],
                     help="sequence parallelism: peer stores into IPC-mapped mailboxes, or NCCL all-gathers")
+    ap.add_argument("--sp-ssm", default="side", choices=["side", "main"],
+                    help="sequence parallelism: the SSM kernels on a second stream next to the slot kernels, "
+                         "or after them on the main stream")
     ap.add_argument("--parallel", default="auto", choices=["auto", "sp", "batch"],
                     help="N > 1: batch = split the global batch over the ranks (no collective, config 4); "
                          "sp = split the sequence (config 5); auto = batch when the batch divides evenly")
@@ -569,7 +572,7 @@ def main():
         from hdcmamba_b200.sp import SequenceParallel
         if cfg.seq_len % (world * cfg.chunk_size) != 0:
             raise SystemExit(f"L={cfg.seq_len} does not split into {world} chunk-aligned segments")
-        sp = SequenceParallel(transport=args.sp_transport)
+        sp = SequenceParallel(transport=args.sp_transport, ssm_placement=args.sp_ssm)
         Ls = cfg.seq_len // world
         ids_host = synthetic_ids(cfg)[:, rank * Ls:(rank + 1) * Ls].contiguous().pin_memory()
 

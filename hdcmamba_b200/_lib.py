@@ -28,6 +28,8 @@ SIGNATURES = {
     "hdc_launch_count": (ctypes.c_longlong, []),
     "hdc_ln_conv_fwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                 c_i64, c_i64, c_i64, c_float, c_int, c_vp]),
+    "hdc_ln_conv_fwd_halo_flag": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                          c_i64, c_i64, c_i64, c_float, c_int, c_vp, c_vp, c_vp]),
     "hdc_ln_conv_bwd_workspace_bytes": (c_size, [c_i64, c_i64, c_i64]),
     "hdc_ln_conv_bwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size,
                                 c_i64, c_i64, c_i64, c_vp]),

@@ -25,13 +25,16 @@
 //   * the arithmetic runs on packed fp32 pairs (add / mul / fma .f32x2).
 #include <type_traits>
 
-#include "tc.cuh"
+#include "flag.cuh"
 
 namespace hdc {
 
 struct LnConvParams {
   const void* x; const void* nw; const void* nb; const void* cw; const void* cb;
   const void* halo; void* out; __nv_bfloat16* mean; __nv_bfloat16* rstd;
+  // sequence parallelism: the halo arrives from another GPU; the CTAs that read it wait
+  // (bounded) until *halo_flag reaches *halo_gen (nullptr: no wait)
+  const uint32_t* halo_flag; const uint32_t* halo_gen;
   int L, D, seg_len, segs_per_b, total_segs, nst;
   float eps; int act;
 };
@@ -182,6 +185,13 @@ __global__ void __launch_bounds__(512) ln_conv_kernel(LnConvParams p) {
   const bool pre_zero = (l0 == 0 && p.halo == nullptr);
   uint8_t* pre = ring + (size_t)(p.nst - 1) * stage_bytes;
   if (tid == 0) {
+    if (l0 == 0 && p.halo && p.halo_flag) {
+      // the peer's stores of the halo are visible once its flag is acquired; the bulk copy
+      // below reads them through the async proxy.  A timed-out wait records code 43 and the
+      // segment proceeds (the output is then invalid; hdc_device_error reports it).
+      wait_flag(p.halo_flag, *p.halo_gen, 43);
+      fence_proxy_async_global();
+    }
     if (!pre_zero) {
       const T* src = l0 > 0 ? x + (size_t)(l0 - 3) * p.D : static_cast<const T*>(p.halo) + (size_t)b * 3 * p.D;
       mbar_expect_tx(&bars[p.nst], (uint32_t)(3 * row_bytes));
@@ -393,10 +403,10 @@ static int ln_conv_dispatch(LnConvParams p, int64_t B, cudaStream_t stream) {
 
 using namespace hdc;
 
-extern "C" int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* norm_b,
-                               const void* conv_w, const void* conv_b, const void* halo, void* out,
-                               void* mean, void* rstd, int64_t B, int64_t L, int64_t D, float eps,
-                               int act, hdc_stream_t stream) {
+static int ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* norm_b, const void* conv_w,
+                       const void* conv_b, const void* halo, void* out, void* mean, void* rstd, int64_t B,
+                       int64_t L, int64_t D, float eps, int act, const uint32_t* halo_flag,
+                       const uint32_t* halo_gen, hdc_stream_t stream) {
   if (dtype != HDC_F32 && dtype != HDC_BF16) return fail(HDC_E_DTYPE, "ln_conv: dtype %d", dtype);
   if (!x || !norm_w || !norm_b || !conv_w || !conv_b || !out) return fail(HDC_E_NULL, "ln_conv: null pointer");
   if ((mean == nullptr) != (rstd == nullptr)) return fail(HDC_E_NULL, "ln_conv: mean and rstd go together");
@@ -413,6 +423,25 @@ extern "C" int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, con
   p.x = x; p.nw = norm_w; p.nb = norm_b; p.cw = conv_w; p.cb = conv_b; p.halo = halo; p.out = out;
   p.mean = static_cast<__nv_bfloat16*>(mean); p.rstd = static_cast<__nv_bfloat16*>(rstd);
   p.L = (int)L; p.D = (int)D; p.eps = eps; p.act = act;
+  p.halo_flag = halo_flag; p.halo_gen = halo_gen;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   return dtype == HDC_F32 ? ln_conv_dispatch<float>(p, B, s) : ln_conv_dispatch<__nv_bfloat16>(p, B, s);
+}
+
+extern "C" int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* norm_b,
+                               const void* conv_w, const void* conv_b, const void* halo, void* out,
+                               void* mean, void* rstd, int64_t B, int64_t L, int64_t D, float eps,
+                               int act, hdc_stream_t stream) {
+  return ln_conv_fwd(dtype, x, norm_w, norm_b, conv_w, conv_b, halo, out, mean, rstd, B, L, D, eps, act, nullptr,
+                     nullptr, stream);
+}
+
+extern "C" int hdc_ln_conv_fwd_halo_flag(int dtype, const void* x, const void* norm_w, const void* norm_b,
+                                         const void* conv_w, const void* conv_b, const void* halo, void* out,
+                                         void* mean, void* rstd, int64_t B, int64_t L, int64_t D, float eps,
+                                         int act, const uint32_t* halo_flag, const uint32_t* halo_gen,
+                                         hdc_stream_t stream) {
+  if (!halo || !halo_flag || !halo_gen) return fail(HDC_E_NULL, "ln_conv_halo_flag: halo, flag and gen required");
+  return ln_conv_fwd(dtype, x, norm_w, norm_b, conv_w, conv_b, halo, out, mean, rstd, B, L, D, eps, act, halo_flag,
+                     halo_gen, stream);
 }

@@ -134,14 +134,16 @@ class HdcMamba9v3Block(nn.Module):
         P = projs.shape[-1]
         if self.semantics == "fixed" and ops.slot_gate_supported(q, H, C):
             # SSM written into combined[..., :ds] on a side stream, concurrently with the slot
-            # scan (GroupNorm * sigmoid(gate) fused into its epilogue) into combined[..., ds:]
+            # scan (GroupNorm * sigmoid(gate) fused into its epilogue) into combined[..., ds:];
+            # the slot kernels are enqueued first, so their CTAs take the SMs first and the
+            # SSM's fill the SMs they leave
             cur = torch.cuda.current_stream(x.device)
             side = _side_stream(x.device)
             side.wait_stream(cur)
-            with torch.cuda.stream(side):
-                ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
             ops.slot_scan_gate(q, k, v, H, C, projs[..., so + 3 * dm:], self.group_norm.weight,
                                self.group_norm.bias, combined[..., ds:], (L * (ds + dm), hd, ds + dm), gamma=gamma)
+            with torch.cuda.stream(side):
+                ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])
             cur.wait_stream(side)
         elif self.semantics == "fixed":
             y_ssm = ops.ssm_scan(projs, self.A_log, ds, C, out=combined[..., :ds])

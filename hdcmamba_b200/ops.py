@@ -41,11 +41,13 @@ def _same_dtype(ref, *ts):
 
 
 # ------------------------------------------------------------------ LN + conv
-def ln_conv(x, norm_w, norm_b, conv_w, conv_b, eps=1e-5, act="none", halo=None, stats=False):
+def ln_conv(x, norm_w, norm_b, conv_w, conv_b, eps=1e-5, act="none", halo=None, stats=False, halo_flag=None):
     """LayerNorm + causal depthwise conv1d (width 4), optional SiLU.
 
     Replaces ``_fused_norm_conv_fwd_kernel`` (hdcmamba/model.py:22-72).
     x: [B, L, D]; conv_w: [D, 4] or [D, 1, 4]; halo: optional [B, 3, D].
+    halo_flag: optional (flag address, generation address) of device uint32s: the CTAs that
+    read the halo wait until the flag reaches the generation (a halo stored by another GPU).
     Returns out (and bf16 mean, rstd [B, L] if ``stats``)."""
     _cuda(x, norm_w, norm_b, conv_w, conv_b, halo)
     B, L, D = x.shape
@@ -63,8 +65,15 @@ def ln_conv(x, norm_w, norm_b, conv_w, conv_b, eps=1e-5, act="none", halo=None, 
         mean = torch.empty(B, L, device=x.device, dtype=torch.bfloat16)
         rstd = torch.empty(B, L, device=x.device, dtype=torch.bfloat16)
     a = {"none": _lib.HDC_ACT_NONE, "silu": _lib.HDC_ACT_SILU}[act]
-    _lib.call("hdc_ln_conv_fwd", _code(x), _p(x), _p(nw), _p(nb), _p(cw), _p(cb), _p(halo), _p(out),
-              _p(mean), _p(rstd), B, L, D, float(eps), a, _stream(x))
+    if halo_flag is not None:
+        if halo is None:
+            raise ValueError("halo_flag needs a halo")
+        _lib.call("hdc_ln_conv_fwd_halo_flag", _code(x), _p(x), _p(nw), _p(nb), _p(cw), _p(cb), _p(halo), _p(out),
+                  _p(mean), _p(rstd), B, L, D, float(eps), a, ctypes.c_void_p(halo_flag[0]),
+                  ctypes.c_void_p(halo_flag[1]), _stream(x))
+    else:
+        _lib.call("hdc_ln_conv_fwd", _code(x), _p(x), _p(nw), _p(nb), _p(cw), _p(cb), _p(halo), _p(out),
+                  _p(mean), _p(rstd), B, L, D, float(eps), a, _stream(x))
     return (out, mean, rstd) if stats else out
 
 

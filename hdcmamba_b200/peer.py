@@ -105,6 +105,11 @@ class PeerMailbox:
         _lib.call("hdc_peer_wait", ctypes.c_void_p(self._ptr.value + flag_off), mask,
                   ctypes.c_void_p(self.gen.data_ptr()), _stream(self.device))
 
+    def flag_address(self, flag_off):
+        """(address of the local uint32 flag at byte ``flag_off``, address of the generation
+        counter): for kernels that wait for the flag themselves."""
+        return self._ptr.value + flag_off, self.gen.data_ptr()
+
     def next_generation(self):
         _lib.call("hdc_peer_gen_bump", ctypes.c_void_p(self.gen.data_ptr()), _stream(self.device))
 

@@ -83,13 +83,18 @@ class _Mailboxes:
 class SequenceParallel:
     """Runs HdcMamba blocks / LMs on this rank's segment of the sequence."""
 
-    def __init__(self, group=None, kernels=None, transport="nccl", check_errors=False):
+    def __init__(self, group=None, kernels=None, transport="nccl", check_errors=False, ssm_placement="side"):
         """``check_errors``: after every forward, synchronise and raise HdcError if a bounded
         device wait (p2p halo / carry flags, the end-of-forward flag barrier, the kernels'
         mbarrier waits) gave up.  Off by default because it synchronises the stream (and
-        cannot run inside CUDA-graph capture); ``check()`` does the same on demand."""
+        cannot run inside CUDA-graph capture); ``check()`` does the same on demand.
+        ``ssm_placement``: "side" runs the SSM kernels on a second stream next to the slot
+        kernels, "main" after them on the current stream (see ``_pair``)."""
         if transport not in ("nccl", "p2p"):
             raise ValueError(f"transport {transport!r}: 'nccl' or 'p2p'")
+        if ssm_placement not in ("side", "main"):
+            raise ValueError(f"ssm_placement {ssm_placement!r}: 'side' or 'main'")
+        self.ssm_placement = ssm_placement
         self.check_errors = check_errors
         self.group = group
         self.rank = dist.get_rank(group)
@@ -164,6 +169,21 @@ class SequenceParallel:
         if self.check_errors:
             self.check()
 
+    def _pair(self, side, cur, slot_fn, ssm_fn):
+        """Run a slot kernel and the SSM kernel that does not depend on it.  "side": the SSM
+        on the side stream, enqueued after the slot kernel so that the slot kernel's CTAs take
+        their SMs first and the SSM fills the SMs they leave; "main": one after the other on
+        the current stream.  Both are complete when this returns (in stream order)."""
+        if side is None or self.ssm_placement == "main":
+            slot_fn()
+            ssm_fn()
+            return
+        side.wait_stream(cur)  # the SSM depends only on what precedes the slot kernel
+        slot_fn()
+        with torch.cuda.stream(side):
+            ssm_fn()
+        cur.wait_stream(side)
+
     def block(self, blk, h, layer=0):
         """One HdcMamba9v3Block on the local segment h [B, Ls, dm] (Ls a multiple of the
         chunk size; fixed semantics).  Returns the block output for the segment."""
@@ -183,27 +203,33 @@ class SequenceParallel:
             mb, lay = self._mb, self._lay
         # (1) halo: the last three input rows of rank r-1
         side = self._side(h)
+        halo_on_side = False
         if p2p:
             if self.rank < self.world - 1:
                 last3 = h[:, -3:, :]
                 if not last3.is_contiguous() or last3.data_ptr() % 16 or (last3.numel() * 2) % 16:
                     last3 = last3.contiguous()
                 if side is not None:  # off this rank's critical path: its LN + conv does not wait for it
+                    halo_on_side = True
                     side.wait_stream(torch.cuda.current_stream(h.device))
                     with torch.cuda.stream(side):
                         mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1], lane=1)
                     last3.record_stream(side)
                 else:
                     mb.put(last3, lay.halo(layer), lay.halo_flag(layer), [self.rank + 1])
-            halo = None
-            if self.rank > 0:
-                mb.wait(lay.halo_flag(layer), [0])
+            halo = halo_flag = None
+            if self.rank > 0:  # the LN+conv CTAs that read the halo wait for its flag themselves
                 halo = mb.view(lay.halo(layer), (B, 3, dm), h.dtype)
+                halo_flag = mb.flag_address(lay.halo_flag(layer))
         else:
             last3 = _all_gather(h[:, -3:, :], self.group)
             halo = last3[self.rank - 1] if self.rank > 0 else None
-        x_conv = K.ln_conv(h, blk.norm.weight, blk.norm.bias, blk.conv1d.weight.squeeze(1), blk.conv1d.bias,
-                           blk.norm.eps, halo=halo)
+            halo_flag = None
+        lnargs = (h, blk.norm.weight, blk.norm.bias, blk.conv1d.weight.squeeze(1), blk.conv1d.bias, blk.norm.eps)
+        if halo_flag is not None:
+            x_conv = K.ln_conv(*lnargs, halo=halo, halo_flag=halo_flag)
+        else:
+            x_conv = K.ln_conv(*lnargs, halo=halo)
         projs = F.linear(x_conv, blk.in_proj.weight, blk.in_proj.bias)
         so = 3 * ds
         q, k, v = projs[..., so:so + dm], projs[..., so + dm:so + 2 * dm], projs[..., so + 2 * dm:so + 3 * dm]
@@ -217,18 +243,16 @@ class SequenceParallel:
             flat = mb.view(lay.carries(layer, self.rank), (n,), torch.float32)
         else:
             flat = torch.empty(n, device=h.device, dtype=torch.float32)
-        if side is not None:  # the SSM kernels overlap the slot kernels on a second stream
-            cur = torch.cuda.current_stream(h.device)
-            side.wait_stream(cur)
-            with torch.cuda.stream(side):
-                K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
-        else:
-            K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
         ws = K.slot_workspace(B, Ls, H, hd, C, h.device)
-        K.slot_state(k, v, H, C, gamma=gamma, state_out=flat[n_st:n_st + n_sl].view(B, H, 64, 64),
-                     decay_out=flat[n_st + n_sl:n_st + n_sl + n_dc].view(B, H), workspace=ws)
-        if side is not None:
-            cur.wait_stream(side)  # the carries are complete before they are exchanged
+
+        def ssm_stats():
+            K.ssm_chunk_stats(projs, blk.A_log, ds, C, out=flat[:n_st].view(B, N, 2 * ds))
+
+        def slot_state():
+            K.slot_state(k, v, H, C, gamma=gamma, state_out=flat[n_st:n_st + n_sl].view(B, H, 64, 64),
+                         decay_out=flat[n_st + n_sl:n_st + n_sl + n_dc].view(B, H), workspace=ws)
+        cur = torch.cuda.current_stream(h.device) if side is not None else None
+        self._pair(side, cur, slot_state, ssm_stats)  # the carries are complete after this
         if p2p:  # to every higher rank; from every lower rank
             mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
                    range(self.rank + 1, self.world))
@@ -239,19 +263,16 @@ class SequenceParallel:
         combined = torch.empty(B, Ls, ds + dm, device=h.device, dtype=h.dtype)
         # SSM: exclusive prefix over the chunks of ranks < r, then this rank's, in place (on
         # the side stream, next to the slot output kernel)
-        if side is not None:
-            side.wait_stream(cur)
-            with torch.cuda.stream(side):
-                K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C,
-                                       out=combined[..., :ds])
-        else:
+        def ssm_out():
             K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C, out=combined[..., :ds])
-        # slot: fold the states of ranks < r in rank order, then the local segments
-        K.slot_scan_gate_carry(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias, combined[..., ds:],
-                               (Ls * (ds + dm), hd, ds + dm), g[n_st:], g[n_st + n_sl:], n, self.rank, ws,
-                               gamma=gamma)
-        if side is not None:
-            cur.wait_stream(side)
+
+        def slot_out():  # fold the states of ranks < r in rank order, then the local segments
+            K.slot_scan_gate_carry(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias,
+                                   combined[..., ds:], (Ls * (ds + dm), hd, ds + dm), g[n_st:], g[n_st + n_sl:], n,
+                                   self.rank, ws, gamma=gamma)
+        self._pair(side, cur, slot_out, ssm_out)
+        if halo_on_side:
+            cur.wait_stream(side)  # the halo put joins the layer (already joined by a side pair)
         combined = K.row_layernorm(combined, 1e-5, out=combined)
         return torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
 

@@ -11,7 +11,9 @@ captures one call of ``fn`` in a CUDA graph, replays it and returns:
 * ``gaps``: per pair of consecutive ops on the capturing stream, the mean time from the end
   stamp of the first to the start stamp of the second (waits for other streams or ranks,
   launch gaps);
-* ``total_us``: first to last stamp of the capturing stream.
+* ``total_us``: first to last stamp of the capturing stream;
+* ``sequence``: the first stamps of the last replay in time order, each with its stream
+  (how the side stream's ops overlap the main stream's).
 
 The stamps add one one-thread kernel per boundary, so the figures attribute time between
 ops; the benchmark figures come from untraced runs.
@@ -70,10 +72,11 @@ def _patch(stamps):
     return saved
 
 
-def trace(fn, device, replays=5, before_replay=None):
+def trace(fn, device, replays=5, before_replay=None, sequence_len=64):
     """Capture ``fn()`` with stamps in a CUDA graph (``fn`` must be capturable and already
     warmed up), replay it ``replays`` times (``before_replay()`` runs before each, e.g. a
-    barrier across ranks) and summarise the stamps."""
+    barrier across ranks) and summarise the stamps; ``sequence`` lists the first
+    ``sequence_len`` stamps of the last replay in time order with their stream."""
     stamps = _Stamps(device)
     g = torch.cuda.CUDAGraph()
     saved = _patch(stamps)
@@ -90,6 +93,7 @@ def trace(fn, device, replays=5, before_replay=None):
     gaps = collections.defaultdict(list)
     totals = []
     n = len(stamps.labels)
+    sequence = []
     for _ in range(replays):
         if before_replay is not None:
             before_replay()
@@ -111,9 +115,13 @@ def trace(fn, device, replays=5, before_replay=None):
                 prev = (label, ti)
         main_t = [ti for (label, s), ti in zip(stamps.labels, t) if s == main]
         totals.append((main_t[-1] - main_t[0]) / 1e3)
+        # the last replay's stamps in time order (us from the first), main / side stream
+        sequence = sorted(((ti - main_t[0]) / 1e3, label, "main" if s == main else "side")
+                          for (label, s), ti in zip(stamps.labels, t))
     del g
     return {
         "total_us": sum(totals) / len(totals),
         "ops": {k: {"us": round(sum(v) / len(v), 2), "per_replay": len(v) // replays} for k, v in durations.items()},
         "gaps": {k: {"us": round(sum(v) / len(v), 2), "per_replay": len(v) // replays} for k, v in gaps.items()},
+        "sequence": [(round(t, 2), label, stream) for t, label, stream in sequence[:sequence_len]],
     }

@@ -65,6 +65,18 @@ int hdc_ln_conv_fwd(int dtype, const void* x, const void* norm_w, const void* no
                     const void* conv_w, const void* conv_b, const void* halo, void* out,
                     void* mean, void* rstd, int64_t B, int64_t L, int64_t D, float eps, int act,
                     hdc_stream_t stream);
+/*
+ * hdc_ln_conv_fwd for a sequence-parallel segment whose halo arrives from another GPU (no
+ * single-launch counterpart in the reference, which has no sequence parallelism): the CTAs
+ * that read the halo first wait (bounded, acquire at system scope) until the uint32 *halo_flag
+ * reaches the generation *halo_gen, so no separate wait kernel precedes the launch.  halo,
+ * halo_flag and halo_gen are required.  A wait that times out records code 43 in
+ * hdc_device_error() and the kernel goes on (its output is then invalid).
+ */
+int hdc_ln_conv_fwd_halo_flag(int dtype, const void* x, const void* norm_w, const void* norm_b,
+                              const void* conv_w, const void* conv_b, const void* halo, void* out,
+                              void* mean, void* rstd, int64_t B, int64_t L, int64_t D, float eps, int act,
+                              const uint32_t* halo_flag, const uint32_t* halo_gen, hdc_stream_t stream);
 
 /*
  * Backward of hdc_ln_conv_fwd (no activation): the reference's
