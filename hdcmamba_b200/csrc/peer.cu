@@ -147,9 +147,10 @@ extern "C" int hdc_peer_put(const void* src, size_t bytes, const uint64_t* dst_b
   if (bytes % 16 || !aligned16(src) || dst_off % 16 || flag_off % 4)
     return fail(HDC_E_ALIGN, "peer_put: src / dst must be 16-byte aligned and sizes multiples of 16");
   if (mask == 0) return 0;
-  // one CTA per 24 KB slice of a target's copy (at most 16): a single SM's peer stores do
-  // not fill an NVLink port
-  const int kc = (int)std::min<size_t>(16, std::max<size_t>(1, bytes / (24 * 1024)));
+  // one CTA per 8 KB slice of a target's copy (at most 64): each CTA's stores, then its
+  // system-scope fence, run in parallel with the other slices' instead of one SM pushing
+  // the whole copy and then waiting for it
+  const int kc = (int)std::min<size_t>(64, std::max<size_t>(1, (bytes + 8191) / 8192));
   peer_put_kernel<<<world * kc, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), bytes / 16, dst_base, dst_off, flag_off, mask, gen, counters, kc);
   return launch_status("peer_put_kernel");

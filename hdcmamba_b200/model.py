@@ -39,6 +39,18 @@ def _side_stream(device):
     return st
 
 
+_EXCHANGE_STREAMS = {}
+
+
+def _exchange_stream(device):
+    """A third stream per device for sequence-parallel puts that no local kernel waits for."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _EXCHANGE_STREAMS.get(idx)
+    if st is None:
+        st = _EXCHANGE_STREAMS[idx] = torch.cuda.Stream(device=idx)
+    return st
+
+
 def _require_cuda(x):
     if not x.is_cuda:
         raise RuntimeError("hdcmamba_b200 runs on CUDA devices only; move the module and input to a B200")

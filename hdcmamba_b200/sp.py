@@ -253,9 +253,20 @@ class SequenceParallel:
                          decay_out=flat[n_st + n_sl:n_st + n_sl + n_dc].view(B, H), workspace=ws)
         cur = torch.cuda.current_stream(h.device) if side is not None else None
         self._pair(side, cur, slot_state, ssm_stats)  # the carries are complete after this
+        exch = None
         if p2p:  # to every higher rank; from every lower rank
-            mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
-                   range(self.rank + 1, self.world))
+            if side is not None and self.rank + 1 < self.world:
+                # no local kernel reads the peers' copies: the put runs on its own stream, off
+                # this rank's critical path (joined at the end of the layer)
+                from .model import _exchange_stream
+                exch = _exchange_stream(h.device)
+                exch.wait_stream(cur)
+                with torch.cuda.stream(exch):
+                    mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
+                           range(self.rank + 1, self.world), lane=2)
+            else:
+                mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
+                       range(self.rank + 1, self.world))
             mb.wait(lay.carry_flags(layer), range(self.rank))
             g = mb.view(lay.carries(layer), (self.world * n,), torch.float32)  # [W * n], rank-major
         else:
@@ -274,7 +285,10 @@ class SequenceParallel:
         if halo_on_side:
             cur.wait_stream(side)  # the halo put joins the layer (already joined by a side pair)
         combined = K.row_layernorm(combined, 1e-5, out=combined)
-        return torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
+        out = torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
+        if exch is not None:
+            cur.wait_stream(exch)  # the carry put joins the layer
+        return out
 
     def model(self, model, h):
         """HdcMamba9v3Model.forward on the local segment (hdcmamba/model.py:402-404)."""

@@ -348,7 +348,7 @@ int hdc_slot_step(int dtype, const void* q, const void* k, const void* v, const 
  *   16-byte aligned) to dst_base[t] + dst_off, then store *gen (a device counter) as a
  *   uint32 flag at dst_base[t] + flag_off with release semantics at system scope.
  *   dst_base is a device array of `world` mailbox base addresses as mapped in this process.
- *   The copy to each target is split over up to 16 CTAs (24 KB slices); `counters` is a
+ *   The copy to each target is split over up to 64 CTAs (8 KB slices); `counters` is a
  *   caller-owned device array of `world` uint32, zero before the call and left zero after it,
  *   through which the CTA finishing a target's last slice raises its flag.  Puts that may
  *   run concurrently (different streams) need separate counter arrays.
