@@ -37,7 +37,8 @@ SIGNATURES = {
     "hdc_ssm_scan_out": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64,
                                  c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_ssm_scan_out_blocked": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp,
-                                         c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
+                                         c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, ctypes.c_uint32, c_vp,
+                                         c_vp]),
     "hdc_ssm_scan_fwd_noalloc": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
                                          c_i64, c_vp]),
     "hdc_ssm_noalloc_capacity": (c_i64, []),
@@ -51,7 +52,7 @@ SIGNATURES = {
                                    c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_slot_gate_carry_fwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp,
                                         c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_size,
-                                        c_i64, c_i64, c_i64, c_i64, c_i64, c_vp]),
+                                        c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, ctypes.c_uint32, c_vp, c_vp]),
     "hdc_slot_scan_fwd_path": (c_int, [c_int, c_vp, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64,
                                        c_i64, c_vp, c_vp, c_vp, c_size, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                        c_int, ctypes.POINTER(c_int), c_vp]),

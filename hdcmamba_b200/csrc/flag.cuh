@@ -45,9 +45,24 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, i
 __device__ __forceinline__ bool wait_flags(const uint32_t* flags, uint32_t mask, const uint32_t* gen, int code) {
   const uint32_t g = *gen;
   bool ok = true;
-  for (int s = 0; s < 32; ++s)
-    if ((mask >> s) & 1u) ok = wait_flag(flags + s, g, code) && ok;
+#pragma unroll 1
+  for (uint32_t m = mask; m != 0; m &= m - 1) ok = wait_flag(flags + (__ffs(m) - 1), g, code) && ok;
   return ok;
+}
+
+// After a wait that another thread finished: this thread acquires every flag of mask itself,
+// so its later loads of the guarded data are ordered after the producer's stores.
+__device__ __forceinline__ void acquire_flags(const uint32_t* flags, uint32_t mask) {
+#pragma unroll 1
+  for (uint32_t m = mask; m != 0; m &= m - 1) (void)ld_acquire_sys(flags + (__ffs(m) - 1));
+}
+
+// CTA-wide wait: thread 0 waits (bounded) for every flag of mask to reach *gen, the CTA
+// synchronises, and every thread acquires the flags.  All threads of the CTA call it.
+__device__ __forceinline__ void cta_wait_flags(const uint32_t* flags, uint32_t mask, const uint32_t* gen, int code) {
+  if (threadIdx.x == 0) wait_flags(flags, mask, gen, code);
+  __syncthreads();
+  acquire_flags(flags, mask);
 }
 
 }  // namespace hdc

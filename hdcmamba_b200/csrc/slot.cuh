@@ -33,6 +33,8 @@ __device__ __forceinline__ float trnd(float v) { return store_round<T>(v); }
 // (fp32 [B*H]).
 struct SlotCarry {
   const float* prev_R; const float* prev_D; int64_t prev_stride; int nprev;
+  // flags guarding prev_R / prev_D when they arrive from other GPUs (mask 0: no wait)
+  const uint32_t* wait_flags; uint32_t wait_mask; const uint32_t* wait_gen;
 };
 
 size_t slot_simt_workspace(int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C);

@@ -97,7 +97,9 @@ extern "C" int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, 
                                        const float* prev_state, const float* prev_decay, int64_t prev_stride,
                                        int64_t n_prev, float* state_out, void* workspace, size_t workspace_bytes,
                                        int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C,
+                                       const uint32_t* wait_flags, uint32_t wait_mask, const uint32_t* wait_gen,
                                        hdc_stream_t stream) {
+  if (wait_mask && (!wait_flags || !wait_gen)) return fail(HDC_E_NULL, "slot_gate_carry: wait_mask needs flags and gen");
   if (dtype != HDC_BF16) return fail(HDC_E_DTYPE, "slot_gate_carry: bf16 activations only");
   if (n_prev < 0 || (n_prev > 0 && (!prev_state || !prev_decay)))
     return fail(HDC_E_NULL, "slot_gate_carry: n_prev=%lld needs prev_state / prev_decay", (long long)n_prev);
@@ -105,7 +107,7 @@ extern "C" int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, 
     return fail(HDC_E_SHAPE, "slot_gate_carry: prev_stride %lld < B*H*4096", (long long)prev_stride);
   if (n_prev > 0 && (!aligned16(prev_state) || prev_stride % 4 != 0))
     return fail(HDC_E_ALIGN, "slot_gate_carry: prev_state must be 16-byte aligned, prev_stride a multiple of 4");
-  const SlotCarry cy{prev_state, prev_decay, prev_stride, (int)n_prev};
+  const SlotCarry cy{prev_state, prev_decay, prev_stride, (int)n_prev, wait_flags, wait_mask, wait_gen};
   return slot_gate_common("slot_gate_carry", q, k, v, in_sb, in_st, gamma, log_a, gate, gate_sb, gate_st, gn_w,
                           gn_b, out, out_sb, out_sh, out_st, nullptr, state_out, workspace, workspace_bytes, B, L,
                           H, hd, C, &cy, reinterpret_cast<cudaStream_t>(stream));

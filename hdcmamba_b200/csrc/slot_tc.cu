@@ -447,7 +447,8 @@ __global__ void __launch_bounds__(OutCfg<CT>::NT, OutCfg<CT>::MINB)
 
   // entering state: state_in, then earlier sequence parts, then the earlier segments'
   // local states, folded -> registers (fp32 R: lanes < 16 hold row f_row, columns
-  // [e0, e0 + EPW)) + sR (bf16)
+  // [e0, e0 + EPW)) + sR (bf16); earlier parts from other GPUs were waited for by
+  // slot_wait_kernel before this launch
   float Rr[EPW];
 #pragma unroll
   for (int pc = 0; pc < EPW / AG; ++pc) {
@@ -843,7 +844,9 @@ struct SlotPipeMaps {
   CUtensorMap gate, out;
 };
 
-template <bool PERSTEP>
+// LATE: the earlier sequence parts' states arrive from other GPUs behind wait flags (a
+// separate instantiation, so the single-GPU kernel keeps its register allocation)
+template <bool PERSTEP, bool LATE>
 __global__ void __launch_bounds__(pipe::NT, 1)
     slot_tc_pipe_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                         const __grid_constant__ CUtensorMap mapV, const __grid_constant__ SlotPipeMaps mg,
@@ -1088,8 +1091,31 @@ __global__ void __launch_bounds__(pipe::NT, 1)
     // the entering state (read by the Qs R products of the first chunk, after its k~ / Qs)
     // is folded while S(n0) runs
     // state_in, then earlier sequence parts, then the earlier segments' local states (lanes
-    // < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR
-    if (f_valid) {
+    // < 16 hold row f_row, columns [e0, e0 + 16)) -> registers + sR.  When the earlier parts
+    // arrive from other GPUs (wait flags), only this segment's predecessors are folded here
+    // (Rr, with the product of their decays in Dloc); the parts are waited for and folded in
+    // after the first chunk's P, R = Dloc R_parts + Rr, so the wait overlaps this CTA's
+    // prologue, the first loads, phi, S and P.
+    constexpr bool late = LATE;
+    float Dloc = 1.f;
+    if (f_valid && late) {
+#pragma unroll 4
+      for (int s = 0; s < seg; ++s) {
+        const float Ds = p.Dseg[(size_t)bh * p.nseg + s];
+        const float4* src =
+            reinterpret_cast<const float4*>(p.Rseg + ((size_t)bh * p.nseg + s) * 4096 + f_row * 64 + e0);
+#pragma unroll
+        for (int e = 0; e < EPW / 4; ++e) {
+          const float4 v = src[e];
+          Rr[4 * e] = Ds * Rr[4 * e] + v.x;
+          Rr[4 * e + 1] = Ds * Rr[4 * e + 1] + v.y;
+          Rr[4 * e + 2] = Ds * Rr[4 * e + 2] + v.z;
+          Rr[4 * e + 3] = Ds * Rr[4 * e + 3] + v.w;
+        }
+        Dloc *= Ds;
+      }
+    }
+    if (f_valid && !late) {
       if (p.state_in) {
         const float* src = p.state_in + (size_t)bh * 4096 + f_row * 64 + e0;
 #pragma unroll
@@ -1198,6 +1224,34 @@ __global__ void __launch_bounds__(pipe::NT, 1)
       tmem_wait_st();
       tc_fence_before();
       warp_arrive(B_P);
+      if constexpr (late) if (n == n0) {
+        // the earlier parts' states from the peers: wait, then R = Dloc R_parts + Rr -> sR
+        if (lane == 0) wait_flags(p.wait_flags, p.wait_mask, p.wait_gen, 44);
+        __syncwarp();
+        acquire_flags(p.wait_flags, p.wait_mask);
+        if (f_valid) {
+          // four columns at a time (few live registers): state_in, then the parts in order
+#pragma unroll
+          for (int e = 0; e < EPW / 4; ++e) {
+            float4 q4 = p.state_in ? *reinterpret_cast<const float4*>(p.state_in + (size_t)bh * 4096 + f_row * 64 + e0 + 4 * e)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+            for (int s = 0; s < p.nprev; ++s) {
+              const float Ds = p.prev_D[(size_t)s * p.prev_stride + bh];
+              const float4 v = *reinterpret_cast<const float4*>(p.prev_R + (size_t)s * p.prev_stride + (size_t)bh * 4096 +
+                                                                f_row * 64 + e0 + 4 * e);
+              q4 = make_float4(Ds * q4.x + v.x, Ds * q4.y + v.y, Ds * q4.z + v.z, Ds * q4.w + v.w);
+            }
+            Rr[4 * e] = fmaf(Dloc, q4.x, Rr[4 * e]);
+            Rr[4 * e + 1] = fmaf(Dloc, q4.y, Rr[4 * e + 1]);
+            Rr[4 * e + 2] = fmaf(Dloc, q4.z, Rr[4 * e + 2]);
+            Rr[4 * e + 3] = fmaf(Dloc, q4.w, Rr[4 * e + 3]);
+          }
+#pragma unroll
+          for (int c = 0; c < EPW / 8; ++c)
+            *reinterpret_cast<uint4*>(sR + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&Rr[c * 8]);
+        }
+      }
       // the P V products run while k~ and Qs are formed
       // k~ = bf16(phi(k) kdec_j) and Qs = bf16(phi(q) qdec_i) in place (S(n) has read them)
       {
@@ -1378,6 +1432,12 @@ bool slot_tc_supported(const SlotParams& p, int64_t B, int64_t in_sb, int64_t in
   return true;
 }
 
+// Lane s waits (bounded) for flags[s] to reach *gen, for every bit s of mask.
+__global__ void slot_wait_kernel(const uint32_t* flags, uint32_t mask, const uint32_t* gen) {
+  const int s = threadIdx.x;
+  if ((mask >> s) & 1u) wait_flag(flags + s, *gen, 44);
+}
+
 template <int CT, bool PS, bool GATE>
 static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* carry, int64_t B, int64_t in_sb,
                   int64_t in_st, void* ws, cudaStream_t s) {
@@ -1405,6 +1465,7 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
   if (int e = make_map(&mv, sp.v, W, sp.L, B, in_st, sb, CT)) return e;
   if (carry) {
     p.prev_R = carry->prev_R; p.prev_D = carry->prev_D; p.prev_stride = carry->prev_stride; p.nprev = carry->nprev;
+    p.wait_flags = carry->wait_flags; p.wait_mask = carry->wait_mask; p.wait_gen = carry->wait_gen;
   }
   // with a carry the workspace already holds every segment's state (hdc_slot_state_fwd)
   if (p.nseg > 1 && !carry) {
@@ -1427,10 +1488,18 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
       CUtensorMap mq32;  // Q in 32-row boxes (row block 0 is loaded in permuted block order)
       if (int e = make_map(&mq32, sp.q, W, sp.L, B, in_st, sb, 32)) return e;
       const size_t sm = pipe::SMEM;
-      cudaFuncSetAttribute(slot_tc_pipe_kernel<PS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      slot_tc_pipe_kernel<PS><<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq32, mk, mv, mg, p);
+      auto go = [&](auto kernel) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        kernel<<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq32, mk, mv, mg, p);
+      };
+      if (p.wait_mask) go(slot_tc_pipe_kernel<PS, true>);
+      else go(slot_tc_pipe_kernel<PS, false>);
       return launch_status("slot_tc_pipe_kernel");
     }
+  }
+  if (p.wait_mask) {  // the lock-step kernel reads the earlier parts at its start: wait first
+    slot_wait_kernel<<<1, 32, 0, s>>>(p.wait_flags, p.wait_mask, p.wait_gen);
+    if (int e = launch_status("slot_wait_kernel")) return e;
   }
   const size_t sm = smem_out_bytes<CT>();
   cudaFuncSetAttribute(slot_tc_out_kernel<CT, PS, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);

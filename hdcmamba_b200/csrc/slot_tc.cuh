@@ -3,7 +3,7 @@
 #include <cuda.h>
 
 #include "slot.cuh"
-#include "tc.cuh"
+#include "flag.cuh"
 
 namespace hdc {
 
@@ -32,6 +32,11 @@ struct SlotTcParams {
   const float* prev_D;
   int64_t prev_stride;
   int nprev;
+  // the earlier parts' states arrive from other GPUs: the kernel waits (bounded) until every
+  // flag s of wait_mask at wait_flags reaches *wait_gen before it reads them (mask 0: no wait)
+  const uint32_t* wait_flags;
+  uint32_t wait_mask;
+  const uint32_t* wait_gen;
 };
 
 // Advance the dynamic shared-memory base to a 1024-byte boundary of its shared-space address

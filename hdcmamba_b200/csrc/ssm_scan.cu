@@ -23,7 +23,7 @@
 #include <climits>
 #include <type_traits>
 
-#include "common.cuh"
+#include "flag.cuh"
 
 namespace hdc {
 
@@ -35,6 +35,9 @@ struct SsmParams {
   // rank-major layout of gathered per-rank statistics); blk = INT_MAX: one block
   int blk; int64_t blk_stride;
   void* y; int64_t ysb, yst;
+  // statistics of earlier sequence parts arriving from other GPUs: the output kernel waits
+  // (bounded) until every flag s of wait_mask reaches *wait_gen before it reads them
+  const uint32_t* wait_flags; uint32_t wait_mask; const uint32_t* wait_gen;
   int L, ds, C, S;
   int CG;   // channels per CTA (kCG; grid.y = ds / kCG channel groups)
   int vec;  // 16-byte loads of the staged columns are aligned
@@ -149,6 +152,7 @@ __global__ void __launch_bounds__(256) ssm_scan_out_kernel(SsmParams p) {
   const int jl = threadIdx.x % kCG, s = threadIdx.x / kCG, j = g * kCG + jl;
   const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[j]));
   ssm_stage<T>(p, b, n, g, tile);
+  if (p.wait_mask) cta_wait_flags(p.wait_flags, p.wait_mask, p.wait_gen, 45);
   // exclusive prefix over chunks [0, m_end): segment thread s folds the contiguous block
   // [m_end * s / S, m_end * (s + 1) / S) (fp32, in chunk order); the blocks are then folded
   // in order.  The split depends only on the absolute chunk index m_end, so every rank of a
@@ -264,13 +268,15 @@ extern "C" int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb
 static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st, const void* A_log,
                                const float* stats, int64_t stats_sb, int64_t blk, int64_t blk_stride,
                                int64_t n_prev, void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L,
-                               int64_t ds, int64_t C, hdc_stream_t stream) {
+                               int64_t ds, int64_t C, hdc_stream_t stream, const uint32_t* wait_flags = nullptr,
+                               uint32_t wait_mask = 0, const uint32_t* wait_gen = nullptr) {
   if (int e = ssm_check(dtype, projs, A_log, B, L, ds, C)) return e;
   if (!stats || !y) return fail(HDC_E_NULL, "ssm: null stats / y");
   SsmParams p{};
   p.projs = projs; p.psb = proj_sb; p.pst = proj_st; p.A_log = A_log; p.stats_r = stats;
   p.stats_sb = stats_sb; p.n_prev = (int)n_prev; p.y = y; p.ysb = y_sb; p.yst = y_st;
   p.blk = (int)blk; p.blk_stride = blk_stride;
+  p.wait_flags = wait_flags; p.wait_mask = wait_mask; p.wait_gen = wait_gen;
   p.L = (int)L; p.ds = (int)ds; p.C = (int)C;
   ssm_setup(p, dtype);
   dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
@@ -301,7 +307,9 @@ extern "C" int hdc_ssm_scan_out_blocked(int dtype, const void* projs, int64_t pr
                                         const void* A_log, const float* stats, int64_t stats_sb,
                                         int64_t block_chunks, int64_t block_stride, int64_t n_prev, void* y,
                                         int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds, int64_t C,
+                                        const uint32_t* wait_flags, uint32_t wait_mask, const uint32_t* wait_gen,
                                         hdc_stream_t stream) {
+  if (wait_mask && (!wait_flags || !wait_gen)) return fail(HDC_E_NULL, "ssm: wait_mask needs flags and gen");
   if (n_prev < 0 || block_chunks < 1 || block_chunks > INT_MAX)
     return fail(HDC_E_SHAPE, "ssm: n_prev=%lld block_chunks=%lld", (long long)n_prev, (long long)block_chunks);
   if (stats_sb < 0 || (B > 1 && stats_sb < block_chunks * 2 * ds) ||
@@ -309,7 +317,7 @@ extern "C" int hdc_ssm_scan_out_blocked(int dtype, const void* projs, int64_t pr
     return fail(HDC_E_SHAPE, "ssm: statistics blocks overlap (stats_sb %lld, block_stride %lld)",
                 (long long)stats_sb, (long long)block_stride);
   return ssm_scan_out_launch(dtype, projs, proj_sb, proj_st, A_log, stats, stats_sb, block_chunks, block_stride,
-                             n_prev, y, y_sb, y_st, B, L, ds, C, stream);
+                             n_prev, y, y_sb, y_st, B, L, ds, C, stream, wait_flags, wait_mask, wait_gen);
 }
 
 // ---------------------------------------------------------------------------------

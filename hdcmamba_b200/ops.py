@@ -155,11 +155,13 @@ def ssm_scan_out(projs, A_log, stats, n_prev, d_state, chunk, out=None):
 
 
 def ssm_scan_out_blocked(projs, A_log, stats, stats_sb, block_chunks, block_stride, n_prev, d_state, chunk,
-                         out=None):
+                         out=None, wait=None):
     """ssm_scan_out reading the statistics of chunks [0, n_prev + N) in place from a
     rank-major gathered buffer: ``stats`` is a 1-D fp32 tensor whose element 0 is chunk 0
     of block 0; chunk m of batch b is at (m // block_chunks) * block_stride + b * stats_sb
-    + (m % block_chunks) * 2 * ds (hdc_ssm_scan_out_blocked)."""
+    + (m % block_chunks) * 2 * ds (hdc_ssm_scan_out_blocked).  ``wait``: optional
+    (flags address, mask, generation address): the kernel waits for the flags before it
+    reads statistics stored by other GPUs."""
     _cuda(projs, A_log, stats, out)
     B, L, P = projs.shape
     if P < 3 * d_state or L % chunk != 0:
@@ -178,8 +180,10 @@ def ssm_scan_out_blocked(projs, A_log, stats, stats_sb, block_chunks, block_stri
         out = torch.empty(B, L, d_state, device=projs.device, dtype=projs.dtype)
     _same_dtype(projs, out)
     osb, ost = _row_view(out, "out")
+    wf, wm, wg = wait if wait is not None else (0, 0, 0)
     _lib.call("hdc_ssm_scan_out_blocked", _code(projs), _p(projs), sb, st, _p(a), _p(stats), stats_sb, block_chunks,
-              block_stride, n_prev, _p(out), osb, ost, B, L, d_state, chunk, _stream(projs))
+              block_stride, n_prev, _p(out), osb, ost, B, L, d_state, chunk, ctypes.c_void_p(wf), wm,
+              ctypes.c_void_p(wg), _stream(projs))
     return out
 
 
@@ -333,11 +337,13 @@ def slot_state(k, v, num_heads, chunk, gamma=None, log_a=None, state_out=None, d
 
 
 def slot_scan_gate_carry(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_strides, prev_state, prev_decay,
-                         prev_stride, n_prev, workspace, gamma=None, log_a=None):
+                         prev_stride, n_prev, workspace, gamma=None, log_a=None, wait=None):
     """``slot_scan_gate`` for one rank's part of the sequence (hdc_slot_gate_carry_fwd):
     the entering state folds the n_prev earlier parts, part s with its fp32 state at
     prev_state[s*prev_stride:] ([B, H, 64, 64]) and decay at prev_decay[s*prev_stride:]
-    ([B, H]); ``workspace`` is the one ``slot_state`` filled for the same k, v."""
+    ([B, H]); ``workspace`` is the one ``slot_state`` filled for the same k, v.  ``wait``:
+    optional (flags address, mask, generation address): the kernel waits for the flags
+    before it reads earlier parts stored by other GPUs."""
     _cuda(q, k, v, gamma, log_a, gate, gn_w, gn_b, out, prev_state, prev_decay, workspace)
     _same_dtype(q, k, v, gate, out)
     B, L, W = q.shape
@@ -364,7 +370,9 @@ def slot_scan_gate_carry(q, k, v, num_heads, chunk, gate, gn_w, gn_b, out, out_s
     _lib.call("hdc_slot_gate_carry_fwd", _code(q), _p(q), _p(k), _p(v), q.stride(0), q.stride(1), _p(gamma),
               _p(log_a), _p(gate), gate.stride(0), gate.stride(1), _p(gw), _p(gb), _p(out), out_strides[0],
               out_strides[1], out_strides[2], _p(prev_state if n_prev else None), _p(prev_decay if n_prev else None),
-              prev_stride, n_prev, None, _p(workspace), workspace.numel(), B, L, H, hd, chunk, _stream(q))
+              prev_stride, n_prev, None, _p(workspace), workspace.numel(), B, L, H, hd, chunk,
+              ctypes.c_void_p(wait[0] if wait else 0), wait[1] if wait else 0, ctypes.c_void_p(wait[2] if wait else 0),
+              _stream(q))
     return out
 
 

@@ -267,20 +267,27 @@ class SequenceParallel:
             else:
                 mb.put(flat, lay.carries(layer, self.rank), lay.carry_flags(layer, self.rank),
                        range(self.rank + 1, self.world))
-            mb.wait(lay.carry_flags(layer), range(self.rank))
+            # the consumers wait for the flags of every lower rank themselves (the SSM output
+            # kernel after staging its inputs, the slot output kernel after its first chunk's P)
+            fa, ga = mb.flag_address(lay.carry_flags(layer))
+            wait = (fa, (1 << self.rank) - 1, ga) if self.rank > 0 else None
             g = mb.view(lay.carries(layer), (self.world * n,), torch.float32)  # [W * n], rank-major
         else:
+            wait = None
             g = _all_gather(flat, self.group).reshape(-1)                     # [W * n], rank-major
         combined = torch.empty(B, Ls, ds + dm, device=h.device, dtype=h.dtype)
         # SSM: exclusive prefix over the chunks of ranks < r, then this rank's, in place (on
         # the side stream, next to the slot output kernel)
+        wk = {"wait": wait} if wait is not None else {}
+
         def ssm_out():
-            K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C, out=combined[..., :ds])
+            K.ssm_scan_out_blocked(projs, blk.A_log, g, N * 2 * ds, N, n, self.rank * N, ds, C,
+                                   out=combined[..., :ds], **wk)
 
         def slot_out():  # fold the states of ranks < r in rank order, then the local segments
             K.slot_scan_gate_carry(q, k, v, H, C, gate, blk.group_norm.weight, blk.group_norm.bias,
                                    combined[..., ds:], (Ls * (ds + dm), hd, ds + dm), g[n_st:], g[n_st + n_sl:], n,
-                                   self.rank, ws, gamma=gamma)
+                                   self.rank, ws, gamma=gamma, **wk)
         self._pair(side, cur, slot_out, ssm_out)
         if halo_on_side:
             cur.wait_stream(side)  # the halo put joins the layer (already joined by a side pair)

@@ -132,12 +132,17 @@ int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj
  * per-rank statistics gathered under sequence parallelism, read in place.  Chunk m of
  * batch b is at stats + (m / block_chunks)*block_stride + b*stats_sb +
  * (m % block_chunks)*2*ds.  Same prefix order and results as hdc_ssm_scan_out.
+ * wait_mask != 0: the statistics of earlier ranks arrive from other GPUs; every CTA first
+ * stages its chunk's inputs, then waits (bounded, acquire at system scope) until each
+ * uint32 flag wait_flags[s] with bit s of wait_mask set reaches *wait_gen (code 45 in
+ * hdc_device_error() on a timeout).  wait_mask == 0: no wait (flags may be NULL).
  */
 int hdc_ssm_scan_out_blocked(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
                              const void* A_log, const float* stats, int64_t stats_sb,
                              int64_t block_chunks, int64_t block_stride, int64_t n_prev, void* y,
                              int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds, int64_t C,
-                             hdc_stream_t stream);
+                             const uint32_t* wait_flags, uint32_t wait_mask,
+                             const uint32_t* wait_gen, hdc_stream_t stream);
 
 /*
  * The whole diagonal-SSM chunked scan (hdc_ssm_chunk_stats + hdc_ssm_scan_out, n_prev = 0)
@@ -230,6 +235,10 @@ int hdc_slot_state_fwd(int dtype, const void* k, const void* v, int64_t in_sb, i
  * segment states are reused; only the output pass runs).  No single-launch counterpart in
  * the reference: it replaces _slot_all_fused's carry of `running` across chunks
  * (hdcmamba/model.py:252, 271-272) across ranks.
+ * wait_mask != 0: prev_state / prev_decay arrive from other GPUs; the kernel waits (bounded,
+ * acquire at system scope) until each uint32 flag wait_flags[s] with bit s of wait_mask set
+ * reaches *wait_gen before it reads them -- at chunk 256 after the first chunk's S and P, so
+ * the wait overlaps them (code 44 in hdc_device_error() on a timeout).  wait_mask == 0: no wait.
  */
 int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, const void* v, int64_t in_sb,
                             int64_t in_st, const void* gamma, const float* log_a, const void* gate,
@@ -238,7 +247,8 @@ int hdc_slot_gate_carry_fwd(int dtype, const void* q, const void* k, const void*
                             const float* prev_state, const float* prev_decay, int64_t prev_stride,
                             int64_t n_prev, float* state_out, void* workspace, size_t workspace_bytes,
                             int64_t B, int64_t L, int64_t H, int64_t hd, int64_t C,
-                            hdc_stream_t stream);
+                            const uint32_t* wait_flags, uint32_t wait_mask,
+                            const uint32_t* wait_gen, hdc_stream_t stream);
 
 /*
  * hdc_slot_scan_fwd with the kernel family chosen per call (tests / cross-checks): path 0 =
