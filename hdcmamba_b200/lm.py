@@ -38,11 +38,11 @@ class HdcMambaLM(nn.Module):
         self.norm = nn.LayerNorm(d_model)
 
     def hidden(self, ids):
-        h = self.embedding(ids)
+        h = self.embedding(ids)  # a fresh activation: the layers update it in place
         if self.use_model:
-            return self.backbone(h)
+            return self.backbone._forward(h, owns_input=True)
         for layer in self.layers:
-            h, _ = layer(h)
+            h = layer._forward_inplace(h)
         return h
 
     def forward(self, ids):

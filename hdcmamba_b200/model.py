@@ -214,6 +214,21 @@ class HdcMamba9v3Block(nn.Module):
                             self.out_proj.weight.t()).reshape(x.shape)
         return y[:, pad:, :], None
 
+    def _forward_inplace(self, x):
+        """``forward(x)[0]`` for an internal activation that nothing else reads (a layer input
+        inside HdcMamba9v3Model / the LM wrapper): in inference the layer's update is added to
+        x in place, inside the out_proj GEMM (beta = 1, output = x), which skips the copy of
+        x into a new output tensor that the out-of-place addmm makes first.  Falls back to
+        ``forward`` when autograd needs the graph or x is padded / not contiguous."""
+        if (self.training or (torch.is_grad_enabled() and (x.requires_grad or self.out_proj.weight.requires_grad))
+                or x.shape[1] % self.chunk_size != 0 or not x.is_contiguous()):
+            return self.forward(x)[0]
+        _require_cuda(x)
+        comb = self._mix(x)
+        x2 = x.view(-1, self.d_model)
+        torch.addmm(x2, comb.reshape(-1, comb.shape[-1]), self.out_proj.weight.t(), out=x2)
+        return x
+
 
 class HdcMamba9v3Model(nn.Module):
     """hdcmamba/model.py:396-404 (chunk size 256 as in the reference; num_slots unused there too)."""
@@ -226,6 +241,11 @@ class HdcMamba9v3Model(nn.Module):
         self.norm_final = nn.LayerNorm(d_model)
 
     def forward(self, x):
-        for layer in self.layers:
-            x, _ = layer(x)
+        return self._forward(x)
+
+    def _forward(self, x, owns_input=False):
+        """The layers after the first (and the first too when ``owns_input``: x is an
+        internal activation of the caller) update the residual stream in place."""
+        for i, layer in enumerate(self.layers):
+            x = layer._forward_inplace(x) if (i > 0 or owns_input) else layer(x)[0]
         return final_layer_norm(self.norm_final, x)

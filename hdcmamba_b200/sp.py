@@ -184,7 +184,7 @@ class SequenceParallel:
             ssm_fn()
         cur.wait_stream(side)
 
-    def block(self, blk, h, layer=0):
+    def block(self, blk, h, layer=0, inplace=False):
         """One HdcMamba9v3Block on the local segment h [B, Ls, dm] (Ls a multiple of the
         chunk size; fixed semantics).  Returns the block output for the segment."""
         if blk.semantics != "fixed":
@@ -292,7 +292,15 @@ class SequenceParallel:
         if halo_on_side:
             cur.wait_stream(side)  # the halo put joins the layer (already joined by a side pair)
         combined = K.row_layernorm(combined, 1e-5, out=combined)
-        out = torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm), blk.out_proj.weight.t()).reshape(B, Ls, dm)
+        if inplace and h.is_cuda:
+            # h is an internal activation: the update is added in place inside the GEMM (no
+            # copy of h into a new output); the halo put that read h has joined above
+            h2 = h.view(-1, dm)
+            torch.addmm(h2, combined.reshape(-1, ds + dm), blk.out_proj.weight.t(), out=h2)
+            out = h
+        else:
+            out = torch.addmm(h.reshape(-1, dm), combined.reshape(-1, ds + dm),
+                              blk.out_proj.weight.t()).reshape(B, Ls, dm)
         if exch is not None:
             cur.wait_stream(exch)  # the carry put joins the layer
         return out
@@ -301,7 +309,7 @@ class SequenceParallel:
         """HdcMamba9v3Model.forward on the local segment (hdcmamba/model.py:402-404)."""
         self._begin(len(model.layers), h, model.layers[0])
         for i, blk in enumerate(model.layers):
-            h = self.block(blk, h, layer=i)
+            h = self.block(blk, h, layer=i, inplace=i > 0)
         self._end()
         out = self._final_norm(model.norm_final, h)
         self._finish()
@@ -311,13 +319,13 @@ class SequenceParallel:
         """HdcMambaLM.forward (embedding -> backbone -> LayerNorm -> tied head) on the local
         segment of token ids [B, Ls]; returns the segment's logits [B, Ls, vocab]."""
         with torch.no_grad():
-            h = lm.embedding(ids_local)
+            h = lm.embedding(ids_local)  # a fresh activation: every layer updates it in place
+            layers = list(lm.backbone.layers) if lm.use_model else list(lm.layers)
+            self._begin(len(layers), h, layers[0])
+            for i, blk in enumerate(layers):
+                h = self.block(blk, h, layer=i, inplace=True)
+            self._end()
             if lm.use_model:
-                h = self.model(lm.backbone, h)
-            else:
-                self._begin(len(lm.layers), h, lm.layers[0])
-                for i, blk in enumerate(lm.layers):
-                    h = self.block(blk, h, layer=i)
-                self._end()
-                self._finish()
+                h = self._final_norm(lm.backbone.norm_final, h)
+            self._finish()
             return F.linear(self._final_norm(lm.norm, h), lm.embedding.weight)
