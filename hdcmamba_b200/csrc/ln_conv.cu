@@ -379,7 +379,8 @@ static int launch_ln_conv(LnConvParams p, int64_t B, cudaStream_t stream) {
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ln_conv_kernel<T, SILU>, threads, smem);
   if (occ < 1) occ = 1;
   const int64_t target = (int64_t)num_sms() * occ;
-  int64_t segs_per_b = (target + B - 1) / B;
+  // rounded down, so B * segs_per_b stays within one wave of resident CTAs
+  int64_t segs_per_b = target / B > 0 ? target / B : 1;
   int64_t seg_len = (p.L + segs_per_b - 1) / segs_per_b;
   seg_len = ((seg_len + LNC_ROWS - 1) / LNC_ROWS) * LNC_ROWS;
   segs_per_b = (p.L + seg_len - 1) / seg_len;

@@ -493,7 +493,9 @@ constexpr int kBwdMaxD = 2048;  // 512 threads x 4 channels
 static void bwd_plan(int64_t B, int64_t L, int64_t D, int* seg_len, int* segs_per_b) {
   const int64_t threads = std::max<int64_t>(32, (D / 4 + 31) / 32 * 32);
   const int64_t target = (int64_t)num_sms() * std::max<int64_t>(1, std::min<int64_t>(4, 512 / threads));
-  int64_t spb = (target + B - 1) / B;
+  // segments per batch row rounded down: B * spb stays within one wave (rounding up gave
+  // B = 8 on 148 SMs 152 CTAs, whose last 4 ran as a second wave of the whole CTA time)
+  int64_t spb = std::max<int64_t>(1, target / B);
   int64_t len = (L + spb - 1) / spb;
   len = (len + 3) / 4 * 4;
   if (len < 16) len = 16;
