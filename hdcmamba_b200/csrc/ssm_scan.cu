@@ -11,8 +11,11 @@
 // Schedule: one CTA per (chunk, group of 16 channels, batch) with 16*S <= 256 threads.
 // The CTA stages the chunk's dt / x / b columns of its channels in shared memory with
 // 16-byte loads, all in flight at once; thread (j, s) then scans C/S consecutive steps of
-// channel j (16 at C 256).  Segment results are combined through
-// shared memory: (h_s, sum_log_s) with h = h_prev * exp(sum_log_s) + h_s.
+// channel j (16 at C 256).  Chunks of C = 16, 32, ..., 256 take the 16-step kernels below
+// (segments summarised by their state and decay product, combined by warp shuffles, the
+// output pass scanning once); other chunk lengths take the general kernels, whose segment
+// results are combined through shared memory: (h_s, sum_log_s) with
+// h = h_prev * exp(sum_log_s) + h_s.
 //   pass 1 (hdc_ssm_chunk_stats): chunk statistics -> stats[b, n, 0:2ds]
 //   pass 2 (hdc_ssm_scan_out):    exclusive prefix over all earlier chunks (including
 //                                 n_prev chunks of earlier sequence segments; folded
@@ -205,6 +208,155 @@ __global__ void __launch_bounds__(256) ssm_scan_out_kernel(SsmParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Chunks of C = 16 S steps, S = 1, 2, 4, 8 or 16 segments of kSteps = 16 steps.
+// Two thread maps over the CTA's 16 S threads:
+//  * step map (jl = tid % 16, s = tid / 16): the thread scans the 16 steps of segment s of
+//    channel jl from the staged tile (the lanes of a warp read one row per step);
+//  * segment map (c = tid / S, s = tid % S): the S segments of channel c sit in S
+//    consecutive lanes, so they combine by shuffles.
+// A segment is summarised by (h, E): h its state from 0 at its start, E = prod a_t its
+// decay; segments combine as (h1, E1) o (h2, E2) = (h1 E2 + h2, E1 E2), with no exp.  The
+// output kernel keeps each step's local (h_t, E_t) in registers, so it scans the chunk once:
+//   h(step t) = hin E_t + h_t,  y_t = bf16( bf16(h) + bf16(G) Ein E_t )
+// with (hin, Ein) the exclusive combine of the earlier segments of the chunk.
+// ---------------------------------------------------------------------------------
+constexpr int kSteps = 16;
+constexpr int kPad = kCG + 1;  // partials [s][kPad]: both maps touch them without bank conflicts
+
+// local scan of segment s of channel jl: states h_t and decay products E_t of its steps,
+// and (STATS) the summed log decay
+template <typename T, bool STATS>
+__device__ __forceinline__ void ssm_local16(const T* tile, int C, int s, int jl, float A, float (&hs)[kSteps],
+                                            float (&Es)[kSteps], float& sl) {
+  const T* td = tile + s * kSteps * kCG + jl;  // dt, then x and b C rows further
+  float h = 0.f, E = 1.f;
+  sl = 0.f;
+#pragma unroll
+  for (int t = 0; t < kSteps; ++t) {
+    const float dts = ssoftplus<T>(to_f(td[t * kCG]));
+    const float ld = dts * A;
+    const float a = sexp<T>(ld);
+    h = fmaf(h, a, dts * to_f(td[(2 * C + t) * kCG]) * to_f(td[(C + t) * kCG]));
+    E *= a;
+    if (STATS) sl += ld;
+    hs[t] = h;
+    Es[t] = E;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) ssm_stats16_kernel(SsmParams p) {
+  extern __shared__ float sh[];  // [3][S][kPad] partials (h, E, summed log decay), then the tile
+  const int S = p.S;
+  T* tile = reinterpret_cast<T*>(sh + ((3 * S * kPad + 3) & ~3));  // 16-byte aligned
+  const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  ssm_stage<T>(p, b, n, g, tile);
+  {
+    const int jl = tid % kCG, s = tid / kCG;
+    const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCG + jl]));
+    __syncthreads();
+    float hs[kSteps], Es[kSteps], sl;
+    ssm_local16<T, true>(tile, p.C, s, jl, A, hs, Es, sl);
+    sh[s * kPad + jl] = hs[kSteps - 1];
+    sh[(S + s) * kPad + jl] = Es[kSteps - 1];
+    sh[(2 * S + s) * kPad + jl] = sl;
+  }
+  __syncthreads();
+  // segment map: ordered butterfly over the S lanes of channel c (the earlier operand
+  // first, so every lane of the group ends with the same bits)
+  const int c = tid / S, s = tid % S;
+  float h = sh[s * kPad + c], E = sh[(S + s) * kPad + c], l = sh[(2 * S + s) * kPad + c];
+  for (int m = 1; m < S; m <<= 1) {
+    const float h2 = __shfl_xor_sync(0xffffffffu, h, m), E2 = __shfl_xor_sync(0xffffffffu, E, m);
+    const float l2 = __shfl_xor_sync(0xffffffffu, l, m);
+    h = (s & m) ? fmaf(h2, E, h) : fmaf(h, E2, h2);
+    E *= E2;
+    l += l2;
+  }
+  if (s == 0) {
+    float* st = p.stats_w + ((size_t)b * (p.L / p.C) + n) * 2 * p.ds;
+    st[g * kCG + c] = bf16_round(h);
+    st[p.ds + g * kCG + c] = bf16_round(l);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) ssm_out16_kernel(SsmParams p) {
+  extern __shared__ float sh[];  // [2][S][kPad] partials, then the staged tile
+  const int S = p.S;
+  T* tile = reinterpret_cast<T*>(sh + ((2 * S * kPad + 3) & ~3));  // 16-byte aligned
+  const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  ssm_stage<T>(p, b, n, g, tile);
+  if (p.wait_mask) cta_wait_flags(p.wait_flags, p.wait_mask, p.wait_gen, 45);
+  // segment map: exclusive prefix over chunks [0, m_end) of channel c.  Lane s folds the
+  // contiguous block [m_end s / S, m_end (s + 1) / S) in chunk order (fp32), then the blocks
+  // fold by an ordered butterfly.  Both depend only on the absolute chunk index m_end, so a
+  // sequence-parallel rank gets the same bits as one GPU over the whole sequence.
+  const int c = tid / S, sc = tid % S, jc = g * kCG + c;
+  float G = 0.f;
+  {
+    const int m_end = p.n_prev + n;
+    const int m0 = (int)((int64_t)m_end * sc / S), m1 = (int)((int64_t)m_end * (sc + 1) / S);
+    float D = 0.f;
+#pragma unroll 4
+    for (int m = m0; m < m1; ++m) {
+      const float* st = ssm_stats_at(p, b, m);
+      const float dec = st[p.ds + jc];
+      G = fmaf(G, sexp<T>(dec), st[jc]);
+      D += dec;
+    }
+    for (int m = 1; m < S; m <<= 1) {
+      const float G2 = __shfl_xor_sync(0xffffffffu, G, m), D2 = __shfl_xor_sync(0xffffffffu, D, m);
+      G = (sc & m) ? fmaf(G2, sexp<T>(D), G) : fmaf(G, sexp<T>(D2), G2);
+      D += D2;
+    }
+    G = bf16_round(G);
+  }
+  __syncthreads();  // tile staged
+  const int jl = tid % kCG, s = tid / kCG;
+  const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCG + jl]));
+  float hs[kSteps], Es[kSteps], sl;
+  ssm_local16<T, false>(tile, p.C, s, jl, A, hs, Es, sl);
+  sh[s * kPad + jl] = hs[kSteps - 1];
+  sh[(S + s) * kPad + jl] = Es[kSteps - 1];
+  __syncthreads();
+  {
+    // segment map: inclusive scan over the segments, then the exclusive (hin, Ein); each
+    // thread overwrites only the partials it read
+    float h = sh[sc * kPad + c], E = sh[(S + sc) * kPad + c];
+    for (int d = 1; d < S; d <<= 1) {
+      const float h2 = __shfl_up_sync(0xffffffffu, h, d, S), E2 = __shfl_up_sync(0xffffffffu, E, d, S);
+      if (sc >= d) {
+        h = fmaf(h2, E, h);
+        E *= E2;
+      }
+    }
+    float hin = 0.f, Ein = 1.f;
+    if (S > 1) {  // (S = 1: a 16-thread CTA, no shuffles)
+      hin = __shfl_up_sync(0xffffffffu, h, 1, S);
+      Ein = __shfl_up_sync(0xffffffffu, E, 1, S);
+    }
+    if (sc == 0) {
+      hin = 0.f;
+      Ein = 1.f;
+    }
+    sh[sc * kPad + c] = hin;
+    sh[(S + sc) * kPad + c] = G * Ein;
+  }
+  __syncthreads();
+  const float hin = sh[s * kPad + jl], GE = sh[(S + s) * kPad + jl];
+  T* yb = static_cast<T*>(p.y) + (size_t)b * p.ysb + (size_t)(n * p.C + s * kSteps) * p.yst + g * kCG + jl;
+#pragma unroll
+  for (int t = 0; t < kSteps; ++t) {
+    const float hh = fmaf(hin, Es[t], hs[t]);
+    yb[(size_t)t * p.yst] = from_f<T>(bf16_round(bf16_round(hh) + GE * Es[t]));
+  }
+}
+
+// the 16-step kernels take C = 16 S with S a power of two up to 16
+static bool ssm_fast(int64_t C) { return C == 16 || C == 32 || C == 64 || C == 128 || C == 256; }
+
 // Channels per CTA: 16, so a chunk's channels spread over ds / 16 CTAs.
 static int ssm_group(int ds) { return ds < kCG ? ds : kCG; }
 
@@ -216,13 +368,25 @@ static int ssm_segments(int ds, int C) {
   return S;
 }
 
+// floats of partials in front of the staged tile (a multiple of 4: the tile takes 16-byte stores)
+static int ssm_parts_floats(const SsmParams& p, bool out) {
+  const int f = ssm_fast(p.C) ? (out ? 2 : 3) * p.S * kPad : (out ? 4 : 2) * p.S * kCG;
+  return (f + 3) / 4 * 4;
+}
+
+// one launch of the statistics (out = false) or output kernel for the plan in p
 template <typename T>
-static size_t ssm_smem(const SsmParams& p, int parts) {
-  return (size_t)parts * p.S * kCG * sizeof(float) + (size_t)3 * p.C * kCG * sizeof(T);
+static void ssm_launch(bool out, const SsmParams& p, dim3 grid, cudaStream_t s) {
+  const size_t smem = (size_t)ssm_parts_floats(p, out) * sizeof(float) + (size_t)3 * p.C * kCG * sizeof(T);
+  void (*k)(SsmParams);
+  if (ssm_fast(p.C)) k = out ? ssm_out16_kernel<T> : ssm_stats16_kernel<T>;
+  else k = out ? ssm_scan_out_kernel<T> : ssm_chunk_stats_kernel<T>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k<<<grid, p.S * p.CG, smem, s>>>(p);
 }
 
 static void ssm_setup(SsmParams& p, int dtype) {
-  p.S = ssm_segments(p.ds, p.C);
+  p.S = ssm_fast(p.C) ? (int)(p.C / kSteps) : ssm_segments(p.ds, p.C);
   p.CG = kCG;
   const size_t es = dtype == HDC_F32 ? 4 : 2;
   p.vec = ((reinterpret_cast<uintptr_t>(p.projs) & 15u) == 0 && (p.pst * es) % 16 == 0 && (p.psb * es) % 16 == 0)
@@ -253,15 +417,8 @@ extern "C" int hdc_ssm_chunk_stats(int dtype, const void* projs, int64_t proj_sb
   ssm_setup(p, dtype);
   dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) {
-    const size_t smem = ssm_smem<float>(p, 2);
-    cudaFuncSetAttribute(ssm_chunk_stats_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    ssm_chunk_stats_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
-  } else {
-    const size_t smem = ssm_smem<__nv_bfloat16>(p, 2);
-    cudaFuncSetAttribute(ssm_chunk_stats_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    ssm_chunk_stats_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
-  }
+  if (dtype == HDC_F32) ssm_launch<float>(false, p, grid, s);
+  else ssm_launch<__nv_bfloat16>(false, p, grid, s);
   return launch_status("ssm_chunk_stats_kernel");
 }
 
@@ -281,15 +438,8 @@ static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, in
   ssm_setup(p, dtype);
   dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) {
-    const size_t smem = ssm_smem<float>(p, 4);
-    cudaFuncSetAttribute(ssm_scan_out_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    ssm_scan_out_kernel<float><<<grid, p.S * p.CG, smem, s>>>(p);
-  } else {
-    const size_t smem = ssm_smem<__nv_bfloat16>(p, 4);
-    cudaFuncSetAttribute(ssm_scan_out_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    ssm_scan_out_kernel<__nv_bfloat16><<<grid, p.S * p.CG, smem, s>>>(p);
-  }
+  if (dtype == HDC_F32) ssm_launch<float>(true, p, grid, s);
+  else ssm_launch<__nv_bfloat16>(true, p, grid, s);
   return launch_status("ssm_scan_out_kernel");
 }
 

@@ -80,7 +80,10 @@ def test_ssm_golden(tag):
     assert rel(y, g[f"{tag}_y"]) < BF16_TOL
 
 
-@pytest.mark.parametrize("B,L,ds,C", [(2, 1024, 64, 256), (1, 2048, 128, 256), (3, 512, 64, 64), (1, 384, 16, 128)])
+# C = 16, 32, 64, 128, 256: the 16-step kernels (1 to 16 segments per chunk); C = 8 and 512:
+# the general kernels
+@pytest.mark.parametrize("B,L,ds,C", [(2, 1024, 64, 256), (1, 2048, 128, 256), (3, 512, 64, 64), (1, 384, 16, 128),
+                                      (2, 320, 32, 32), (1, 256, 16, 16), (2, 96, 16, 8), (1, 1024, 32, 512)])
 def test_ssm_bf16_vs_oracle(B, L, ds, C):
     P = 3 * ds + 40
     projs = torch.randn(B, L, P, generator=gen(8))
