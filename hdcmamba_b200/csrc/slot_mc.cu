@@ -31,6 +31,12 @@ constexpr int CHUNK = CT * 128;   // one chunk's rows inside a tile
 constexpr int TABN = CT + 4;      // one chunk's decay table (CT + 1 entries used)
 constexpr size_t SMEM_A = 1024 + 4 * TILE + 2 * G * TABN * 4 + 3 * 8 + 16;
 constexpr size_t SMEM_B = 1024 + 6 * TILE + 2 * G * TABN * 4 + 6 * 8 + 16;
+// Pass B loads chunk x's Q rows permuted in 16-row blocks: tile rows [16 q, 16 q + 16) of the
+// chunk (TMEM lane quarter q of its M = 64 accumulators) hold chunk rows of block (q + x) mod 4.
+// The causal P work of a row block grows 1 : 2 : 3 : 4 with the block, and lane quarter q is
+// read only by the warps of one SM sub-partition, so over the four chunks of a group every
+// sub-partition gets the same P work.  Chunk row of tile row r (0 <= r < CT) of chunk x:
+__host__ __device__ constexpr int q_chunk_row(int x, int r) { return ((((r >> 4) + x) & 3) << 4) | (r & 15); }
 }  // namespace mc
 
 // Decay table of chunk x of group g for this (b, h): per-step, c_i and the chunk decay
@@ -252,7 +258,11 @@ __global__ void __launch_bounds__(mc::NT, 1)
     const int row = (n0 + g * G) * CT;
     mbar_expect_tx(&bars[st], 2 * TILE);
     tma_load_3d(sK, &mapK, h * p.hd, row, b, &bars[st]);
-    tma_load_3d(sK + TILE, &mapQ, h * p.hd, row, b, &bars[st]);
+    // Q in 16-row boxes, each chunk's row blocks permuted (q_chunk_row)
+#pragma unroll
+    for (int j = 0; j < ROWS / 16; ++j)
+      tma_load_3d(sK + TILE + j * 16 * 128, &mapQ, h * p.hd, row + (j >> 2) * CT + q_chunk_row(j >> 2, (j & 3) * 16),
+                  b, &bars[st]);
     pending |= 1 << st;
   };
   auto issue_v = [&](int g) {
@@ -353,8 +363,9 @@ __global__ void __launch_bounds__(mc::NT, 1)
       for (int it = 0; it < IT; ++it) {
         const int idx = tid + it * NT, row = idx >> 3, x = row >> 6, i = row & (CT - 1);
         const float* T = mc_tab(sTab, PERSTEP, g, x);
+        const int iq = q_chunk_row(x, i);  // chunk row of Q tile row `row`
         const float kd = PERSTEP ? fast_exp(T[CT - 1] - T[i]) : T[CT - 1 - i];
-        const float qd = PERSTEP ? fast_exp(T[i]) : T[i];
+        const float qd = PERSTEP ? fast_exp(T[iq]) : T[iq];
         const uint64_t kd2 = f2_make(kd, kd), qd2 = f2_make(qd, qd);
         uint32_t* wk = reinterpret_cast<uint32_t*>(&kv[it]);
         uint32_t* wq = reinterpret_cast<uint32_t*>(&qv[it]);
@@ -367,36 +378,35 @@ __global__ void __launch_bounds__(mc::NT, 1)
         reinterpret_cast<uint4*>(sQ)[idx] = qv[it];
       }
     }
-    // ---- P_x = bf16(mask(S_x) decay): rows f_row, columns [e0, e0 + 16) of every chunk -> sPR
+    // ---- P_x = bf16(mask(S_x) decay): tile rows f_row (chunk rows q_chunk_row(x, f_row)),
+    // columns [e0, e0 + 16) of every chunk -> sPR
     {
-      const int i = f_row;
-      if (wg <= quarter) {  // some column of the piece is at or below the diagonal of these rows
-        float sv[G][16];
-        tmem_ld16x2(tL + e0, tL + 128 + e0, sv[0], sv[1]);
-        tmem_ld16x2(tL + 256 + e0, tL + 384 + e0, sv[2], sv[3]);
-        if (f_valid) {
+      float sv[G][16];
+      tmem_ld16x2(tL + e0, tL + 128 + e0, sv[0], sv[1]);
+      tmem_ld16x2(tL + 256 + e0, tL + 384 + e0, sv[2], sv[3]);
+      if (f_valid) {
 #pragma unroll
-          for (int x = 0; x < G; ++x) {
+        for (int x = 0; x < G; ++x) {
+          const int qb = (quarter + x) & 3;  // chunk row block of this lane quarter
+          const int i = qb * 16 + lane;
+          float v[16];
+          if (wg <= qb) {  // some column of the piece is at or below the diagonal of these rows
             const float* T = mc_tab(sTab, PERSTEP, g, x);
             const float ci = PERSTEP ? T[i] : 0.f;
-            float v[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const int j = e0 + e;
               const float dm = j <= i ? (PERSTEP ? fast_exp(ci - T[j]) : T[i - j]) : 0.f;
               v[e] = j <= i ? sv[x][e] * dm : 0.f;
             }
+          } else {
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
-              *reinterpret_cast<uint4*>(sPR + x * CHUNK + sw128_chunk(i, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&v[c * 8]);
+            for (int e = 0; e < 16; ++e) v[e] = 0.f;
           }
-        }
-      } else if (f_valid) {
-#pragma unroll
-        for (int x = 0; x < G; ++x)
 #pragma unroll
           for (int c = 0; c < 2; ++c)
-            *reinterpret_cast<uint4*>(sPR + x * CHUNK + sw128_chunk(i, (e0 >> 3) + c)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(sPR + x * CHUNK + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&v[c * 8]);
+        }
       }
     }
     fence_proxy_async_smem();
@@ -482,7 +492,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
           for (int x = 0; x < G; ++x)
 #pragma unroll
             for (int c = 0; c < 2; ++c)
-              *reinterpret_cast<uint4*>(sPR + sw128_chunk(x * CT + f_row, (e0 >> 3) + c)) =
+              *reinterpret_cast<uint4*>(sPR + sw128_chunk(x * CT + q_chunk_row(x, f_row), (e0 >> 3) + c)) =
                   pack16<__nv_bfloat16>(&yv[x][c * 8]);
         }
         __syncthreads();
@@ -498,7 +508,7 @@ __global__ void __launch_bounds__(mc::NT, 1)
       } else if (f_valid) {
 #pragma unroll
         for (int x = 0; x < G; ++x) {
-          const int t_row = (n0 + g * G + x) * CT + f_row;
+          const int t_row = (n0 + g * G + x) * CT + q_chunk_row(x, f_row);
           __nv_bfloat16* yrow = static_cast<__nv_bfloat16*>(p.y) + (size_t)b * p.y_sb + (size_t)h * p.y_sh +
                                 (size_t)t_row * p.y_st + e0;
 #pragma unroll
@@ -569,7 +579,7 @@ int slot_mc_fwd(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, v
   const int64_t W = (int64_t)sp.H * sp.hd;
   const int64_t sb = B > 1 ? in_sb : (int64_t)sp.L * in_st;
   CUtensorMap mq, mk, mv;
-  if (int e = slot_make_map(&mq, sp.q, W, sp.L, B, in_st, sb, mc::ROWS)) return e;
+  if (int e = slot_make_map(&mq, sp.q, W, sp.L, B, in_st, sb, 16)) return e;  // 16-row boxes (q_chunk_row)
   if (int e = slot_make_map(&mk, sp.k, W, sp.L, B, in_st, sb, mc::ROWS)) return e;
   if (int e = slot_make_map(&mv, sp.v, W, sp.L, B, in_st, sb, mc::ROWS)) return e;
   const bool ps = sp.log_a != nullptr;
