@@ -194,6 +194,9 @@ __global__ void __launch_bounds__(spipe::NT, 1)
   uint32_t* sTmem = reinterpret_cast<uint32_t*>(bars + NBAR);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, cgrp = warp >> 2;
+  // the output kernel (launched as this grid's programmatic dependent) may start its
+  // CTAs as this grid's CTAs exit; it waits for this grid before it reads the states
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int nseg_a = p.nseg_a;
   const int bh = blockIdx.x / nseg_a, seg = blockIdx.x - bh * nseg_a;
   const int b = bh / p.H, h = bh - b * p.H;
@@ -1096,6 +1099,10 @@ __global__ void __launch_bounds__(pipe::NT, 1)
     // (Rr, with the product of their decays in Dloc); the parts are waited for and folded in
     // after the first chunk's P, R = Dloc R_parts + Rr, so the wait overlaps this CTA's
     // prologue, the first loads, phi, S and P.
+    // the segment states come from the state pass: when this kernel was launched as its
+    // programmatic dependent, everything above (loads, phi and S of the first chunk) ran
+    // while that pass was finishing; wait for it here (returns at once otherwise)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     constexpr bool late = LATE;
     float Dloc = 1.f;
     if (f_valid && late) {
@@ -1488,12 +1495,26 @@ static int run_tc(const SlotParams& sp, const SlotGate* gt, const SlotCarry* car
       CUtensorMap mq32;  // Q in 32-row boxes (row block 0 is loaded in permuted block order)
       if (int e = make_map(&mq32, sp.q, W, sp.L, B, in_st, sb, 32)) return e;
       const size_t sm = pipe::SMEM;
+      // right after the state pass: a programmatic dependent launch, so that output CTAs
+      // take the SMs as state CTAs leave them and overlap their first chunk's loads, phi and
+      // S with the end of the state pass (the kernel waits before it reads the states)
+      const bool after_state = p.nseg > 1 && !carry;
       auto go = [&](auto kernel) {
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        kernel<<<(unsigned)(BH * p.nseg), pipe::NT, sm, s>>>(mq32, mk, mv, mg, p);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)(BH * p.nseg));
+        cfg.blockDim = dim3(pipe::NT);
+        cfg.dynamicSmemBytes = sm;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = after_state ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, kernel, mq32, mk, mv, mg, p);
       };
-      if (p.wait_mask) go(slot_tc_pipe_kernel<PS, true>);
-      else go(slot_tc_pipe_kernel<PS, false>);
+      const cudaError_t le = p.wait_mask ? go(slot_tc_pipe_kernel<PS, true>) : go(slot_tc_pipe_kernel<PS, false>);
+      if (le != cudaSuccess) return fail((int)le, "slot_tc_pipe_kernel launch: %s", cudaGetErrorString(le));
       return launch_status("slot_tc_pipe_kernel");
     }
   }
