@@ -378,35 +378,40 @@ __global__ void __launch_bounds__(mc::NT, 1)
         reinterpret_cast<uint4*>(sQ)[idx] = qv[it];
       }
     }
-    // ---- P_x = bf16(mask(S_x) decay): tile rows f_row (chunk rows q_chunk_row(x, f_row)),
-    // columns [e0, e0 + 16) of every chunk -> sPR
+    // ---- P_x = bf16(mask(S_x) decay): columns [e0, e0 + 16) of every chunk -> sPR.  The M = 64
+    // accumulators fill TMEM lanes 0-15 of each quarter, so the two half-warps split the
+    // columns: lanes 16-31 take columns 8-15 of the row that lane - 16 read (tile row
+    // quarter * 16 + lane % 16, chunk row q_chunk_row(x, tile row)).
     {
       float sv[G][16];
       tmem_ld16x2(tL + e0, tL + 128 + e0, sv[0], sv[1]);
       tmem_ld16x2(tL + 256 + e0, tL + 384 + e0, sv[2], sv[3]);
-      if (f_valid) {
+      const int hl = lane >> 4, prow = quarter * 16 + (lane & 15);
 #pragma unroll
-        for (int x = 0; x < G; ++x) {
-          const int qb = (quarter + x) & 3;  // chunk row block of this lane quarter
-          const int i = qb * 16 + lane;
-          float v[16];
-          if (wg <= qb) {  // some column of the piece is at or below the diagonal of these rows
-            const float* T = mc_tab(sTab, PERSTEP, g, x);
-            const float ci = PERSTEP ? T[i] : 0.f;
+      for (int x = 0; x < G; ++x) {
+        const int qb = (quarter + x) & 3;  // chunk row block of this lane quarter
+        const int i = qb * 16 + (lane & 15);
+        float v[8];
+        if (wg <= qb) {  // some column of the piece is at or below the diagonal of these rows
+          float w[8];
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int j = e0 + e;
-              const float dm = j <= i ? (PERSTEP ? fast_exp(ci - T[j]) : T[i - j]) : 0.f;
-              v[e] = j <= i ? sv[x][e] * dm : 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) v[e] = 0.f;
+          for (int e = 0; e < 8; ++e) {
+            const float up = __shfl_up_sync(0xffffffffu, sv[x][8 + e], 16);
+            w[e] = hl ? up : sv[x][e];
           }
+          const float* T = mc_tab(sTab, PERSTEP, g, x);
+          const float ci = PERSTEP ? T[i] : 0.f;
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            *reinterpret_cast<uint4*>(sPR + x * CHUNK + sw128_chunk(f_row, (e0 >> 3) + c)) = pack16<__nv_bfloat16>(&v[c * 8]);
+          for (int e = 0; e < 8; ++e) {
+            const int j = e0 + 8 * hl + e;
+            const float dm = j <= i ? (PERSTEP ? fast_exp(ci - T[j]) : T[i - j]) : 0.f;
+            v[e] = j <= i ? w[e] * dm : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = 0.f;
         }
+        *reinterpret_cast<uint4*>(sPR + x * CHUNK + sw128_chunk(prow, (e0 >> 3) + hl)) = pack16<__nv_bfloat16>(v);
       }
     }
     fence_proxy_async_smem();
