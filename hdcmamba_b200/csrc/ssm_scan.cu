@@ -11,11 +11,11 @@
 // Schedule: one CTA per (chunk, group of 16 channels, batch) with 16*S <= 256 threads.
 // The CTA stages the chunk's dt / x / b columns of its channels in shared memory with
 // 16-byte loads, all in flight at once; thread (j, s) then scans C/S consecutive steps of
-// channel j (16 at C 256).  Chunks of C = 16, 32, ..., 256 take the 16-step kernels below
-// (segments summarised by their state and decay product, combined by warp shuffles, the
-// output pass scanning once); other chunk lengths take the general kernels, whose segment
-// results are combined through shared memory: (h_s, sum_log_s) with
-// h = h_prev * exp(sum_log_s) + h_s.
+// channel j (16 at C 256); segment results are combined through shared memory:
+// (h_s, sum_log_s) with h = h_prev * exp(sum_log_s) + h_s.  Chunks of C = 16, 32, ..., 256
+// take the 16-step kernels below instead (8 channels per CTA, loads straight from global
+// memory, segments summarised by their state and decay product and combined by warp
+// shuffles, the output pass scanning once).
 //   pass 1 (hdc_ssm_chunk_stats): chunk statistics -> stats[b, n, 0:2ds]
 //   pass 2 (hdc_ssm_scan_out):    exclusive prefix over all earlier chunks (including
 //                                 n_prev chunks of earlier sequence segments; folded
@@ -42,7 +42,7 @@ struct SsmParams {
   // (bounded) until every flag s of wait_mask reaches *wait_gen before it reads them
   const uint32_t* wait_flags; uint32_t wait_mask; const uint32_t* wait_gen;
   int L, ds, C, S;
-  int CG;   // channels per CTA (kCG; grid.y = ds / kCG channel groups)
+  int CG;   // channels per CTA (kCD or kCG; grid.y = ds / CG channel groups)
   int vec;  // 16-byte loads of the staged columns are aligned
 };
 
@@ -209,10 +209,14 @@ __global__ void __launch_bounds__(256) ssm_scan_out_kernel(SsmParams p) {
 }
 
 // ---------------------------------------------------------------------------------
-// Chunks of C = 16 S steps, S = 1, 2, 4, 8 or 16 segments of kSteps = 16 steps.
-// Two thread maps over the CTA's 16 S threads:
-//  * step map (jl = tid % 16, s = tid / 16): the thread scans the 16 steps of segment s of
-//    channel jl from the staged tile (the lanes of a warp read one row per step);
+// Chunks of C = 16 S steps, S = 1, 2, 4, 8 or 16 segments of kSteps = 16 steps, kCD = 8
+// channels per CTA (8 S threads, ~1 KB of shared memory).  The CTAs are small enough to
+// sit on an SM next to a slot-scan CTA (one per SM with ~200 KB of shared memory), so the
+// SSM, launched on a side stream, runs beside the slot kernels instead of after them.
+// Two thread maps over the CTA's threads:
+//  * step map (jl = tid % 8, s = tid / 8): the thread loads the 16 steps of segment s of
+//    channel jl straight from global memory (all 48 loads in flight at once; the 8 lanes of
+//    a segment read 16 contiguous bytes per row) and scans them;
 //  * segment map (c = tid / S, s = tid % S): the S segments of channel c sit in S
 //    consecutive lanes, so they combine by shuffles.
 // A segment is summarised by (h, E): h its state from 0 at its start, E = prod a_t its
@@ -222,22 +226,32 @@ __global__ void __launch_bounds__(256) ssm_scan_out_kernel(SsmParams p) {
 // with (hin, Ein) the exclusive combine of the earlier segments of the chunk.
 // ---------------------------------------------------------------------------------
 constexpr int kSteps = 16;
-constexpr int kPad = kCG + 1;  // partials [s][kPad]: both maps touch them without bank conflicts
+constexpr int kCD = 8;         // channels per CTA of these kernels
+constexpr int kPad = kCD + 1;  // partials [s][kPad]: both maps touch them without bank conflicts
 
-// local scan of segment s of channel jl: states h_t and decay products E_t of its steps,
-// and (STATS) the summed log decay
+// local scan of segment s of channel g * kCD + jl of chunk n: states h_t and decay products
+// E_t of its steps, and (STATS) the summed log decay
 template <typename T, bool STATS>
-__device__ __forceinline__ void ssm_local16(const T* tile, int C, int s, int jl, float A, float (&hs)[kSteps],
-                                            float (&Es)[kSteps], float& sl) {
-  const T* td = tile + s * kSteps * kCG + jl;  // dt, then x and b C rows further
+__device__ __forceinline__ void ssm_local16(const SsmParams& p, int b, int n, int g, int s, int jl, float A,
+                                            float (&hs)[kSteps], float (&Es)[kSteps], float& sl) {
+  const T* src = static_cast<const T*>(p.projs) + (size_t)b * p.psb + (size_t)(n * p.C + s * kSteps) * p.pst +
+                 g * kCD + jl;
+  T dt[kSteps], xv[kSteps], bv[kSteps];
+#pragma unroll
+  for (int t = 0; t < kSteps; ++t) {
+    const T* r = src + (size_t)t * p.pst;
+    dt[t] = r[0];
+    xv[t] = r[p.ds];
+    bv[t] = r[2 * p.ds];
+  }
   float h = 0.f, E = 1.f;
   sl = 0.f;
 #pragma unroll
   for (int t = 0; t < kSteps; ++t) {
-    const float dts = ssoftplus<T>(to_f(td[t * kCG]));
+    const float dts = ssoftplus<T>(to_f(dt[t]));
     const float ld = dts * A;
     const float a = sexp<T>(ld);
-    h = fmaf(h, a, dts * to_f(td[(2 * C + t) * kCG]) * to_f(td[(C + t) * kCG]));
+    h = fmaf(h, a, dts * to_f(bv[t]) * to_f(xv[t]));
     E *= a;
     if (STATS) sl += ld;
     hs[t] = h;
@@ -246,18 +260,15 @@ __device__ __forceinline__ void ssm_local16(const T* tile, int C, int s, int jl,
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) ssm_stats16_kernel(SsmParams p) {
-  extern __shared__ float sh[];  // [3][S][kPad] partials (h, E, summed log decay), then the tile
+__global__ void __launch_bounds__(128) ssm_stats16_kernel(SsmParams p) {
+  __shared__ float sh[3 * 16 * kPad];  // [3][S][kPad] partials (h, E, summed log decay)
   const int S = p.S;
-  T* tile = reinterpret_cast<T*>(sh + ((3 * S * kPad + 3) & ~3));  // 16-byte aligned
   const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
-  ssm_stage<T>(p, b, n, g, tile);
   {
-    const int jl = tid % kCG, s = tid / kCG;
-    const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCG + jl]));
-    __syncthreads();
+    const int jl = tid % kCD, s = tid / kCD;
+    const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCD + jl]));
     float hs[kSteps], Es[kSteps], sl;
-    ssm_local16<T, true>(tile, p.C, s, jl, A, hs, Es, sl);
+    ssm_local16<T, true>(p, b, n, g, s, jl, A, hs, Es, sl);
     sh[s * kPad + jl] = hs[kSteps - 1];
     sh[(S + s) * kPad + jl] = Es[kSteps - 1];
     sh[(2 * S + s) * kPad + jl] = sl;
@@ -276,24 +287,27 @@ __global__ void __launch_bounds__(256) ssm_stats16_kernel(SsmParams p) {
   }
   if (s == 0) {
     float* st = p.stats_w + ((size_t)b * (p.L / p.C) + n) * 2 * p.ds;
-    st[g * kCG + c] = bf16_round(h);
-    st[p.ds + g * kCG + c] = bf16_round(l);
+    st[g * kCD + c] = bf16_round(h);
+    st[p.ds + g * kCD + c] = bf16_round(l);
   }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) ssm_out16_kernel(SsmParams p) {
-  extern __shared__ float sh[];  // [2][S][kPad] partials, then the staged tile
+__global__ void __launch_bounds__(128) ssm_out16_kernel(SsmParams p) {
+  __shared__ float sh[2 * 16 * kPad];  // [2][S][kPad] partials
   const int S = p.S;
-  T* tile = reinterpret_cast<T*>(sh + ((2 * S * kPad + 3) & ~3));  // 16-byte aligned
   const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
-  ssm_stage<T>(p, b, n, g, tile);
+  // step map: this thread's 16 steps (their loads overlap the wait and the prefix below)
+  const int jl = tid % kCD, s = tid / kCD;
+  const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCD + jl]));
+  float hs[kSteps], Es[kSteps], sl;
+  ssm_local16<T, false>(p, b, n, g, s, jl, A, hs, Es, sl);
   if (p.wait_mask) cta_wait_flags(p.wait_flags, p.wait_mask, p.wait_gen, 45);
   // segment map: exclusive prefix over chunks [0, m_end) of channel c.  Lane s folds the
   // contiguous block [m_end s / S, m_end (s + 1) / S) in chunk order (fp32), then the blocks
   // fold by an ordered butterfly.  Both depend only on the absolute chunk index m_end, so a
   // sequence-parallel rank gets the same bits as one GPU over the whole sequence.
-  const int c = tid / S, sc = tid % S, jc = g * kCG + c;
+  const int c = tid / S, sc = tid % S, jc = g * kCD + c;
   float G = 0.f;
   {
     const int m_end = p.n_prev + n;
@@ -313,11 +327,6 @@ __global__ void __launch_bounds__(256) ssm_out16_kernel(SsmParams p) {
     }
     G = bf16_round(G);
   }
-  __syncthreads();  // tile staged
-  const int jl = tid % kCG, s = tid / kCG;
-  const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCG + jl]));
-  float hs[kSteps], Es[kSteps], sl;
-  ssm_local16<T, false>(tile, p.C, s, jl, A, hs, Es, sl);
   sh[s * kPad + jl] = hs[kSteps - 1];
   sh[(S + s) * kPad + jl] = Es[kSteps - 1];
   __syncthreads();
@@ -333,7 +342,7 @@ __global__ void __launch_bounds__(256) ssm_out16_kernel(SsmParams p) {
       }
     }
     float hin = 0.f, Ein = 1.f;
-    if (S > 1) {  // (S = 1: a 16-thread CTA, no shuffles)
+    if (S > 1) {
       hin = __shfl_up_sync(0xffffffffu, h, 1, S);
       Ein = __shfl_up_sync(0xffffffffu, E, 1, S);
     }
@@ -346,7 +355,7 @@ __global__ void __launch_bounds__(256) ssm_out16_kernel(SsmParams p) {
   }
   __syncthreads();
   const float hin = sh[s * kPad + jl], GE = sh[(S + s) * kPad + jl];
-  T* yb = static_cast<T*>(p.y) + (size_t)b * p.ysb + (size_t)(n * p.C + s * kSteps) * p.yst + g * kCG + jl;
+  T* yb = static_cast<T*>(p.y) + (size_t)b * p.ysb + (size_t)(n * p.C + s * kSteps) * p.yst + g * kCD + jl;
 #pragma unroll
   for (int t = 0; t < kSteps; ++t) {
     const float hh = fmaf(hin, Es[t], hs[t]);
@@ -368,26 +377,23 @@ static int ssm_segments(int ds, int C) {
   return S;
 }
 
-// floats of partials in front of the staged tile (a multiple of 4: the tile takes 16-byte stores)
-static int ssm_parts_floats(const SsmParams& p, bool out) {
-  const int f = ssm_fast(p.C) ? (out ? 2 : 3) * p.S * kPad : (out ? 4 : 2) * p.S * kCG;
-  return (f + 3) / 4 * 4;
-}
-
 // one launch of the statistics (out = false) or output kernel for the plan in p
 template <typename T>
 static void ssm_launch(bool out, const SsmParams& p, dim3 grid, cudaStream_t s) {
-  const size_t smem = (size_t)ssm_parts_floats(p, out) * sizeof(float) + (size_t)3 * p.C * kCG * sizeof(T);
-  void (*k)(SsmParams);
-  if (ssm_fast(p.C)) k = out ? ssm_out16_kernel<T> : ssm_stats16_kernel<T>;
-  else k = out ? ssm_scan_out_kernel<T> : ssm_chunk_stats_kernel<T>;
+  if (ssm_fast(p.C)) {  // static shared memory only
+    if (out) ssm_out16_kernel<T><<<grid, p.S * p.CG, 0, s>>>(p);
+    else ssm_stats16_kernel<T><<<grid, p.S * p.CG, 0, s>>>(p);
+    return;
+  }
+  const size_t smem = (size_t)(out ? 4 : 2) * p.S * kCG * sizeof(float) + (size_t)3 * p.C * kCG * sizeof(T);
+  void (*k)(SsmParams) = out ? ssm_scan_out_kernel<T> : ssm_chunk_stats_kernel<T>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k<<<grid, p.S * p.CG, smem, s>>>(p);
 }
 
 static void ssm_setup(SsmParams& p, int dtype) {
   p.S = ssm_fast(p.C) ? (int)(p.C / kSteps) : ssm_segments(p.ds, p.C);
-  p.CG = kCG;
+  p.CG = ssm_fast(p.C) ? kCD : kCG;
   const size_t es = dtype == HDC_F32 ? 4 : 2;
   p.vec = ((reinterpret_cast<uintptr_t>(p.projs) & 15u) == 0 && (p.pst * es) % 16 == 0 && (p.psb * es) % 16 == 0)
               ? 1 : 0;
