@@ -114,3 +114,18 @@ def test_library_rejects_bad_arguments_without_a_gpu():
                                  None)
     assert rc == -2
     assert lib.hdc_slot_workspace_bytes(1, 256, 2, 64, 64) > 0
+
+
+@pytest.mark.parametrize("D", [768, 2048])
+def test_lnconv_bwd_plan_stays_within_one_wave(D):
+    """The backward's segment plan (visible through its workspace size: one fp32 [7, D]
+    partial per CTA) never launches more CTAs than one wave holds on the 148-SM part the
+    library assumes without a GPU; rounding the segments per batch row up had given B = 8,
+    D = 2048 152 CTAs, whose last 4 ran as a second wave."""
+    lib = _lib.load()
+    per_sm = max(1, min(4, 512 // ((D // 4 + 31) // 32 * 32)))
+    for B in (1, 3, 8, 16, 37, 148, 200):
+        for L in (64, 1000, 8192):
+            ctas = lib.hdc_ln_conv_bwd_workspace_bytes(B, L, D) // (7 * D * 4)
+            assert ctas >= B
+            assert ctas <= max(B, 148 * per_sm), (B, L, ctas)
