@@ -61,6 +61,9 @@ __global__ void __launch_bounds__(mc::NT, 1)
     slot_mc_state_kernel(const __grid_constant__ CUtensorMap mapK, const __grid_constant__ CUtensorMap mapV,
                          SlotTcParams p) {
   using namespace mc;
+  // the output kernel (launched as this grid's programmatic dependent) may start its CTAs as
+  // this grid's CTAs exit; it waits for this grid before it reads the states
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = align1024(smem_raw);
   // stage st: K at base + 2 st TILE, V right after it
@@ -278,6 +281,10 @@ __global__ void __launch_bounds__(mc::NT, 1)
     if (ngroups > 1) issue_kq(1, 1);
   }
 
+  // pass A's states: when this kernel was launched as its programmatic dependent, the setup and
+  // the first loads above ran while it was finishing; wait for it here (returns at once
+  // otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // entering state: state_in, then the local states of pass A's pieces before this segment
   // (fp32; lanes < 16 hold row f_row, columns [e0, e0 + 16))
   float Rr[16];
@@ -600,14 +607,24 @@ int slot_mc_fwd(const SlotParams& sp, int64_t B, int64_t in_sb, int64_t in_st, v
     }
     if (int e = launch_status("slot_mc_state_kernel")) return e;
   }
-  const unsigned grid = (unsigned)(BH * p.nseg);
-  if (ps) {
-    cudaFuncSetAttribute(slot_mc_out_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mc::SMEM_B);
-    slot_mc_out_kernel<true><<<grid, mc::NT, mc::SMEM_B, s>>>(mq, mk, mv, p);
-  } else {
-    cudaFuncSetAttribute(slot_mc_out_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mc::SMEM_B);
-    slot_mc_out_kernel<false><<<grid, mc::NT, mc::SMEM_B, s>>>(mq, mk, mv, p);
-  }
+  // after the state pass: a programmatic dependent launch (output CTAs take the SMs as state
+  // CTAs leave them; the kernel waits before it reads the states)
+  auto go = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mc::SMEM_B);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(BH * p.nseg));
+    cfg.blockDim = dim3(mc::NT);
+    cfg.dynamicSmemBytes = mc::SMEM_B;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.nseg > 1 ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, p);
+  };
+  const cudaError_t le = ps ? go(slot_mc_out_kernel<true>) : go(slot_mc_out_kernel<false>);
+  if (le != cudaSuccess) return fail((int)le, "slot_mc_out_kernel launch: %s", cudaGetErrorString(le));
   return launch_status("slot_mc_out_kernel");
 }
 
