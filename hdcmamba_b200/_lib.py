@@ -34,6 +34,8 @@ SIGNATURES = {
     "hdc_ln_conv_bwd": (c_int, [c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_size,
                                 c_i64, c_i64, c_i64, c_vp]),
     "hdc_ssm_chunk_stats": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
+    "hdc_ssm_scan_fwd": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_i64,
+                                 c_i64, c_vp]),
     "hdc_ssm_scan_out": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i64, c_i64,
                                  c_i64, c_i64, c_i64, c_i64, c_vp]),
     "hdc_ssm_scan_out_blocked": (c_int, [c_int, c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp,

@@ -261,6 +261,8 @@ __device__ __forceinline__ void ssm_local16(const SsmParams& p, int b, int n, in
 
 template <typename T>
 __global__ void __launch_bounds__(128) ssm_stats16_kernel(SsmParams p) {
+  // hdc_ssm_scan_fwd launches the output kernel as this grid's programmatic dependent
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ float sh[3 * 16 * kPad];  // [3][S][kPad] partials (h, E, summed log decay)
   const int S = p.S;
   const int n = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
@@ -302,6 +304,10 @@ __global__ void __launch_bounds__(128) ssm_out16_kernel(SsmParams p) {
   const float A = -sexp<T>(to_f(static_cast<const T*>(p.A_log)[g * kCD + jl]));
   float hs[kSteps], Es[kSteps], sl;
   ssm_local16<T, false>(p, b, n, g, s, jl, A, hs, Es, sl);
+  // launched as the statistics kernel's programmatic dependent (hdc_ssm_scan_fwd), the loads
+  // and the local scan above overlapped its end: wait for it before reading the statistics
+  // (returns at once otherwise)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (p.wait_mask) cta_wait_flags(p.wait_flags, p.wait_mask, p.wait_gen, 45);
   // segment map: exclusive prefix over chunks [0, m_end) of channel c.  Lane s folds the
   // contiguous block [m_end s / S, m_end (s + 1) / S) in chunk order (fp32), then the blocks
@@ -378,11 +384,29 @@ static int ssm_segments(int ds, int C) {
 }
 
 // one launch of the statistics (out = false) or output kernel for the plan in p
+// dependent: the output kernel directly follows this library's statistics kernel on the
+// stream, so it may be a programmatic dependent launch (16-step kernels only: they wait for
+// the statistics kernel before reading its results, and read nothing else it writes)
 template <typename T>
-static void ssm_launch(bool out, const SsmParams& p, dim3 grid, cudaStream_t s) {
+static void ssm_launch(bool out, const SsmParams& p, dim3 grid, cudaStream_t s, bool dependent = false) {
   if (ssm_fast(p.C)) {  // static shared memory only
-    if (out) ssm_out16_kernel<T><<<grid, p.S * p.CG, 0, s>>>(p);
-    else ssm_stats16_kernel<T><<<grid, p.S * p.CG, 0, s>>>(p);
+    if (out && dependent) {
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(p.S * p.CG);
+      cfg.dynamicSmemBytes = 0;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaLaunchKernelEx(&cfg, ssm_out16_kernel<T>, p);
+    } else if (out) {
+      ssm_out16_kernel<T><<<grid, p.S * p.CG, 0, s>>>(p);
+    } else {
+      ssm_stats16_kernel<T><<<grid, p.S * p.CG, 0, s>>>(p);
+    }
     return;
   }
   const size_t smem = (size_t)(out ? 4 : 2) * p.S * kCG * sizeof(float) + (size_t)3 * p.C * kCG * sizeof(T);
@@ -432,7 +456,8 @@ static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, in
                                const float* stats, int64_t stats_sb, int64_t blk, int64_t blk_stride,
                                int64_t n_prev, void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L,
                                int64_t ds, int64_t C, hdc_stream_t stream, const uint32_t* wait_flags = nullptr,
-                               uint32_t wait_mask = 0, const uint32_t* wait_gen = nullptr) {
+                               uint32_t wait_mask = 0, const uint32_t* wait_gen = nullptr,
+                               bool dependent = false) {
   if (int e = ssm_check(dtype, projs, A_log, B, L, ds, C)) return e;
   if (!stats || !y) return fail(HDC_E_NULL, "ssm: null stats / y");
   SsmParams p{};
@@ -444,8 +469,8 @@ static int ssm_scan_out_launch(int dtype, const void* projs, int64_t proj_sb, in
   ssm_setup(p, dtype);
   dim3 grid((unsigned)(L / C), (unsigned)(ds / p.CG), (unsigned)B);
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == HDC_F32) ssm_launch<float>(true, p, grid, s);
-  else ssm_launch<__nv_bfloat16>(true, p, grid, s);
+  if (dtype == HDC_F32) ssm_launch<float>(true, p, grid, s, dependent);
+  else ssm_launch<__nv_bfloat16>(true, p, grid, s, dependent);
   return launch_status("ssm_scan_out_kernel");
 }
 
@@ -457,6 +482,15 @@ extern "C" int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, i
     return fail(HDC_E_SHAPE, "ssm: stats batch stride too small");
   return ssm_scan_out_launch(dtype, projs, proj_sb, proj_st, A_log, stats, stats_sb, INT_MAX, 0, n_prev, y, y_sb,
                              y_st, B, L, ds, C, stream);
+}
+
+extern "C" int hdc_ssm_scan_fwd(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st, const void* A_log,
+                                float* stats, void* y, int64_t y_sb, int64_t y_st, int64_t B, int64_t L, int64_t ds,
+                                int64_t C, hdc_stream_t stream) {
+  if (int e = hdc_ssm_chunk_stats(dtype, projs, proj_sb, proj_st, A_log, stats, B, L, ds, C, stream)) return e;
+  if (!y) return fail(HDC_E_NULL, "ssm: null y");
+  return ssm_scan_out_launch(dtype, projs, proj_sb, proj_st, A_log, stats, (L / C) * 2 * ds, INT_MAX, 0, 0, y, y_sb,
+                             y_st, B, L, ds, C, stream, nullptr, 0, nullptr, /*dependent=*/true);
 }
 
 extern "C" int hdc_ssm_scan_out_blocked(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,

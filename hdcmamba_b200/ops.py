@@ -188,9 +188,23 @@ def ssm_scan_out_blocked(projs, A_log, stats, stats_sb, block_chunks, block_stri
 
 
 def ssm_scan(projs, A_log, d_state, chunk, out=None):
-    """The whole diagonal-SSM chunked scan (hdcmamba/model.py:175-233, launched 345-363)."""
-    stats = ssm_chunk_stats(projs, A_log, d_state, chunk)
-    return ssm_scan_out(projs, A_log, stats, 0, d_state, chunk, out=out)
+    """The whole diagonal-SSM chunked scan (hdcmamba/model.py:175-233, launched 345-363):
+    ``hdc_ssm_scan_fwd``, statistics then outputs, enqueued back to back.
+    ``out``: optional [B, L, >=ds] view (unit column stride) to write into."""
+    _cuda(projs, A_log, out)
+    B, L, P = projs.shape
+    if P < 3 * d_state or L % chunk != 0:
+        raise ValueError(f"projs [B, L, {P}] needs >= 3*d_state columns and L % chunk == 0")
+    sb, st = _row_view(projs, "projs")
+    a = A_log.to(projs.dtype).contiguous()
+    if out is None:
+        out = torch.empty(B, L, d_state, device=projs.device, dtype=projs.dtype)
+    _same_dtype(projs, out)
+    osb, ost = _row_view(out, "out")
+    stats = torch.empty(B, L // chunk, 2 * d_state, device=projs.device, dtype=torch.float32)
+    _lib.call("hdc_ssm_scan_fwd", _code(projs), _p(projs), sb, st, _p(a), _p(stats), _p(out), osb, ost, B, L,
+              d_state, chunk, _stream(projs))
+    return out
 
 
 # ------------------------------------------------------------------ slot scan

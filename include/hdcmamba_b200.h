@@ -127,6 +127,17 @@ int hdc_ssm_scan_out(int dtype, const void* projs, int64_t proj_sb, int64_t proj
                      int64_t C, hdc_stream_t stream);
 
 /*
+ * The whole diagonal-SSM chunked scan in one call: hdc_ssm_chunk_stats into the caller's
+ * stats ([B, L/C, 2*ds] fp32 scratch), then hdc_ssm_scan_out with n_prev = 0.
+ * Replaces the three SSM kernels of hdcmamba/model.py:175-233 (launched 345-363).  The two
+ * passes are enqueued back to back, so the output pass may start its loads and local scans
+ * while the statistics pass finishes (it waits for that pass before reading stats).
+ */
+int hdc_ssm_scan_fwd(int dtype, const void* projs, int64_t proj_sb, int64_t proj_st,
+                     const void* A_log, float* stats, void* y, int64_t y_sb, int64_t y_st,
+                     int64_t B, int64_t L, int64_t ds, int64_t C, hdc_stream_t stream);
+
+/*
  * hdc_ssm_scan_out with the statistics stored in blocks of block_chunks chunks, block i
  * at stats + i*block_stride (batch b of a block at + b*stats_sb): the rank-major layout of
  * per-rank statistics gathered under sequence parallelism, read in place.  Chunk m of
