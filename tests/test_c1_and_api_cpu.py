@@ -114,6 +114,13 @@ def test_library_rejects_bad_arguments_without_a_gpu():
                                  None)
     assert rc == -2
     assert lib.hdc_slot_workspace_bytes(1, 256, 2, 64, 64) > 0
+    # the one-call SSM scan checks its arguments the same way
+    rc = lib.hdc_ssm_scan_fwd(7, ctypes.c_void_p(16), 1, 1, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                              ctypes.c_void_p(32), 1, 1, 1, 256, 64, 64, None)
+    assert rc == -1
+    rc = lib.hdc_ssm_scan_fwd(1, ctypes.c_void_p(16), 1, 1, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                              ctypes.c_void_p(32), 1, 1, 1, 100, 48, 64, None)
+    assert rc == -2
 
 
 @pytest.mark.parametrize("D", [768, 2048])
